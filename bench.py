@@ -1,0 +1,344 @@
+"""bench.py -- W8A8 ConvRot linear throughput on B200, one JSON line on rank 0.
+
+A step is one pass of the DiT block's four int8 ConvRot linears over one 32760-token batch (BASELINE.json
+configs[1]): qkv 5120->15360, fc1 5120->13824, out-proj 5120->5120, fc2 13824->5120.  Each linear is the
+reference's fused path (attn8::gemm_s8 with rotate): the fused Hadamard-256 rotation + per-token int8
+quantization kernel, then the tcgen05 int8 GEMM with its fused scale/bias epilogue, bf16 out.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+--impl reference times the reference's CPU path for the same linears (rotate -> dequantise -> float matmul,
+portable/kernels.rs:220-242) on the host cores, on a bounded row sample.  Under torchrun every rank runs its own
+32760-token shard (weak scaling, no collective on the data path); times are CUDA events, max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "h3-rs_b200"))
+
+METRIC = "W8A8 ConvRot linear TOPS (% of int8 peak) at DiT shapes, 1/2/4/8 B200"
+M_TOKENS = 32760
+LINEARS = [("qkv", 5120, 15360), ("fc1", 5120, 13824), ("out", 5120, 5120), ("fc2", 13824, 5120)]
+WORKLOAD = ("BASELINE c1: DiT-scale int8 ConvRot linears, M=32760 tokens; qkv 5120->15360, fc1 5120->13824, "
+            "out 5120->5120, fc2 13824->5120; bf16 in/out, per-token int8 activations, int8 weights")
+NOMINAL_INT8_TOPS = 4500.0
+
+
+def ops_per_step(m: int) -> float:
+    return float(sum(2.0 * m * k * n for _, k, n in LINEARS))
+
+
+def load_peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        if self.path and os.path.exists(self.path):
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+            os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        loaded = [s for s in sm if mx and s > 0.5 * max(mx)] or sm
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+# --------------------------------------------------------------------------------------------- CPU baseline
+
+def cpu_baseline(budget_s: float = 12.0) -> dict:
+    """The reference's CPU path (oracle port of portable/kernels.rs:220-242) on a bounded row sample of every
+    linear of the workload: TOPS = algorithmic ops of the sample / wall time, numpy BLAS on all host cores."""
+    import numpy as np
+    from oracle import oracle as O
+    rng = np.random.default_rng(0)
+    cores = os.cpu_count() or 1
+
+    def run(rows: int) -> tuple[float, float]:
+        ops, t = 0.0, 0.0
+        for _, k, n in LINEARS:
+            x = O.f32_to_bf16_bits(rng.standard_normal((rows, k)).astype(np.float32))
+            w = rng.integers(-127, 128, size=(n, k), dtype=np.int8)
+            ws = (rng.random(n, dtype=np.float32) * 9e-3 + 1e-3).astype(np.float32)
+            b = O.bf16_round((rng.standard_normal(n) * 0.02).astype(np.float32))
+            t0 = time.perf_counter()
+            O.cpu_int8_linear(x, w, ws, b, rotate=True)
+            t += time.perf_counter() - t0
+            ops += 2.0 * rows * k * n
+        return ops, t
+
+    ops, t = run(32)
+    rows = 32
+    if t < budget_s / 4:
+        rows = int(min(M_TOKENS, max(32, 32 * (budget_s / 2) / max(t, 1e-3))))
+        rows = max(32, rows // 32 * 32)
+        ops, t = run(rows)
+    return {"value": ops / t / 1e12, "unit": "TOPS", "cores": cores, "kind": "port",
+            "sample": f"{rows} of {M_TOKENS} tokens through each of the 4 linears (weights dequantised per call, "
+                      f"as portable/kernels.rs:220-242 does); {t:.1f} s of CPU work",
+            "seconds": t}
+
+
+def run_reference(args) -> None:
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return
+    samples = [cpu_baseline(budget_s=8.0) for _ in range(max(1, min(args.steps, 3)))]
+    value = statistics.median(s["value"] for s in samples)
+    cb = dict(samples[0])
+    cb["value"] = value
+    cb.pop("seconds", None)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": ws, "steps": len(samples),
+        "warmup": 0, "ms_per_step": 2e3 * ops_per_step(M_TOKENS) / 2 / (value * 1e12) * 1e0,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": config_block(ws),
+        "cpu_baseline": cb,
+        "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    line["ms_per_step"] = 1e3 * ops_per_step(M_TOKENS) / (value * 1e12)
+    print(json.dumps(line), flush=True)
+
+
+def config_block(n_gpus: int) -> dict:
+    return {"workload": WORKLOAD, "M_per_gpu": M_TOKENS, "linears": [f"{nm}:{k}x{n}" for nm, k, n in LINEARS],
+            "rotate": "ConvRot Hadamard-256, fused into the quantizer", "epilogue": "xs*ws*acc + bias -> bf16",
+            "l2": "no flush: every activation (335-905 MB) and output is larger than the 126 MB L2",
+            "parallelism": f"token-sharded x{n_gpus} (weak: 32760 tokens per GPU, weights replicated, no collective)"}
+
+
+# --------------------------------------------------------------------------------------------- our arm
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    import torch
+    import h3q
+
+    ws_n, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if ws_n > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    if not h3q.available_arch(local):
+        raise SystemExit("bench.py: this library needs an sm_100 (B200) GPU")
+
+    M = M_TOKENS
+    g = torch.Generator(device=dev).manual_seed(1234 + rank)
+    layers = []
+    for name, k, n in LINEARS:
+        x = torch.randn((M, k), generator=g, device=dev)
+        oc = torch.randperm(k, generator=g, device=dev)[:8]
+        x[:, oc] *= 20.0
+        x = x.to(torch.bfloat16)
+        w = torch.randint(-127, 128, (n, k), generator=g, device=dev, dtype=torch.int8)
+        wsc = torch.rand(n, generator=g, device=dev) * 9e-3 + 1e-3
+        b = (torch.randn(n, generator=g, device=dev) * 0.02).to(torch.bfloat16).float()
+        layers.append(dict(name=name, k=k, n=n, x=x, w=w, ws=wsc, b=b,
+                           q=torch.empty((M, k), dtype=torch.int8, device=dev),
+                           xs=torch.empty(M, dtype=torch.float32, device=dev),
+                           out=torch.empty((M, n), dtype=torch.bfloat16, device=dev)))
+    L = h3q.lib()
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+
+    def one_step(events=None):
+        for i, ly in enumerate(layers):
+            if events is not None:
+                events[i][0].record(stream)
+            h3q.check(L.h3q_quant_rows_i8(ly["x"].data_ptr(), 2, ly["q"].data_ptr(), ly["xs"].data_ptr(), M, ly["k"],
+                                          1, sp))
+            if events is not None:
+                events[i][1].record(stream)
+            h3q.check(L.h3q_gemm_s8_quantized(ly["q"].data_ptr(), ly["xs"].data_ptr(), ly["w"].data_ptr(),
+                                              ly["ws"].data_ptr(), ly["n"], ly["b"].data_ptr(), ly["out"].data_ptr(),
+                                              2, M, ly["n"], ly["k"], h3q.EPI_LINEAR, None, None, None, sp))
+            if events is not None:
+                events[i][2].record(stream)
+
+    for _ in range(args.warmup):
+        one_step()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in LINEARS] for _ in range(args.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        start.record(stream)
+        for s in range(args.steps):
+            one_step(ev[s])
+        stop.record(stream)
+        torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    elapsed_ms = start.elapsed_time(stop)
+    if dist is not None:
+        t = torch.tensor([elapsed_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+    ms_step = elapsed_ms / args.steps
+    value = ws_n * ops_per_step(M) / (ms_step * 1e-3) / 1e12
+    status = h3q.device_status(local)
+    if status:
+        raise SystemExit(f"bench.py: a kernel reported device error {status}")
+
+    # per-kernel averages inside the timed region
+    gemm_ms = sum(ev[s][i][1].elapsed_time(ev[s][i][2]) for s in range(args.steps) for i in range(len(LINEARS)))
+    quant_ms = sum(ev[s][i][0].elapsed_time(ev[s][i][1]) for s in range(args.steps) for i in range(len(LINEARS)))
+    launches = args.steps * len(LINEARS)
+    gemm_ops_launch = ops_per_step(M) / len(LINEARS)
+    gemm_avg_ms = gemm_ms / launches
+    quant_bytes_launch = sum(3.0 * M * k + 4.0 * M for _, k, _ in LINEARS) / len(LINEARS)
+    quant_avg_ms = quant_ms / launches
+    peaks = load_peaks()
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+    achieved = gemm_ops_launch / (gemm_avg_ms * 1e-3) / 1e12
+    q_achieved = quant_bytes_launch / (quant_avg_ms * 1e-3) / 1e9
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "gemm_i8_traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            traffic = json.load(f).get("dram_bytes_per_launch")
+
+    # end to end through the C ABI with host buffers: H2D of each linear's input, gemm_s8, D2H of its output
+    e2e = None
+    if rank == 0 or True:
+        host_x = [ly["x"].cpu().pin_memory() for ly in layers]
+        host_o = [torch.empty((M, ly["n"]), dtype=torch.bfloat16).pin_memory() for ly in layers]
+        wsp = torch.empty(max(L.h3q_gemm_s8_workspace_size(M, ly["k"]) for ly in layers), dtype=torch.uint8, device=dev)
+        xdev = [torch.empty_like(ly["x"]) for ly in layers]
+
+        def e2e_step():
+            for i, ly in enumerate(layers):
+                xdev[i].copy_(host_x[i], non_blocking=True)
+                h3q.check(L.h3q_gemm_s8(xdev[i].data_ptr(), ly["w"].data_ptr(), ly["ws"].data_ptr(), ly["n"],
+                                        ly["b"].data_ptr(), ly["out"].data_ptr(), M, ly["n"], ly["k"], 0, 1,
+                                        wsp.data_ptr(), wsp.numel(), sp))
+                host_o[i].copy_(ly["out"], non_blocking=True)
+
+        e2e_step()
+        torch.cuda.synchronize()
+        e_steps = max(2, min(args.steps, 5))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        e_ms = e0.elapsed_time(e1) / e_steps
+        if dist is not None:
+            t = torch.tensor([e_ms], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            e_ms = float(t.item())
+        e2e = {"value": ws_n * ops_per_step(M) / (e_ms * 1e-3) / 1e12, "unit": "TOPS",
+               "h2d_bytes_per_step": int(sum(h.numel() * 2 for h in host_x)),
+               "d2h_bytes_per_step": int(sum(h.numel() * 2 for h in host_o)), "ms_per_step": e_ms,
+               "path": "h3q_gemm_s8 (C ABI) with pinned host input/output, copies inside the timed region"}
+
+    cb = None
+    if rank == 0 and ws_n == 1 and not args.no_cpu_baseline:
+        cb = cpu_baseline()
+        cb.pop("seconds", None)
+
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": ws_n, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": config_block(ws_n),
+        "frac_of_int8_peak": value / ws_n / int8_peak,
+        "roofline": {"kernel": "gemm_i8_kernel (tcgen05 kind::i8, fused epilogue)", "bound": "tensor",
+                     "achieved": achieved, "peak": int8_peak, "unit": "TOPS", "frac": achieved / int8_peak,
+                     "peak_note": f"2 x {peaks['source']} bf16 burst {peaks['bf16_tflops']:.0f} TF/s (dense int8 "
+                                  f"issues at twice the bf16 rate); frac of nominal 4500: "
+                                  f"{achieved / NOMINAL_INT8_TOPS:.3f}",
+                     "traffic": traffic, "avg_launch_ms": gemm_avg_ms, "ops_per_launch": gemm_ops_launch},
+        "roofline_quant": {"kernel": "quant_rows_kernel<2> (rotate + per-token int8)", "bound": "hbm",
+                           "achieved": q_achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                           "frac": q_achieved / peaks["hbm_gbs"], "avg_launch_ms": quant_avg_ms,
+                           "bytes_per_launch": quant_bytes_launch},
+        "cpu_baseline": cb, "e2e": e2e, "clocks": clk.summary(),
+        "gpu_launches": 2 * launches,
+    }
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,232 @@
+"""h3q -- Python binding of the B200 quantized-linear library (lib/libh3q.so, C ABI in include/h3q.h).
+
+The functions mirror h3-rs's op API (attn8::gemm_s8, kernels::int8_linear_ex, kernels::dequant_i8, ...): they
+take torch CUDA tensors, allocate outputs and workspaces with torch's allocator, and call the C ABI on the
+current stream.  There is no fallback: if libh3q.so is missing or the device is not sm_100, calls raise.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(os.path.dirname(_HERE), "lib", "libh3q.so")
+_LIB = None
+
+OK, ERR_ARG, ERR_UNSUPPORTED, ERR_CUDA, ERR_TIMEOUT, ERR_NCCL, ERR_WORKSPACE = range(7)
+EPI_LINEAR, EPI_SWIGLU_PAIRS, EPI_SWIGLU_HALVES, EPI_GELU_TANH, EPI_GATE_RESID, EPI_ACC_I32 = range(6)
+
+_vp, _i64, _int, _sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_size_t
+
+# name -> (restype, argtypes) of every symbol include/h3q.h declares
+SIGNATURES = {
+    "h3q_last_error": (ctypes.c_char_p, []),
+    "h3q_version": (ctypes.c_char_p, []),
+    "h3q_available_arch": (_int, [_int]),
+    "h3q_can_fuse_rotation": (_int, [_sz, _sz]),
+    "h3q_device_status": (_int, [_int, ctypes.POINTER(_int)]),
+    "h3q_quant_rows_i8": (_int, [_vp, _int, _vp, _vp, _i64, _i64, _int, _vp]),
+    "h3q_gemm_s8_workspace_size": (_sz, [_i64, _i64]),
+    "h3q_gemm_s8": (_int, [_vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _int, _int, _vp, _sz, _vp]),
+    "h3q_int8_linear_workspace_size": (_sz, [_i64, _i64]),
+    "h3q_int8_linear_ex": (_int, [_vp, _int, _vp, _vp, _i64, _vp, _vp, _int, _i64, _i64, _i64, _int, _int, _vp, _sz,
+                                  _vp]),
+    "h3q_gemm_s8_quantized": (_int, [_vp, _vp, _vp, _vp, _i64, _vp, _vp, _int, _i64, _i64, _i64, _int, _vp, _vp, _vp,
+                                     _vp]),
+    "h3q_gemm_s8_acc": (_int, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "h3q_dequant_i8": (_int, [_vp, _vp, _i64, _vp, _int, _i64, _i64, _vp]),
+    "h3q_dequant_nvfp4": (_int, [_vp, _vp, _vp, _vp, _int, _i64, _i64, _vp]),
+    "h3q_gate_add": (_int, [_vp, _vp, _int, _vp, _vp, _vp, _i64, _i64, _vp]),
+}
+
+
+class H3QError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"[h3q status {status}] {msg}")
+        self.status = status
+
+
+def lib() -> ctypes.CDLL:
+    """The loaded libh3q.so (raises if it was not built)."""
+    global _LIB
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"h3q native library not built: {LIB_PATH} (run `make -C h3-rs_b200`)")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _LIB = L
+    return _LIB
+
+
+def last_error() -> str:
+    return lib().h3q_last_error().decode()
+
+
+def check(status: int) -> None:
+    if status != OK:
+        raise H3QError(status, last_error())
+
+
+def _kind(dtype) -> int:
+    import torch
+    return {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}[dtype]
+
+
+def _p(t) -> int:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(dev=None) -> int:
+    import torch
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _cuda(*ts) -> None:
+    for t in ts:
+        if t is not None and (not t.is_cuda or not t.is_contiguous()):
+            raise ValueError("h3q: expected contiguous CUDA tensors")
+
+
+def available_arch(device: int = 0) -> bool:
+    """attn8::available_arch (attn8.rs:584-589) for this build: an sm_100 device."""
+    return bool(lib().h3q_available_arch(device))
+
+
+def can_fuse_rotation(k: int, group: int) -> bool:
+    """kernels::can_fuse_rotation (kernels.rs:1081-1085)."""
+    return bool(lib().h3q_can_fuse_rotation(k, group))
+
+
+def device_status(device: int = 0) -> int:
+    code = _int(0)
+    lib().h3q_device_status(device, ctypes.byref(code))
+    return code.value
+
+
+def quant_rows(x, rotate: bool):
+    """kernels::quant_rows_raw (kernels.rs:1133-1161): (int8 codes [M,K], f32 scales [M])."""
+    import torch
+    _cuda(x)
+    M, K = x.shape
+    q = torch.empty((M, K), dtype=torch.int8, device=x.device)
+    s = torch.empty(M, dtype=torch.float32, device=x.device)
+    check(lib().h3q_quant_rows_i8(_p(x), _kind(x.dtype), _p(q), _p(s), M, K, int(rotate), _stream(x.device)))
+    return q, s
+
+
+def gemm_s8(x, w, ws, bias=None, swiglu: bool = False, rotate: bool = False, workspace=None):
+    """attn8::gemm_s8 (attn8.rs:570-581): bf16 x [M,K] (quantized per row on the fly), int8 w [N,K] (int8 or
+    uint8 bytes), f32 ws ([N] or scalar), f32 bias [N] or None -> bf16 [M,N] (or [M,N/2] with swiglu)."""
+    import torch
+    if x.dtype != torch.bfloat16:
+        raise H3QError(ERR_ARG, "gemm_s8: bf16 input with K % 64 == 0 required")
+    ws = ws.to(torch.float32).reshape(-1).contiguous()
+    bias = None if bias is None else bias.to(torch.float32).contiguous()
+    _cuda(x, w, ws, bias)
+    M, K = x.shape
+    N = w.shape[0]
+    out = torch.empty((M, N // 2 if swiglu else N), dtype=torch.bfloat16, device=x.device)
+    need = lib().h3q_gemm_s8_workspace_size(M, K)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=x.device)
+    check(lib().h3q_gemm_s8(_p(x), _p(w), _p(ws), ws.numel(), _p(bias), _p(out), M, N, K, int(swiglu), int(rotate),
+                            _p(workspace), workspace.numel(), _stream(x.device)))
+    return out
+
+
+def int8_linear_ex(x, w, scale, bias=None, out_dtype=None, swiglu: bool = False, rotate: bool = False,
+                   workspace=None):
+    """kernels::int8_linear_ex (kernels.rs:1088-1097)."""
+    import torch
+    out_dtype = out_dtype or x.dtype
+    scale = scale.to(torch.float32).reshape(-1).contiguous()
+    bias = None if bias is None else bias.to(torch.float32).contiguous()
+    _cuda(x, w, scale, bias)
+    M, K = x.shape
+    N = w.shape[0]
+    out = torch.empty((M, N // 2 if swiglu else N), dtype=out_dtype, device=x.device)
+    need = lib().h3q_int8_linear_workspace_size(M, K)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=x.device)
+    check(lib().h3q_int8_linear_ex(_p(x), _kind(x.dtype), _p(w), _p(scale), scale.numel(), _p(bias), _p(out),
+                                   _kind(out_dtype), M, N, K, int(swiglu), int(rotate), _p(workspace),
+                                   workspace.numel(), _stream(x.device)))
+    return out
+
+
+def int8_linear(x, w, scale, bias=None, out_dtype=None):
+    """kernels::int8_linear (kernels.rs:1074-1076)."""
+    return int8_linear_ex(x, w, scale, bias, out_dtype, False, False)
+
+
+def gemm_s8_quantized(a, xs, w, ws, bias=None, epilogue: int = EPI_LINEAR, out_dtype=None, gate=None,
+                      gate_idx=None, resid=None, out=None):
+    """The tcgen05 GEMM on pre-quantized rows with a chosen epilogue (include/h3q.h)."""
+    import torch
+    ws = ws.to(torch.float32).reshape(-1).contiguous()
+    _cuda(a, xs, w, ws, bias, gate, gate_idx, resid)
+    M, K = a.shape
+    N = w.shape[0]
+    if epilogue == EPI_ACC_I32:
+        dt, n_out = torch.int32, N
+    elif epilogue in (EPI_SWIGLU_PAIRS, EPI_SWIGLU_HALVES):
+        dt, n_out = (torch.bfloat16 if epilogue == EPI_SWIGLU_PAIRS else (out_dtype or torch.bfloat16)), N // 2
+    elif epilogue == EPI_LINEAR:
+        dt, n_out = out_dtype or torch.bfloat16, N
+    else:
+        dt, n_out = torch.bfloat16, N
+    if out is None:
+        out = torch.empty((M, n_out), dtype=dt, device=a.device)
+    okind = _kind(dt) if dt != torch.int32 else 0
+    check(lib().h3q_gemm_s8_quantized(_p(a), _p(xs), _p(w), _p(ws), ws.numel(), _p(bias), _p(out), okind, M, N, K,
+                                      epilogue, _p(gate), _p(gate_idx), _p(resid), _stream(a.device)))
+    return out
+
+
+def gemm_s8_acc(a, w):
+    """Raw int32 accumulators of a [M,K] x w [N,K]^T."""
+    import torch
+    _cuda(a, w)
+    M, K = a.shape
+    N = w.shape[0]
+    acc = torch.empty((M, N), dtype=torch.int32, device=a.device)
+    check(lib().h3q_gemm_s8_acc(_p(a), _p(w), _p(acc), M, N, K, _stream(a.device)))
+    return acc
+
+
+def dequant_i8(q, scale, out_dtype):
+    """kernels::dequant_i8 (kernels.rs:636-638)."""
+    import torch
+    scale = scale.to(torch.float32).reshape(-1).contiguous()
+    _cuda(q, scale)
+    rows, cols = q.shape
+    out = torch.empty((rows, cols), dtype=out_dtype, device=q.device)
+    check(lib().h3q_dequant_i8(_p(q), _p(scale), scale.numel(), _p(out), _kind(out_dtype), rows, cols,
+                               _stream(q.device)))
+    return out
+
+
+def dequant_nvfp4(q, block_scale, global_scale, out_dtype):
+    """kernels::dequant_nvfp4 (kernels.rs:677-680)."""
+    import torch
+    g = global_scale.to(torch.float32).reshape(1).contiguous()
+    _cuda(q, block_scale, g)
+    rows, kp = q.shape
+    out = torch.empty((rows, 2 * kp), dtype=out_dtype, device=q.device)
+    check(lib().h3q_dequant_nvfp4(_p(q), _p(block_scale), _p(g), _p(out), _kind(out_dtype), rows, 2 * kp,
+                                  _stream(q.device)))
+    return out
+
+
+def gate_add(x, y, gate, idx):
+    """kernels::gate_add (kernels.rs:879-883)."""
+    import torch
+    y = y.to(x.dtype).contiguous()
+    _cuda(x, y, gate, idx)
+    S, C = x.shape
+    out = torch.empty_like(x)
+    check(lib().h3q_gate_add(_p(x), _p(y), _kind(x.dtype), _p(gate), _p(idx), _p(out), S, C, _stream(x.device)))
+    return out

@@ -1,0 +1,130 @@
+/*
+ * h3q.h -- C ABI of the B200 (sm_100a) quantized-linear library that stands in for h3-rs's CUDA hot path.
+ *
+ * Every entry point takes raw device pointers, explicit sizes and a cudaStream_t (passed as void*), launches
+ * asynchronously on that stream, allocates no device memory on the hot path (callers pass outputs and, where
+ * needed, a workspace sized by the matching *_workspace_size function) and reports failures through a status
+ * code plus h3q_last_error() text.  Nothing aborts the process.  A kernel that gives up waiting inside the
+ * GPU latches a code into a per-device error word, read by h3q_device_status().
+ *
+ * Each declaration names the h3-rs function it replaces (paths inside the h3-rs source tree).  Tensors are
+ * row-major and contiguous; "kind" codes follow kernels.rs's kind_of (kernels.rs:547-554): 0 = f32,
+ * 1 = f16, 2 = bf16.
+ */
+#ifndef H3Q_H_
+#define H3Q_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  H3Q_OK = 0,
+  H3Q_ERR_ARG = 1,         /* invalid arguments: the reference's `bail!` checks, plus null/alignment checks */
+  H3Q_ERR_UNSUPPORTED = 2, /* valid for the reference but outside what this build implements */
+  H3Q_ERR_CUDA = 3,        /* a CUDA runtime / driver call failed */
+  H3Q_ERR_TIMEOUT = 4,     /* a kernel gave up waiting on one of its own barriers (h3q_device_status) */
+  H3Q_ERR_NCCL = 5,        /* reserved for multi-GPU entry points */
+  H3Q_ERR_WORKSPACE = 6    /* the caller's workspace is smaller than *_workspace_size */
+} h3q_status;
+
+enum { H3Q_KIND_F32 = 0, H3Q_KIND_F16 = 1, H3Q_KIND_BF16 = 2 };
+
+/* Epilogues of h3q_gemm_s8_quantized. */
+enum {
+  H3Q_EPI_LINEAR = 0,        /* out[m,n] = acc*xs[m]*ws[n] + bias[n]   (gemm_s8 / int8_epilogue)            */
+  H3Q_EPI_SWIGLU_PAIRS = 1,  /* interleaved (gate, up) columns -> out[m, n/2], bf16 (attn8.rs:334-337)       */
+  H3Q_EPI_SWIGLU_HALVES = 2, /* gate = column j, up = column N/2 + j -> out[m, j] (kernels.rs:353-373)      */
+  H3Q_EPI_GELU_TANH = 3,     /* out = gelu_tanh(bf16 y), bf16 (ops.rs:46-48 applied to the linear output)  */
+  H3Q_EPI_GATE_RESID = 4,    /* out = resid + bf16(y) * bf16(gate[idx[m], n]), bf16 (kernels.rs:418-428)   */
+  H3Q_EPI_ACC_I32 = 5        /* raw int32 accumulators [M, N] (the cuBLASLt path's int32 result)          */
+};
+
+/* Text of the last error raised on the calling thread ("" if none). */
+const char* h3q_last_error(void);
+
+/* Library version string. */
+const char* h3q_version(void);
+
+/* attn8::available_arch (attn8.rs:584-589): 1 when `device` can run these kernels (sm_100), else 0. */
+int h3q_available_arch(int device);
+
+/* kernels::can_fuse_rotation (kernels.rs:1081-1085): whether the rotation fuses into the quantizer for an
+ * input width k and ConvRot group size.  Always on here (group 256, k % 256 == 0, k / 256 <= 64); the
+ * reference gates it behind H3_FUSED_ROT=1 because its butterfly was slow on RTX 4090. */
+int h3q_can_fuse_rotation(size_t k, size_t group);
+
+/* Reads and clears the error word that kernels on `device` latch when a bounded wait runs out.  Synchronizes
+ * the device.  *code receives 0 when no kernel reported a failure.  Returns H3Q_ERR_TIMEOUT if one did. */
+h3q_status h3q_device_status(int device, int* code);
+
+/* kernels::quant_rows_raw (kernels.rs:1133-1161): x [m,k] of kind x_kind -> int8 codes q [m,k] and f32
+ * scales [m].  rotate selects the fused ConvRot-256 rotation; like the reference, bf16 input with
+ * k / 256 <= 56 uses the quant_rows_i8_rot2 summation order (kernels.rs:220-293), any other rotated call the
+ * quant_rows_i8_rot order (kernels.rs:166-213).  Rotation needs k % 256 == 0 and k / 256 <= 64. */
+h3q_status h3q_quant_rows_i8(const void* x, int x_kind, int8_t* q, float* scale, int64_t m, int64_t k, int rotate,
+                             void* stream);
+
+/* Workspace bytes h3q_gemm_s8 needs for an [m,k] activation (int8 codes + f32 row scales). */
+size_t h3q_gemm_s8_workspace_size(int64_t m, int64_t k);
+
+/* attn8::gemm_s8 (attn8.rs:570-581, kernel attn8.rs:258-344): bf16 x [m,k] is quantized per row (optionally
+ * ConvRot-rotated) and multiplied by the int8 weight w [n,k]:
+ *   out[m,n] = bf16(sum_k q[m,k] w[n,k] * xs[m] * ws[n] + bias[n])
+ * ws has ws_numel entries: per output row when ws_numel == n && n > 1, else ws[0] for all (attn8.rs:553).
+ * bias is f32 [n] or NULL.  swiglu: rows of w interleave (gate, up) pairs and out is [m, n/2] =
+ * silu(gate) * up.  Requires k % 64 == 0 (the reference's check, attn8.rs:571-573). */
+h3q_status h3q_gemm_s8(const uint16_t* x, const int8_t* w, const float* ws, int64_t ws_numel, const float* bias,
+                       uint16_t* out, int64_t m, int64_t n, int64_t k, int swiglu, int rotate, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
+/* Workspace bytes h3q_int8_linear_ex needs. */
+size_t h3q_int8_linear_workspace_size(int64_t m, int64_t k);
+
+/* kernels::int8_linear_ex (kernels.rs:1088-1097, op kernels.rs:955-1070): x [m,k] (kind x_kind) quantized per
+ * row (rotated with the quant_rows_i8_rot order when rotate && k % 256 == 0 && k / 256 <= 64, otherwise
+ * unrotated, exactly as the reference), times w [n,k], epilogue int8_epilogue or, with swiglu, the split-half
+ * int8_epilogue_swiglu (gate = column j, up = column n/2 + j), written in out_kind.  The reference's int32
+ * accumulator round trip through HBM is fused away.  Requires k % 4 == 0 and an output width % 4 == 0
+ * (kernels.rs:977, :1062); this build also needs k % 16 == 0. */
+h3q_status h3q_int8_linear_ex(const void* x, int x_kind, const int8_t* w, const float* scale, int64_t scale_numel,
+                              const float* bias, void* out, int out_kind, int64_t m, int64_t n, int64_t k, int swiglu,
+                              int rotate, void* workspace, size_t workspace_bytes, void* stream);
+
+/* The tensor-core GEMM on already-quantized activations a [m,k] (scales xs [m]) and weight w [n,k], with any
+ * epilogue above.  The building block of h3q_gemm_s8 / h3q_int8_linear_ex, exported so callers can reuse one
+ * quantization across several weights (the DiT's fused qkv and gate/up share their input).
+ *   H3Q_EPI_GATE_RESID: gate is an f32 table [R, n], gate_idx u32 [m] selects its row (NULL: row 0), resid is
+ *   bf16 [m, n]; out = bf16(resid + bf16(y) * bf16(gate)).  out_kind is ignored for bf16-only epilogues. */
+h3q_status h3q_gemm_s8_quantized(const int8_t* a, const float* xs, const int8_t* w, const float* ws,
+                                 int64_t ws_numel, const float* bias, void* out, int out_kind, int64_t m, int64_t n,
+                                 int64_t k, int epilogue, const float* gate, const uint32_t* gate_idx,
+                                 const uint16_t* resid, void* stream);
+
+/* Raw int32 accumulators acc[m,n] = sum_k a[m,k] w[n,k] (the cuBLASLt IMMA result of kernels.rs:1026-1044). */
+h3q_status h3q_gemm_s8_acc(const int8_t* a, const int8_t* w, int32_t* acc, int64_t m, int64_t n, int64_t k,
+                           void* stream);
+
+/* kernels::dequant_i8 (kernels.rs:607-638, kernel :40-49): out[r,c] = q[r,c] * scale[r or 0] in out_kind;
+ * per row when scale_numel == rows && rows > 1 (kernels.rs:616). */
+h3q_status h3q_dequant_i8(const int8_t* q, const float* scale, int64_t scale_numel, void* out, int out_kind,
+                          int64_t rows, int64_t cols, void* stream);
+
+/* kernels::dequant_nvfp4 (kernels.rs:640-680, kernel :65-81): q [rows, k/2] (even column in the high nibble),
+ * block scales e4m3 in the 128x4 swizzled layout, f32 global scale (device pointer) -> out [rows, k]. */
+h3q_status h3q_dequant_nvfp4(const uint8_t* q, const uint8_t* block_scale, const float* global_scale, void* out,
+                             int out_kind, int64_t rows, int64_t k, void* stream);
+
+/* kernels::gate_add (kernels.rs:849-883, kernel :418-428): out = x + y * gate[idx[s], c] (gate rounded to
+ * the kind of x), x/y/out [s, c] of kind `kind` (f16 or bf16), gate f32 [R, c], idx u32 [s]. */
+h3q_status h3q_gate_add(const void* x, const void* y, int kind, const float* gate, const uint32_t* idx, void* out,
+                        int64_t s, int64_t c, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* H3Q_H_ */

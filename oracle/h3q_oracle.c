@@ -1,0 +1,522 @@
+/*
+ * h3q_oracle.c -- TEST INFRASTRUCTURE ONLY.
+ *
+ * A plain-C restatement, on the CPU, of the arithmetic that apiplant/h3-rs performs on its quantized-linear
+ * and int8-attention hot path.  It is the checker for the CUDA library: tests/, __graft_entry__.smoke() and
+ * bench.py's cpu_baseline / --impl reference legs are the only callers.  Nothing in the product library links
+ * it, and the product path never falls back to it.
+ *
+ * Every function names the reference file:line it restates (paths inside the h3-rs source tree).  Operation
+ * order is kept exactly where the reference's result depends on it (the Hadamard butterflies, the scale
+ * computation, the epilogue's multiply-add), so integer codes, scales and int32 accumulators match
+ * bit for bit.
+ *
+ * Build with -ffp-contract=off: the explicit fmaf() calls below are the only fused multiply-adds, placed where
+ * the reference's NVRTC build (fmad on by default) contracts `a * b + c`.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define H3O_API __attribute__((visibility("default")))
+
+/* ---------------------------------------------------------------- number formats (kernels.rs:17-25) */
+
+static inline float bf2f(uint16_t v) {
+    uint32_t u = (uint32_t)v << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+
+/* round-to-nearest-even f32 -> bf16, NaN -> 0x7fc0 (kernels.rs:18-23, attn8.rs:27-32) */
+static inline uint16_t f2bf(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return 0x7fc0;
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+static inline float bf16r(float f) { return bf2f(f2bf(f)); }
+
+static inline float h2f(uint16_t v) {
+    _Float16 h;
+    memcpy(&h, &v, 2);
+    return (float)h;
+}
+
+static inline uint16_t f2h(float f) {
+    _Float16 h = (_Float16)f; /* IEEE round-to-nearest-even, as cvt.rn.f16.f32 */
+    uint16_t v;
+    memcpy(&v, &h, 2);
+    return v;
+}
+
+/* kind: 0 = f32, 1 = f16, 2 = bf16 (kernels.rs:27-38) */
+static inline float ldf(const void* p, int kind, size_t i) {
+    if (kind == 0) return ((const float*)p)[i];
+    if (kind == 1) return h2f(((const uint16_t*)p)[i]);
+    return bf2f(((const uint16_t*)p)[i]);
+}
+
+static inline void stf(void* p, int kind, size_t i, float v) {
+    if (kind == 0) ((float*)p)[i] = v;
+    else if (kind == 1) ((uint16_t*)p)[i] = f2h(v);
+    else ((uint16_t*)p)[i] = f2bf(v);
+}
+
+H3O_API uint16_t h3o_f2bf(float f) { return f2bf(f); }
+H3O_API float h3o_bf2f(uint16_t v) { return bf2f(v); }
+
+/* cvt.rni.s32.f32 / __float2int_rn: round half to even, NaN -> 0, saturating */
+static inline int f2i_rn(float v) {
+    if (isnan(v)) return 0;
+    float r = rintf(v);
+    if (r >= 2147483648.0f) return 2147483647;
+    if (r < -2147483648.0f) return (-2147483647 - 1);
+    return (int)r;
+}
+
+/* ---------------------------------------------------------------- seeded generator (rng.rs:8-116) */
+
+typedef struct {
+    uint32_t state[624];
+    int idx;
+    int has_cached;
+    double cached;
+} h3o_gen;
+
+/* TorchGen::new (rng.rs:15-22): torch.manual_seed(seed) */
+H3O_API void h3o_gen_init(h3o_gen* g, uint64_t seed) {
+    g->state[0] = (uint32_t)(seed & 0xffffffffu);
+    for (int i = 1; i < 624; ++i)
+        g->state[i] = 1812433253u * (g->state[i - 1] ^ (g->state[i - 1] >> 30)) + (uint32_t)i;
+    g->idx = 624;
+    g->has_cached = 0;
+    g->cached = 0.0;
+}
+
+H3O_API size_t h3o_gen_size(void) { return sizeof(h3o_gen); }
+
+/* TorchGen::twist (rng.rs:24-35) */
+static void gen_twist(h3o_gen* g) {
+    for (int i = 0; i < 624; ++i) {
+        uint32_t y = (g->state[i] & 0x80000000u) | (g->state[(i + 1) % 624] & 0x7fffffffu);
+        uint32_t v = g->state[(i + 397) % 624] ^ (y >> 1);
+        if (y & 1u) v ^= 0x9908b0dfu;
+        g->state[i] = v;
+    }
+    g->idx = 0;
+}
+
+/* TorchGen::next_u32 (rng.rs:37-47) */
+H3O_API uint32_t h3o_gen_u32(h3o_gen* g) {
+    if (g->idx >= 624) gen_twist(g);
+    uint32_t y = g->state[g->idx++];
+    y ^= y >> 11;
+    y ^= (y << 7) & 0x9d2c5680u;
+    y ^= (y << 15) & 0xefc60000u;
+    return y ^ (y >> 18);
+}
+
+static uint64_t gen_u64(h3o_gen* g) {
+    uint64_t hi = h3o_gen_u32(g), lo = h3o_gen_u32(g);
+    return (hi << 32) | lo;
+}
+
+/* TorchGen::uniform (rng.rs:55-57): 24-bit uniform in [0, 1) */
+H3O_API float h3o_gen_uniform(h3o_gen* g) {
+    return (float)(h3o_gen_u32(g) & ((1u << 24) - 1)) * (1.0f / (float)(1u << 24));
+}
+
+/* TorchGen::normal_scalar (rng.rs:60-77) */
+static float gen_normal_scalar(h3o_gen* g) {
+    if (g->has_cached) {
+        g->has_cached = 0;
+        return (float)g->cached;
+    }
+    double u1 = (double)(gen_u64(g) & ((1ull << 53) - 1)) * (1.0 / (double)(1ull << 53));
+    double u2 = (double)(gen_u64(g) & ((1ull << 53) - 1)) * (1.0 / (double)(1ull << 53));
+    double r = sqrt(-2.0 * log1p(-u2));
+    double th = 2.0 * 3.14159265358979323846 * u1;
+    g->cached = r * sin(th);
+    g->has_cached = 1;
+    return (float)(r * cos(th));
+}
+
+/* fill16 (rng.rs:101-110) */
+static void fill16(float* d) {
+    const float two_pi = 2.0f * 3.14159265358979323846f;
+    for (int j = 0; j < 8; ++j) {
+        float u1 = 1.0f - d[j];
+        float u2 = d[j + 8];
+        float r = sqrtf(-2.0f * logf(u1));
+        float th = two_pi * u2;
+        d[j] = r * cosf(th);
+        d[j + 8] = r * sinf(th);
+    }
+}
+
+/* TorchGen::randn (rng.rs:80-96): torch.randn(n) for float32 */
+H3O_API void h3o_gen_randn(h3o_gen* g, float* d, size_t n) {
+    if (n < 16) {
+        for (size_t i = 0; i < n; ++i) d[i] = gen_normal_scalar(g);
+        return;
+    }
+    for (size_t i = 0; i < n; ++i) d[i] = h3o_gen_uniform(g);
+    size_t i = 0;
+    for (; i + 16 <= n; i += 16) fill16(d + i);
+    if (n % 16 != 0) {
+        size_t s = n - 16;
+        for (size_t j = s; j < n; ++j) d[j] = h3o_gen_uniform(g);
+        fill16(d + s);
+    }
+}
+
+/*
+ * Synthetic W8A8 linear inputs, drawn from one TorchGen stream in this order:
+ *   x [M,K] ~ N(0,1); `n_outliers` distinct channels (next_u32 % K, repeats skipped) scaled x20; x -> bf16
+ *   w [N,K] int8 uniform over [-127, 127] (next_u32 % 255 - 127)
+ *   ws [N] ~ U(1e-3, 1e-2)
+ *   bias [N] ~ N(0, 0.02) rounded to bf16, kept as f32 (the reference loads bias as f32, weights.rs:498)
+ */
+H3O_API void h3o_make_linear_inputs(uint64_t seed, int64_t M, int64_t K, int64_t N, int n_outliers,
+                                    uint16_t* x, int8_t* w, float* ws, float* bias) {
+    h3o_gen g;
+    h3o_gen_init(&g, seed);
+    size_t mk = (size_t)M * (size_t)K;
+    float* tmp = (float*)malloc(sizeof(float) * (mk > (size_t)N ? mk : (size_t)N) + 64);
+    h3o_gen_randn(&g, tmp, mk);
+    int64_t outl[64];
+    int no = n_outliers < K ? n_outliers : (int)K;
+    if (no > 64) no = 64;
+    for (int i = 0; i < no;) {
+        int64_t c = (int64_t)(h3o_gen_u32(&g) % (uint32_t)K);
+        int dup = 0;
+        for (int j = 0; j < i; ++j) dup |= (outl[j] == c);
+        if (!dup) outl[i++] = c;
+    }
+    for (int i = 0; i < no; ++i)
+        for (int64_t r = 0; r < M; ++r) tmp[(size_t)r * K + outl[i]] *= 20.0f;
+    for (size_t i = 0; i < mk; ++i) x[i] = f2bf(tmp[i]);
+    size_t nk = (size_t)N * (size_t)K;
+    for (size_t i = 0; i < nk; ++i) w[i] = (int8_t)((int)(h3o_gen_u32(&g) % 255u) - 127);
+    for (int64_t i = 0; i < N; ++i) ws[i] = 1e-3f + 9e-3f * h3o_gen_uniform(&g);
+    h3o_gen_randn(&g, tmp, (size_t)N);
+    for (int64_t i = 0; i < N; ++i) bias[i] = bf16r(0.02f * tmp[i]);
+    free(tmp);
+}
+
+/* ---------------------------------------------------------------- ConvRot Hadamard (weights.rs:441-489) */
+
+/* hadamard(size) (weights.rs:441-465): Kronecker powers of the regular H4, divided by sqrt(size). */
+H3O_API int h3o_hadamard(int size, float* h_out) {
+    static const float h4[16] = {1, 1, 1, -1, 1, 1, -1, 1, 1, -1, 1, 1, -1, 1, 1, 1};
+    int p4 = 4;
+    while (p4 < size) p4 *= 4;
+    if (size < 4 || p4 != size) return -1; /* "ConvRot group size is not a power of 4" (weights.rs:460-462) */
+    int n = 4;
+    float* h = (float*)malloc(sizeof(float) * (size_t)size * size);
+    float* t = (float*)malloc(sizeof(float) * (size_t)size * size);
+    memcpy(h, h4, sizeof(h4));
+    while (n < size) {
+        for (int i = 0; i < n; ++i)
+            for (int j = 0; j < n; ++j)
+                for (int a = 0; a < 4; ++a)
+                    for (int b = 0; b < 4; ++b)
+                        t[(size_t)(i * 4 + a) * (n * 4) + j * 4 + b] = h[(size_t)i * n + j] * h4[a * 4 + b];
+        n *= 4;
+        float* s = h;
+        h = t;
+        t = s;
+    }
+    int ok = (n == size);
+    if (ok) {
+        float norm = sqrtf((float)size);
+        for (size_t i = 0; i < (size_t)size * size; ++i) h_out[i] = h[i] / norm;
+    }
+    free(h);
+    free(t);
+    return ok ? 0 : -1;
+}
+
+/* rotate_activation(x, 256) in f64 (weights.rs:482-489): exact-arithmetic reference for property tests */
+H3O_API void h3o_rotate_f64(const float* x, double* out, int64_t rows, int64_t K) {
+    float H[256 * 256];
+    h3o_hadamard(256, H);
+    for (int64_t r = 0; r < rows; ++r)
+        for (int64_t g = 0; g < K / 256; ++g) {
+            const float* xr = x + r * K + g * 256;
+            for (int j = 0; j < 256; ++j) {
+                double s = 0.0;
+                for (int i = 0; i < 256; ++i) s += (double)xr[i] * (double)H[i * 256 + j];
+                out[r * K + g * 256 + j] = s;
+            }
+        }
+}
+
+/* ---------------------------------------------------------------- per-row int8 quantizers */
+
+/*
+ * One 256-group through quant_rows_i8_rot2's warp butterfly (kernels.rs:220-270).  Element i of the group
+ * is held by lane i/8 as a[i%8].  Digits of i in base 4 are transformed in the order 0, 1, 2, 3 with the
+ * regular H4 (out_p = sum - 2*a_{3-p}, kernels.rs:218).  Digit 0 sums in-thread as ((a0+a1)+a2)+a3
+ * (kernels.rs:237-241); digits 1..3 sum pairwise as (a_p + a_{p^1}) + (a_{p^2} + a_{p^3}) through shuffles
+ * (kernels.rs:244-265).  The output is multiplied by 1/16 (kernels.rs:268).
+ */
+static void rot2_group(float v[256]) {
+    float a[32][8], b[32][8];
+    for (int l = 0; l < 32; ++l)
+        for (int e = 0; e < 8; ++e) a[l][e] = v[l * 8 + e];
+    /* digit 0 (e & 3): in-thread */
+    for (int l = 0; l < 32; ++l)
+        for (int hb = 0; hb < 8; hb += 4) {
+            float s = ((a[l][hb] + a[l][hb + 1]) + a[l][hb + 2]) + a[l][hb + 3];
+            float b0 = s - 2.f * a[l][hb + 3], b1 = s - 2.f * a[l][hb + 2];
+            float b2 = s - 2.f * a[l][hb + 1], b3 = s - 2.f * a[l][hb];
+            a[l][hb] = b0; a[l][hb + 1] = b1; a[l][hb + 2] = b2; a[l][hb + 3] = b3;
+        }
+    /* digit 1 = (e >> 2) + 2 * (lane & 1) */
+    for (int l = 0; l < 32; ++l)
+        for (int e = 0; e < 4; ++e) {
+            int p = l ^ 1;
+            float s = (a[l][e] + a[l][e + 4]) + (a[p][e] + a[p][e + 4]);
+            b[l][e] = s - 2.f * a[p][e + 4];
+            b[l][e + 4] = s - 2.f * a[p][e];
+        }
+    memcpy(a, b, sizeof(a));
+    /* digits 2 and 3 = (lane >> 1) & 3, (lane >> 3) & 3 */
+    for (int d = 0; d < 2; ++d) {
+        int sh = d == 0 ? 1 : 3;
+        for (int l = 0; l < 32; ++l)
+            for (int e = 0; e < 8; ++e) {
+                int l1 = l ^ (1 << sh), l2 = l ^ (2 << sh), l3 = l ^ (3 << sh);
+                float s1 = a[l][e] + a[l1][e];
+                float s2 = a[l2][e] + a[l2 ^ (1 << sh)][e];
+                b[l][e] = (s1 + s2) - 2.f * a[l3][e];
+            }
+        memcpy(a, b, sizeof(a));
+    }
+    for (int l = 0; l < 32; ++l)
+        for (int e = 0; e < 8; ++e) v[l * 8 + e] = a[l][e] * (1.f / 16.f);
+}
+
+/*
+ * One 256-group through quant_rows_i8_rot's shared-memory butterfly (kernels.rs:166-197): strides 1, 4, 16,
+ * 64, each output from the four inputs a0..a3 of its digit with left-to-right sums
+ * p=0: a0+a1+a2-a3, p=1: a0+a1-a2+a3, p=2: a0-a1+a2+a3, p=3: -a0+a1+a2+a3 (kernels.rs:183-187), then * 1/16.
+ */
+static void rot1_group(float v[256]) {
+    float sm[256], o[256];
+    memcpy(sm, v, sizeof(sm));
+    for (int st = 0, stride = 1; st < 4; ++st, stride *= 4) {
+        for (int i = 0; i < 256; ++i) {
+            int p = (i / stride) & 3, i0 = i - p * stride;
+            float a0 = sm[i0], a1 = sm[i0 + stride], a2 = sm[i0 + 2 * stride], a3 = sm[i0 + 3 * stride];
+            float r;
+            if (p == 0) r = ((a0 + a1) + a2) - a3;
+            else if (p == 1) r = ((a0 + a1) - a2) + a3;
+            else if (p == 2) r = ((a0 - a1) + a2) + a3;
+            else r = ((-a0 + a1) + a2) + a3;
+            o[i] = r;
+        }
+        memcpy(sm, o, sizeof(sm));
+    }
+    for (int i = 0; i < 256; ++i) v[i] = sm[i] * (1.f / 16.f);
+}
+
+/*
+ * Per-row int8 quantization of x [M,K] (kind 0/1/2), optionally ConvRot-rotated.
+ *   mode 0: quant_rows_i8 (kernels.rs:296-318): no rotation; q = (s8)min(max(rintf(v*inv), -128), 127)
+ *   mode 1: quant_rows_i8_rot (kernels.rs:166-213): smem butterfly; same clamp form as mode 0
+ *   mode 2: quant_rows_i8_rot2 (kernels.rs:220-293): warp butterfly, bf16 only; q = clamp(__float2int_rn)
+ * Scale s = fmaxf(max|v| / 127, 1e-30), inv = 1/s (IEEE divisions; kernels.rs:206, :278, :313).
+ */
+H3O_API int h3o_quant_rows(const void* x, int kind, int8_t* q, float* scale, int64_t M, int64_t K, int mode) {
+    if (mode != 0 && K % 256 != 0) return -1;
+    if (mode == 2 && kind != 2) return -1;
+    float* v = (float*)malloc(sizeof(float) * (size_t)K);
+    for (int64_t r = 0; r < M; ++r) {
+        size_t base = (size_t)r * K;
+        for (int64_t i = 0; i < K; ++i) v[i] = ldf(x, kind, base + i);
+        if (mode == 1)
+            for (int64_t g = 0; g < K / 256; ++g) rot1_group(v + g * 256);
+        if (mode == 2)
+            for (int64_t g = 0; g < K / 256; ++g) rot2_group(v + g * 256);
+        float m = 0.f;
+        for (int64_t i = 0; i < K; ++i) m = fmaxf(m, fabsf(v[i]));
+        float s = fmaxf(m / 127.f, 1e-30f), inv = 1.f / s;
+        scale[r] = s;
+        for (int64_t i = 0; i < K; ++i) {
+            float t = v[i] * inv;
+            int qi;
+            if (mode == 2) {
+                qi = f2i_rn(t);
+                qi = qi < -128 ? -128 : (qi > 127 ? 127 : qi);
+            } else {
+                float rr = fminf(fmaxf(rintf(t), -128.f), 127.f); /* NaN -> -128 through fmaxf */
+                qi = (int)rr;
+            }
+            q[base + i] = (int8_t)qi;
+        }
+    }
+    free(v);
+    return 0;
+}
+
+/* ---------------------------------------------------------------- int8 GEMM core and epilogues */
+
+/* acc[m,n] = sum_k A[m,k] * B[n,k] (int32; attn8.rs:258-318 main loop, kernels.rs:1026-1044 cuBLASLt IMMA) */
+H3O_API void h3o_gemm_s8_acc(const int8_t* A, const int8_t* B, int32_t* acc, int64_t M, int64_t N, int64_t K) {
+    for (int64_t m = 0; m < M; ++m) {
+        const int8_t* a = A + m * K;
+        for (int64_t n = 0; n < N; ++n) {
+            const int8_t* b = B + n * K;
+            int32_t s = 0;
+            for (int64_t k = 0; k < K; ++k) s += (int32_t)a[k] * (int32_t)b[k];
+            acc[m * N + n] = s;
+        }
+    }
+}
+
+/* bf16(gelu_tanh(bf16 y)), candle's `gelu` (ops.rs:46-48): 0.5 y (1 + tanh(sqrt(2/pi) (y + 0.044715 y^3))) */
+static float gelu_tanh_f(float y) {
+    const float c = 0.7978845608028654f;
+    return 0.5f * y * (1.f + tanhf(c * (y + 0.044715f * y * y * y)));
+}
+
+/*
+ * Fused-epilogue GEMM output from int32 accumulators, as gemm_s8 computes it (attn8.rs:320-343):
+ *   v = fmaf((float)acc * xs[m], ws[n], bias[n])        (NVRTC contracts `acc * x * w + b`)
+ * epi 0: out[m,n] = bf16(v)
+ * epi 1: SwiGLU over interleaved (gate, up) column pairs (attn8.rs:334-337):
+ *        gt = bf16r(v0), up = bf16r(v1), sg = bf16r(gt / (1 + exp(-gt))), out[m,n/2] = bf16(sg * up)
+ * epi 2: out = bf16(gelu_tanh(bf16r(v)))  (candle gelu applied to the bf16 linear output, ops.rs:46-48)
+ * epi 3: out = bf16(fmaf(bf16r(v), bf16r(gate[idx[m], n]), resid[m,n]))  (gate_add on the bf16 output,
+ *        kernels.rs:418-428; `x + y * g` contracted)
+ * ws_per_row: ws has N entries, else ws[0] for every column (attn8.rs:553).  bias may be NULL.
+ */
+H3O_API void h3o_gemm_s8_epilogue(const int32_t* acc, const float* xs, const float* ws, int ws_per_row,
+                                  const float* bias, uint16_t* out, int64_t M, int64_t N, int epi,
+                                  const float* gate, const uint32_t* gate_idx, const uint16_t* resid) {
+    for (int64_t m = 0; m < M; ++m) {
+        float x = xs[m];
+        if (epi == 1) {
+            for (int64_t n = 0; n + 1 < N; n += 2) {
+                float w0 = ws_per_row ? ws[n] : ws[0], w1 = ws_per_row ? ws[n + 1] : ws[0];
+                float v0 = fmaf((float)acc[m * N + n] * x, w0, bias ? bias[n] : 0.f);
+                float v1 = fmaf((float)acc[m * N + n + 1] * x, w1, bias ? bias[n + 1] : 0.f);
+                float gt = bf16r(v0), up = bf16r(v1);
+                float sg = bf16r(gt / (1.f + expf(-gt)));
+                out[m * (N / 2) + n / 2] = f2bf(sg * up);
+            }
+            continue;
+        }
+        for (int64_t n = 0; n < N; ++n) {
+            float w = ws_per_row ? ws[n] : ws[0];
+            float v = fmaf((float)acc[m * N + n] * x, w, bias ? bias[n] : 0.f);
+            float o;
+            if (epi == 2) {
+                o = gelu_tanh_f(bf16r(v));
+            } else if (epi == 3) {
+                uint32_t gi = gate_idx ? gate_idx[m] : 0u;
+                float g = bf16r(gate[(size_t)gi * N + n]);
+                o = fmaf(bf16r(v), g, bf2f(resid[m * N + n]));
+            } else {
+                o = v;
+            }
+            out[m * N + n] = f2bf(o);
+        }
+    }
+}
+
+/*
+ * cuBLASLt-path epilogues (kernels.rs:333-373): out dtype okind (0 f32, 1 f16, 2 bf16).
+ *   swiglu = 0: out[m,n] = fmaf(acc * xs[m], ws[n], bias[n])                       (int8_epilogue)
+ *   swiglu = 1: split halves, gate = col j, up = col F+j of acc [M, 2F] (int8_epilogue_swiglu):
+ *               out[m,j] = silu_r(gate) * up_r(up), bf16 re-rounding of the operands when okind is bf16
+ * N is the output width (F when swiglu).
+ */
+H3O_API void h3o_int8_epilogue(const int32_t* acc, const float* xs, const float* ws, int ws_per_row,
+                               const float* bias, void* out, int okind, int64_t M, int64_t N, int swiglu) {
+    for (int64_t m = 0; m < M; ++m) {
+        float x = xs[m];
+        if (!swiglu) {
+            for (int64_t n = 0; n < N; ++n) {
+                float w = ws_per_row ? ws[n] : ws[0];
+                stf(out, okind, (size_t)(m * N + n), fmaf((float)acc[m * N + n] * x, w, bias ? bias[n] : 0.f));
+            }
+            continue;
+        }
+        const int32_t* row = acc + m * 2 * N;
+        for (int64_t j = 0; j < N; ++j) {
+            float wg = ws_per_row ? ws[j] : ws[0];
+            float wu = ws_per_row ? ws[N + j] : wg;
+            float g = fmaf((float)row[j] * x, wg, bias ? bias[j] : 0.f);
+            float u = fmaf((float)row[N + j] * x, wu, bias ? bias[N + j] : 0.f);
+            if (okind == 2) g = bf16r(g);
+            float s = g / (1.f + expf(-g));
+            if (okind == 2) { s = bf16r(s); u = bf16r(u); }
+            stf(out, okind, (size_t)(m * N + j), s * u);
+        }
+    }
+}
+
+/* gate_add (kernels.rs:418-428): out = x + y * round_to_kind(gate[idx[s], c]), contracted to one fma */
+H3O_API void h3o_gate_add(const void* x, const void* y, int kind, const float* gate, const uint32_t* idx,
+                          void* out, int64_t S, int64_t C) {
+    for (int64_t s = 0; s < S; ++s)
+        for (int64_t c = 0; c < C; ++c) {
+            size_t i = (size_t)(s * C + c);
+            float g = gate[(size_t)idx[s] * C + c];
+            g = (kind == 1) ? h2f(f2h(g)) : bf16r(g);
+            stf(out, kind, i, fmaf(ldf(y, kind, i), g, ldf(x, kind, i)));
+        }
+}
+
+/* ---------------------------------------------------------------- weight decode */
+
+/* dequant_i8 (kernels.rs:40-49, portable/kernels.rs:14-27): out = (float)q * scale[row or 0] */
+H3O_API void h3o_dequant_i8(const int8_t* q, const float* scale, int per_row, void* out, int okind,
+                            int64_t rows, int64_t cols) {
+    for (int64_t r = 0; r < rows; ++r)
+        for (int64_t c = 0; c < cols; ++c)
+            stf(out, okind, (size_t)(r * cols + c), (float)q[r * cols + c] * (per_row ? scale[r] : scale[0]));
+}
+
+/* fp8 e4m3 decode (kernels.rs:51-58, portable/kernels.rs:29-44) */
+H3O_API float h3o_fp8e4m3(uint8_t v) {
+    int sgn = v >> 7, e = (v >> 3) & 15, m = v & 7;
+    float r;
+    if (e == 0) r = ldexpf((float)m / 8.0f, -6);
+    else if (e == 15 && m == 7) r = NAN;
+    else r = ldexpf(1.0f + (float)m / 8.0f, e - 7);
+    return sgn ? -r : r;
+}
+
+static const float E2M1[16] = {0.0f, 0.5f, 1.0f, 1.5f, 2.0f, 3.0f, 4.0f, 6.0f,
+                               -0.0f, -0.5f, -1.0f, -1.5f, -2.0f, -3.0f, -4.0f, -6.0f};
+
+/* byte offset of block scale (row r, 16-wide block b) in the 128x4 swizzled table (kernels.rs:76-78) */
+H3O_API int64_t h3o_nvfp4_scale_offset(int64_t r, int64_t b, int64_t k) {
+    int64_t nb = k / 16, ncb = (nb + 3) / 4;
+    int64_t rb = r / 128, rin = r % 128, cb = b / 4, cin = b % 4;
+    return (rb * ncb + cb) * 512 + (rin % 32) * 16 + (rin / 32) * 4 + cin;
+}
+
+/*
+ * dequant_nvfp4 (kernels.rs:65-81, portable/kernels.rs:46-70): q [N, K/2] two e2m1 codes per byte, even
+ * column in the HIGH nibble; W[r,c] = E2M1[nib] * e4m3(bs[swz(r, c/16)]) * g.
+ */
+H3O_API void h3o_dequant_nvfp4(const uint8_t* q, const uint8_t* bs, float g, void* out, int okind,
+                               int64_t nrows, int64_t k) {
+    for (int64_t r = 0; r < nrows; ++r)
+        for (int64_t c = 0; c < k; ++c) {
+            uint8_t byte = q[r * (k / 2) + c / 2];
+            int nib = (c & 1) ? (byte & 15) : (byte >> 4);
+            float s = h3o_fp8e4m3(bs[h3o_nvfp4_scale_offset(r, c / 16, k)]);
+            stf(out, okind, (size_t)(r * k + c), E2M1[nib] * s * g);
+        }
+}

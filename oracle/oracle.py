@@ -1,0 +1,261 @@
+"""TEST INFRASTRUCTURE ONLY -- Python face of the CPU oracle (liboracle.so, h3q_oracle.c) and of the
+reference's dequantise-then-matmul CPU path.
+
+Callers: tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / --impl reference legs, as the
+checker or the timed CPU baseline.  The product library never imports this module.
+
+Every function names the h3-rs file:line it restates (paths inside the h3-rs source tree).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB = None
+
+c_i64, c_int, c_f32, c_u64, c_vp = ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_uint64, ctypes.c_void_p
+
+
+def lib() -> ctypes.CDLL:
+    global _LIB
+    if _LIB is None:
+        path = os.path.join(_HERE, "liboracle.so")
+        if not os.path.exists(path):
+            raise RuntimeError(f"oracle not built: {path} (run `make -C oracle`)")
+        L = ctypes.CDLL(path)
+        L.h3o_gen_size.restype = ctypes.c_size_t
+        L.h3o_gen_u32.restype = ctypes.c_uint32
+        L.h3o_gen_uniform.restype = c_f32
+        L.h3o_fp8e4m3.restype = c_f32
+        L.h3o_fp8e4m3.argtypes = [ctypes.c_uint8]
+        L.h3o_nvfp4_scale_offset.restype = c_i64
+        L.h3o_nvfp4_scale_offset.argtypes = [c_i64, c_i64, c_i64]
+        L.h3o_quant_rows.restype = c_int
+        L.h3o_hadamard.restype = c_int
+        _LIB = L
+    return _LIB
+
+
+def _p(a: np.ndarray) -> ctypes.c_void_p:
+    return ctypes.c_void_p(a.ctypes.data) if a is not None else ctypes.c_void_p(0)
+
+
+# ----------------------------------------------------------------------------- bf16 helpers (kernels.rs:17-23)
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even f32 -> bf16 bit patterns (uint16), NaN -> 0x7fc0."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    nan = (u & 0x7FFFFFFF) > 0x7F800000
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    r[nan] = 0x7FC0
+    return r
+
+
+def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
+    return (np.ascontiguousarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def bf16_round(x: np.ndarray) -> np.ndarray:
+    return bf16_bits_to_f32(f32_to_bf16_bits(x))
+
+
+# ----------------------------------------------------------------------------- seeded generator (rng.rs:8-116)
+
+class TorchGen:
+    """rng.rs TorchGen: PyTorch's CPU mt19937 + normal_fill, one stream shared by consecutive draws."""
+
+    def __init__(self, seed: int):
+        self._buf = ctypes.create_string_buffer(lib().h3o_gen_size())
+        lib().h3o_gen_init(self._buf, c_u64(seed))
+
+    def randn(self, n: int) -> np.ndarray:
+        out = np.empty(n, dtype=np.float32)
+        lib().h3o_gen_randn(self._buf, _p(out), ctypes.c_size_t(n))
+        return out
+
+    def next_u32(self) -> int:
+        return lib().h3o_gen_u32(self._buf)
+
+    def uniform(self) -> float:
+        return lib().h3o_gen_uniform(self._buf)
+
+
+def make_linear_inputs(seed: int, M: int, K: int, N: int, n_outliers: int = 8):
+    """Synthetic W8A8 inputs from one TorchGen stream (x bf16 bits [M,K], w int8 [N,K], ws f32 [N], bias f32 [N]);
+    the draw order is documented in h3q_oracle.c (h3o_make_linear_inputs)."""
+    x = np.empty((M, K), dtype=np.uint16)
+    w = np.empty((N, K), dtype=np.int8)
+    ws = np.empty(N, dtype=np.float32)
+    bias = np.empty(N, dtype=np.float32)
+    lib().h3o_make_linear_inputs(c_u64(seed), c_i64(M), c_i64(K), c_i64(N), c_int(n_outliers),
+                                 _p(x), _p(w), _p(ws), _p(bias))
+    return x, w, ws, bias
+
+
+# ----------------------------------------------------------------------------- rotation / quantization
+
+def hadamard(size: int = 256) -> np.ndarray:
+    """weights.rs:441-465: normalised regular Hadamard (Kronecker powers of H4) as f32 [size, size]."""
+    h = np.empty((size, size), dtype=np.float32)
+    if lib().h3o_hadamard(c_int(size), _p(h)) != 0:
+        raise ValueError(f"ConvRot group size {size} is not a power of 4")
+    return h
+
+
+def rotate_f64(x: np.ndarray) -> np.ndarray:
+    """weights.rs:482-489 rotate_activation in exact (f64) arithmetic; x f32 [rows, K]."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.shape, dtype=np.float64)
+    lib().h3o_rotate_f64(_p(x), _p(out), c_i64(x.shape[0]), c_i64(x.shape[1]))
+    return out
+
+
+QUANT_PLAIN, QUANT_ROT, QUANT_ROT2 = 0, 1, 2
+
+
+def quant_rows(x: np.ndarray, kind: int, mode: int):
+    """Per-row int8 quantizers: mode 0 quant_rows_i8 (kernels.rs:296-318), 1 quant_rows_i8_rot
+    (kernels.rs:166-213), 2 quant_rows_i8_rot2 (kernels.rs:220-293).  x holds raw elements of `kind`
+    (f32 array, or uint16 bit patterns for f16/bf16).  Returns (q int8 [M,K], scale f32 [M])."""
+    x = np.ascontiguousarray(x)
+    M, K = x.shape
+    q = np.empty((M, K), dtype=np.int8)
+    s = np.empty(M, dtype=np.float32)
+    rc = lib().h3o_quant_rows(_p(x), c_int(kind), _p(q), _p(s), c_i64(M), c_i64(K), c_int(mode))
+    if rc != 0:
+        raise ValueError("unsupported quantizer arguments")
+    return q, s
+
+
+def reference_quant_mode(kind: int, K: int, rotate: bool) -> int:
+    """The quantizer kernels::quant_rows_raw selects (kernels.rs:1139-1140)."""
+    if rotate and kind == 2 and K % 256 == 0 and K // 256 <= 56:
+        return QUANT_ROT2
+    return QUANT_ROT if rotate else QUANT_PLAIN
+
+
+def gemm_s8_acc(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """int32 accumulators sum_k a[m,k] b[n,k] (exact)."""
+    a = np.ascontiguousarray(a, dtype=np.int8)
+    b = np.ascontiguousarray(b, dtype=np.int8)
+    # int64 matmul is exact; the accumulators stay far inside int32 for K <= 2^17
+    return (a.astype(np.int64) @ b.astype(np.int64).T).astype(np.int32)
+
+
+EPI_LINEAR, EPI_SWIGLU_PAIRS, EPI_SWIGLU_HALVES, EPI_GELU, EPI_GATE_RESID, EPI_ACC = 0, 1, 2, 3, 4, 5
+
+
+def gemm_s8_epilogue(acc, xs, ws, bias, epi=EPI_LINEAR, gate=None, gate_idx=None, resid=None) -> np.ndarray:
+    """gemm_s8's fused epilogue (attn8.rs:320-343) plus the GELU / gated-residual variants; bf16 bits out."""
+    acc = np.ascontiguousarray(acc, dtype=np.int32)
+    M, N = acc.shape
+    ws = np.ascontiguousarray(ws, dtype=np.float32)
+    per_row = 1 if (ws.size == N and N > 1) else 0
+    out = np.empty((M, N // 2 if epi == EPI_SWIGLU_PAIRS else N), dtype=np.uint16)
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    g = None if gate is None else np.ascontiguousarray(gate, dtype=np.float32)
+    gi = None if gate_idx is None else np.ascontiguousarray(gate_idx, dtype=np.uint32)
+    r = None if resid is None else np.ascontiguousarray(resid, dtype=np.uint16)
+    lib().h3o_gemm_s8_epilogue(_p(acc), _p(np.ascontiguousarray(xs, dtype=np.float32)), _p(ws), c_int(per_row),
+                               _p(b), _p(out), c_i64(M), c_i64(N), c_int(epi), _p(g), _p(gi), _p(r))
+    return out
+
+
+def int8_epilogue(acc, xs, ws, bias, okind: int, swiglu: bool) -> np.ndarray:
+    """int8_epilogue / int8_epilogue_swiglu of the cuBLASLt path (kernels.rs:333-373)."""
+    acc = np.ascontiguousarray(acc, dtype=np.int32)
+    M, Nacc = acc.shape
+    N = Nacc // 2 if swiglu else Nacc
+    ws = np.ascontiguousarray(ws, dtype=np.float32)
+    per_row = 1 if (ws.size == Nacc and Nacc > 1) else 0
+    out = np.empty((M, N), dtype=np.float32 if okind == 0 else np.uint16)
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    lib().h3o_int8_epilogue(_p(acc), _p(np.ascontiguousarray(xs, dtype=np.float32)), _p(ws), c_int(per_row), _p(b),
+                            _p(out), c_int(okind), c_i64(M), c_i64(N), c_int(1 if swiglu else 0))
+    return out
+
+
+def gemm_s8(x_bf16: np.ndarray, w: np.ndarray, ws, bias, swiglu: bool, rotate: bool):
+    """attn8::gemm_s8 restated (attn8.rs:570-581 -> quant_rows_raw + gemm_s8 kernel).
+    Returns (out bf16 bits, q, xs, acc)."""
+    K = x_bf16.shape[1]
+    q, xs = quant_rows(x_bf16, 2, reference_quant_mode(2, K, rotate))
+    acc = gemm_s8_acc(q, w)
+    out = gemm_s8_epilogue(acc, xs, ws, bias, EPI_SWIGLU_PAIRS if swiglu else EPI_LINEAR)
+    return out, q, xs, acc
+
+
+def dequant_i8(q: np.ndarray, scale: np.ndarray, okind: int = 0) -> np.ndarray:
+    """kernels.rs:40-49 / portable/kernels.rs:14-27; scale per row iff it has `rows` entries and rows > 1."""
+    q = np.ascontiguousarray(q, dtype=np.int8)
+    rows, cols = q.shape
+    scale = np.ascontiguousarray(scale, dtype=np.float32)
+    per_row = 1 if (scale.size == rows and rows > 1) else 0
+    out = np.empty((rows, cols), dtype=np.float32 if okind == 0 else np.uint16)
+    lib().h3o_dequant_i8(_p(q), _p(scale), c_int(per_row), _p(out), c_int(okind), c_i64(rows), c_i64(cols))
+    return out
+
+
+def fp8e4m3(v: int) -> float:
+    return lib().h3o_fp8e4m3(v)
+
+
+def nvfp4_scale_offset(r: int, b: int, k: int) -> int:
+    return lib().h3o_nvfp4_scale_offset(r, b, k)
+
+
+def dequant_nvfp4(q: np.ndarray, bs: np.ndarray, g: float, okind: int = 0) -> np.ndarray:
+    """kernels.rs:65-81 / portable/kernels.rs:46-70."""
+    q = np.ascontiguousarray(q, dtype=np.uint8)
+    rows, kp = q.shape
+    k = 2 * kp
+    out = np.empty((rows, k), dtype=np.float32 if okind == 0 else np.uint16)
+    lib().h3o_dequant_nvfp4(_p(q), _p(np.ascontiguousarray(bs, dtype=np.uint8)), c_f32(g), _p(out), c_int(okind),
+                            c_i64(rows), c_i64(k))
+    return out
+
+
+def gate_add(x, y, kind: int, gate, idx) -> np.ndarray:
+    """kernels.rs:418-428."""
+    x = np.ascontiguousarray(x)
+    S, C = x.shape
+    out = np.empty_like(x)
+    lib().h3o_gate_add(_p(x), _p(np.ascontiguousarray(y)), c_int(kind), _p(np.ascontiguousarray(gate, dtype=np.float32)),
+                       _p(np.ascontiguousarray(idx, dtype=np.uint32)), _p(out), c_i64(S), c_i64(C))
+    return out
+
+
+# ----------------------------------------------------------------------------- the reference's CPU path
+
+def cpu_int8_linear(x_bf16: np.ndarray, w: np.ndarray, scale: np.ndarray, bias, rotate: bool, swiglu: bool = False):
+    """portable::int8_linear_ex (portable/kernels.rs:220-242) on bf16 activations: rotate_activation as a
+    matmul with the Hadamard in the activation dtype (weights.rs:482-489; result rounded to bf16), dequant_i8
+    to bf16 (portable/kernels.rs:14-27), float matmul (f32 accumulation here), + bias, optional split-half
+    SwiGLU (ops.rs:39-44), bf16 output.  No activation quantization: this is the reference's CPU semantics
+    and the timed CPU baseline.  Returns bf16 bits."""
+    x = bf16_bits_to_f32(x_bf16)
+    M, K = x.shape
+    if rotate:
+        h = bf16_round(hadamard(256))
+        x = bf16_round((x.reshape(-1, 256) @ h).reshape(M, K))
+    wd = bf16_round(dequant_i8(w, scale, 0))
+    y = x @ wd.T
+    y = bf16_round(y)
+    if bias is not None:
+        y = bf16_round(y + bf16_round(np.asarray(bias, dtype=np.float32))[None, :])
+    if swiglu:
+        f = y.shape[1] // 2
+        g, u = y[:, :f], y[:, f:]
+        y = bf16_round(bf16_round(g / (1.0 + np.exp(-g))) * u)
+    return f32_to_bf16_bits(y)
+
+
+def max_abs_rel(y: np.ndarray, r: np.ndarray) -> float:
+    """max|y - r| / max|r|, the tolerance measure of the parity contract."""
+    y = np.asarray(y, dtype=np.float64)
+    r = np.asarray(r, dtype=np.float64)
+    den = np.max(np.abs(r))
+    return float(np.max(np.abs(y - r)) / den) if den > 0 else float(np.max(np.abs(y - r)))

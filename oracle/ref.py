@@ -1,0 +1,91 @@
+"""TEST INFRASTRUCTURE ONLY -- the reference's own CUDA C kernels (kernels.rs / attn8.rs raw strings),
+compiled for sm_100a into oracle/_ref/libh3ref.so by `make -C oracle ref`, launched exactly as the
+reference's host code launches them.  Used by GPU tests to pin the CPU oracle and the h3q kernels to the
+reference's actual device results.  Takes torch CUDA tensors.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB = None
+
+
+def path() -> str:
+    return os.path.join(_HERE, "_ref", "libh3ref.so")
+
+
+def available() -> bool:
+    return os.path.exists(path())
+
+
+def lib() -> ctypes.CDLL:
+    global _LIB
+    if _LIB is None:
+        _LIB = ctypes.CDLL(path())
+        for name in ("h3ref_quant_rows", "h3ref_quant_rows_linear", "h3ref_int8_epilogue", "h3ref_dequant_i8",
+                     "h3ref_dequant_nvfp4", "h3ref_gate_add", "h3ref_gemm_s8", "h3ref_col_sum",
+                     "h3ref_quant_heads", "h3ref_v_to_f16", "h3ref_attn_qk8"):
+            getattr(_LIB, name).restype = ctypes.c_int
+    return _LIB
+
+
+def _stream():
+    import torch
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _ptr(t):
+    return ctypes.c_void_p(0 if t is None else t.data_ptr())
+
+
+def _check(rc: int, what: str) -> None:
+    if rc != 0:
+        raise RuntimeError(f"{what}: CUDA error {rc}")
+
+
+def quant_rows(x, kind: int, rotate: bool, linear_path: bool = False):
+    """quant_rows_raw (kernels.rs:1133-1161) or, with linear_path, Int8Linear's quantizer (kernels.rs:979-991)."""
+    import torch
+    M, K = x.shape
+    q = torch.empty((M, K), dtype=torch.int8, device=x.device)
+    s = torch.empty(M, dtype=torch.float32, device=x.device)
+    fn = lib().h3ref_quant_rows_linear if linear_path else lib().h3ref_quant_rows
+    _check(fn(_ptr(x), kind, _ptr(q), _ptr(s), M, K, int(rotate), _stream()), "ref quant_rows")
+    return q, s
+
+
+def gemm_s8(a, b, xs, ws, bias, swiglu: bool):
+    """The gemm_s8 kernel (attn8.rs:258-344) on pre-quantized rows; bf16 out as int16 view."""
+    import torch
+    M, K = a.shape
+    N = b.shape[0]
+    out = torch.empty((M, N // 2 if swiglu else N), dtype=torch.bfloat16, device=a.device)
+    per_row = int(ws.numel() == N and N > 1)
+    _check(lib().h3ref_gemm_s8(_ptr(a), _ptr(b), _ptr(xs), _ptr(ws), per_row, _ptr(bias), int(bias is not None),
+                               _ptr(out), M, N, K, int(swiglu), _stream()), "ref gemm_s8")
+    return out
+
+
+def int8_epilogue(acc, xs, ws, bias, out_dtype, swiglu: bool):
+    import torch
+    M, Nacc = acc.shape
+    n_out = Nacc // 2 if swiglu else Nacc
+    out = torch.empty((M, n_out), dtype=out_dtype, device=acc.device)
+    okind = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}[out_dtype]
+    per_row = int(ws.numel() == Nacc and Nacc > 1)
+    _check(lib().h3ref_int8_epilogue(_ptr(acc), _ptr(xs), _ptr(ws), per_row, _ptr(bias), int(bias is not None),
+                                     _ptr(out), okind, ctypes.c_ulonglong(M), ctypes.c_ulonglong(n_out), int(swiglu),
+                                     _stream()), "ref int8_epilogue")
+    return out
+
+
+def dequant_nvfp4(q, bs, g, out_dtype):
+    import torch
+    rows, kp = q.shape
+    out = torch.empty((rows, 2 * kp), dtype=out_dtype, device=q.device)
+    okind = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}[out_dtype]
+    _check(lib().h3ref_dequant_nvfp4(_ptr(q), _ptr(bs), _ptr(g), _ptr(out), ctypes.c_ulonglong(rows),
+                                     ctypes.c_ulonglong(2 * kp), okind, _stream()), "ref dequant_nvfp4")
+    return out

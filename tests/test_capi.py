@@ -1,0 +1,90 @@
+"""CPU tests of the C ABI: the library loads, exports every function include/h3q.h declares, and its host-side
+argument checks (the reference's `bail!`s) answer before any device work.  No GPU calls."""
+import ctypes
+import os
+import re
+
+import pytest
+
+import h3q
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_functions():
+    text = open(os.path.join(ROOT, "include", "h3q.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(h3q_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_the_op_api():
+    names = declared_functions()
+    for expected in ("h3q_gemm_s8", "h3q_int8_linear_ex", "h3q_quant_rows_i8", "h3q_dequant_i8",
+                     "h3q_dequant_nvfp4", "h3q_gate_add", "h3q_available_arch", "h3q_can_fuse_rotation"):
+        assert expected in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = ctypes.CDLL(h3q.LIB_PATH)
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+    assert set(declared_functions()) <= set(h3q.SIGNATURES), "python binding misses a declared symbol"
+
+
+def test_can_fuse_rotation_mirrors_reference_gate():
+    assert h3q.can_fuse_rotation(5120, 256)
+    assert h3q.can_fuse_rotation(16384, 256)
+    assert not h3q.can_fuse_rotation(16640, 256)
+    assert not h3q.can_fuse_rotation(5000, 256)
+    assert not h3q.can_fuse_rotation(5120, 64)
+
+
+def test_workspace_size():
+    assert h3q.lib().h3q_gemm_s8_workspace_size(3, 1024) == 3072 + 12
+    assert h3q.lib().h3q_gemm_s8_workspace_size(3, 1000) == 3072 + 12
+    assert h3q.lib().h3q_gemm_s8_workspace_size(32760, 5120) >= 32760 * 5120 + 4 * 32760
+
+
+def test_gemm_s8_rejects_k_not_multiple_of_64():
+    """attn8.rs:571-573: "gemm_s8: bf16 input with K % 64 == 0 required"."""
+    L = h3q.lib()
+    st = L.h3q_gemm_s8(None, None, None, 1, None, None, 4, 128, 100, 0, 0, None, 0, None)
+    assert st == h3q.ERR_ARG
+    assert "K % 64 == 0" in h3q.last_error()
+
+
+def test_gemm_s8_rejects_odd_swiglu_and_short_workspace():
+    L = h3q.lib()
+    assert L.h3q_gemm_s8(None, None, None, 1, None, None, 4, 127, 128, 1, 0, None, 0, None) == h3q.ERR_ARG
+    assert L.h3q_gemm_s8(None, None, None, 1, None, None, 4, 128, 128, 0, 0, None, 10, None) == h3q.ERR_WORKSPACE
+
+
+def test_int8_linear_ex_shape_checks():
+    """kernels.rs:977 "bad shapes" (k % 4) and kernels.rs:1062 (output width % 4)."""
+    L = h3q.lib()
+    assert L.h3q_int8_linear_ex(None, 2, None, None, 1, None, None, 2, 4, 128, 130, 0, 0, None, 0, None) == h3q.ERR_ARG
+    assert "bad shapes" in h3q.last_error()
+    assert L.h3q_int8_linear_ex(None, 2, None, None, 1, None, None, 2, 4, 6, 128, 0, 0, None, 0, None) == h3q.ERR_ARG
+    assert "multiple of 4" in h3q.last_error()
+    assert L.h3q_int8_linear_ex(None, 5, None, None, 1, None, None, 2, 4, 8, 128, 0, 0, None, 0, None) == h3q.ERR_ARG
+
+
+def test_quant_rows_rotation_checks():
+    L = h3q.lib()
+    assert L.h3q_quant_rows_i8(None, 2, None, None, 4, 300, 1, None) == h3q.ERR_ARG
+    assert "does not divide" in h3q.last_error()
+    assert L.h3q_quant_rows_i8(None, 2, None, None, 4, 256 * 65, 1, None) == h3q.ERR_UNSUPPORTED
+
+
+def test_empty_shapes_are_no_ops():
+    L = h3q.lib()
+    assert L.h3q_gemm_s8(None, None, None, 1, None, None, 0, 128, 128, 0, 0, None, 0, None) == h3q.OK
+    assert L.h3q_quant_rows_i8(None, 2, None, None, 0, 256, 1, None) == h3q.OK
+    assert L.h3q_dequant_i8(None, None, 1, None, 2, 0, 16, None) == h3q.OK
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    monkeypatch.setattr(h3q, "LIB_PATH", str(tmp_path / "nope.so"))
+    monkeypatch.setattr(h3q, "_LIB", None)
+    with pytest.raises(RuntimeError, match="not built"):
+        h3q.lib()
