@@ -106,57 +106,56 @@ def dist_env():
 
 # --------------------------------------------------------------------------------------------- CPU baseline
 
-def cpu_baseline(budget_s: float = 12.0) -> dict:
-    """The reference's CPU path (oracle port of portable/kernels.rs:220-242) on a bounded row sample of every
-    linear of the workload: TOPS = algorithmic ops of the sample / wall time, numpy BLAS on all host cores."""
+def cpu_baseline(rows: int = 256) -> dict:
+    """The reference's CPU path (oracle port of portable/kernels.rs:220-242) for every linear of the workload:
+    each call dequantises the whole weight (timed in full, once per linear, as the reference does per call), then
+    rotates and multiplies the activations (timed on a `rows`-token sample and scaled to 32760 tokens).
+    TOPS = algorithmic ops of the full workload / that extrapolated time.  numpy BLAS uses every host core."""
     import numpy as np
     from oracle import oracle as O
     rng = np.random.default_rng(0)
     cores = os.cpu_count() or 1
-
-    def run(rows: int) -> tuple[float, float]:
-        ops, t = 0.0, 0.0
-        for _, k, n in LINEARS:
-            x = O.f32_to_bf16_bits(rng.standard_normal((rows, k)).astype(np.float32))
-            w = rng.integers(-127, 128, size=(n, k), dtype=np.int8)
-            ws = (rng.random(n, dtype=np.float32) * 9e-3 + 1e-3).astype(np.float32)
-            b = O.bf16_round((rng.standard_normal(n) * 0.02).astype(np.float32))
-            t0 = time.perf_counter()
-            O.cpu_int8_linear(x, w, ws, b, rotate=True)
-            t += time.perf_counter() - t0
-            ops += 2.0 * rows * k * n
-        return ops, t
-
-    ops, t = run(32)
-    rows = 32
-    if t < budget_s / 4:
-        rows = int(min(M_TOKENS, max(32, 32 * (budget_s / 2) / max(t, 1e-3))))
-        rows = max(32, rows // 32 * 32)
-        ops, t = run(rows)
-    return {"value": ops / t / 1e12, "unit": "TOPS", "cores": cores, "kind": "port",
-            "sample": f"{rows} of {M_TOKENS} tokens through each of the 4 linears (weights dequantised per call, "
-                      f"as portable/kernels.rs:220-242 does); {t:.1f} s of CPU work",
-            "seconds": t}
+    t_full, t_deq, t_rows_s = 0.0, 0.0, 0.0
+    for _, k, n in LINEARS:
+        w = rng.integers(-127, 128, size=(n, k), dtype=np.int8)
+        ws = (rng.random(n, dtype=np.float32) * 9e-3 + 1e-3).astype(np.float32)
+        b = O.bf16_round((rng.standard_normal(n) * 0.02).astype(np.float32))
+        x = O.f32_to_bf16_bits(rng.standard_normal((rows, k)).astype(np.float32))
+        t0 = time.perf_counter()
+        wd = O.cpu_dequant_weight(w, ws)
+        t1 = time.perf_counter()
+        O.cpu_linear_rows(x, wd, b, rotate=True)
+        t2 = time.perf_counter()
+        t_deq += t1 - t0
+        t_rows_s += t2 - t1
+        t_full += (t1 - t0) + (t2 - t1) * (M_TOKENS / rows)
+    value = ops_per_step(M_TOKENS) / t_full / 1e12
+    return {"value": value, "unit": "TOPS", "cores": cores, "kind": "port",
+            "sample": f"all 4 linears: full weight dequantisation timed ({t_deq:.1f} s, single-threaded like "
+                      f"portable/kernels.rs:14-27), rotate+matmul timed on {rows} of {M_TOKENS} tokens "
+                      f"({t_rows_s:.1f} s, numpy BLAS on {cores} threads) and scaled linearly to {M_TOKENS} tokens "
+                      f"(extrapolated full-step time {t_full:.1f} s)",
+            "seconds": t_deq + t_rows_s}
 
 
 def run_reference(args) -> None:
+    """--impl reference: the reference's CPU implementation of the path (oracle port; the Rust crate cannot be
+    built here) on this host's cores, same metric, unit and workload; rank 0 only."""
     ws, rank, _ = dist_env()
     if rank != 0:
         return
-    samples = [cpu_baseline(budget_s=8.0) for _ in range(max(1, min(args.steps, 3)))]
+    samples = [cpu_baseline() for _ in range(max(1, min(args.steps, 3)))]
     value = statistics.median(s["value"] for s in samples)
     cb = dict(samples[0])
     cb["value"] = value
     cb.pop("seconds", None)
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": ws, "steps": len(samples),
-        "warmup": 0, "ms_per_step": 2e3 * ops_per_step(M_TOKENS) / 2 / (value * 1e12) * 1e0,
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-        "data": "synthetic", "config": config_block(ws),
+        "warmup": 0, "ms_per_step": 1e3 * ops_per_step(M_TOKENS) / (value * 1e12), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config_block(ws),
         "cpu_baseline": cb,
         "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    line["ms_per_step"] = 1e3 * ops_per_step(M_TOKENS) / (value * 1e12)
     print(json.dumps(line), flush=True)
 
 
@@ -169,6 +168,26 @@ def config_block(n_gpus: int) -> dict:
 
 # --------------------------------------------------------------------------------------------- our arm
 
+def run_profile_case(args) -> None:
+    """One fc1-shaped linear at 4096 tokens (A 21 MB, W 71 MB, out 113 MB: more than L2 in total, a few hundred
+    MB on the device): warmup + steps launches of the quantizer and the GEMM, for ncu --set full captures."""
+    import torch
+    import h3q
+    dev = torch.device("cuda", 0)
+    M, K, N = 4096, 5120, 13824
+    g = torch.Generator(device=dev).manual_seed(7)
+    x = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
+    w = torch.randint(-127, 128, (N, K), generator=g, device=dev, dtype=torch.int8)
+    wsc = torch.rand(N, generator=g, device=dev) * 9e-3 + 1e-3
+    b = torch.zeros(N, device=dev)
+    for _ in range(args.warmup + args.steps):
+        q, xs = h3q.quant_rows(x, True)
+        h3q.gemm_s8_quantized(q, xs, w, wsc, b, h3q.EPI_LINEAR)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": f"M={M} K={K} N={N}", "launches": 2 * (args.warmup + args.steps),
+                      "device_status": h3q.device_status(0)}))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -176,9 +195,14 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", action="store_true",
+                    help="small case for ncu captures: one 4096-token fc1 linear (quant + GEMM), nothing else")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.profile:
+        run_profile_case(args)
         return
 
     import torch

@@ -155,8 +155,8 @@ h3q_status h3q_quant_rows_i8(const void* x, int x_kind, int8_t* q, float* scale,
   if ((order != 0 || k % 256 == 0) && (!aligned16(x) || !aligned16(q)))
     return fail(H3Q_ERR_ARG, "%s: x and q must be 16-byte aligned", what);
   if (order == 0 && k % 256 == 0 && k / 256 > 64)  // wide unrotated rows take the generic kernel
-    return cuda_status(launch_quant_rows(x, x_kind, q, scale, m, k, -1, (cudaStream_t)stream), what);
-  return cuda_status(launch_quant_rows(x, x_kind, q, scale, m, k, order, (cudaStream_t)stream), what);
+    return cuda_status(launch_quant_rows(x, x_kind, q, scale, m, k, -1, error_word(), (cudaStream_t)stream), what);
+  return cuda_status(launch_quant_rows(x, x_kind, q, scale, m, k, order, error_word(), (cudaStream_t)stream), what);
 }
 
 size_t h3q_gemm_s8_workspace_size(int64_t m, int64_t k) { return quant_ws_bytes(m, k); }
@@ -200,7 +200,7 @@ h3q_status h3q_int8_linear_ex(const void* x, int x_kind, const int8_t* w, const 
   if (!x || !xs) return fail(H3Q_ERR_ARG, "%s: null pointer", what);
   if (!aligned16(x)) return fail(H3Q_ERR_ARG, "%s: x must be 16-byte aligned", what);
   cudaError_t e = launch_quant_rows(x, x_kind, qa, xs, m, k, rot ? 1 : (k % 256 == 0 && k / 256 <= 64 ? 0 : -1),
-                                    (cudaStream_t)stream);
+                                    error_word(), (cudaStream_t)stream);
   if (e != cudaSuccess) return cuda_status(e, what);
   return gemm_core(qa, xs, w, scale, scale_numel, bias, out, out_kind, m, n, k, swiglu ? kEpiSwigluHalves : kEpiLinear,
                    nullptr, nullptr, nullptr, (cudaStream_t)stream, what);

@@ -31,7 +31,7 @@ struct GemmArgs {
 };
 
 cudaError_t launch_quant_rows(const void* x, int kind, int8_t* q, float* scale, int64_t M, int64_t K, int order,
-                              cudaStream_t st);
+                              int* err, cudaStream_t st);
 void fill_f32(float* p, float v, int64_t n, cudaStream_t st);
 cudaError_t launch_gemm_i8(const int8_t* A, const int8_t* B, const GemmArgs& a, cudaStream_t st);
 int sm_count(int device);

@@ -18,8 +18,11 @@
 // uses the exact FADD trick (t + 1.5*2^23) instead of F2I conversions, which issue at a quarter of the FP32
 // rate.  One warp-aligned thread team of roundup(4G, 32) threads per row; the row max is a warp reduction
 // plus one shared-memory atomic per warp.
+#include <climits>
 #include <cstdint>
 #include <cuda_bf16.h>
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include "ptx.cuh"
 #include "h3q_internal.h"
@@ -56,13 +59,14 @@ template <> struct In<__nv_bfloat16> {
   }
 };
 
-// One in-register radix-4 stage over the 4 values a[b], a[b+st], a[b+2st], a[b+3st].
+// One in-register radix-4 stage over the 4 values a[b], a[b+st], a[b+2st], a[b+3st].  `s - 2a` is one FFMA:
+// 2a is exact, so fma(-2, a, s) rounds the same real number once, as the reference's `s - 2.f * partner`.
 template <int ORDER>
 __device__ __forceinline__ void h4_inreg(float& a0, float& a1, float& a2, float& a3, bool first) {
   if (ORDER == 2) {
     float s = first ? __fadd_rn(__fadd_rn(__fadd_rn(a0, a1), a2), a3) : __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(a2, a3));
-    float b0 = __fsub_rn(s, __fmul_rn(2.f, a3)), b1 = __fsub_rn(s, __fmul_rn(2.f, a2));
-    float b2 = __fsub_rn(s, __fmul_rn(2.f, a1)), b3 = __fsub_rn(s, __fmul_rn(2.f, a0));
+    float b0 = __fmaf_rn(-2.f, a3, s), b1 = __fmaf_rn(-2.f, a2, s);
+    float b2 = __fmaf_rn(-2.f, a1, s), b3 = __fmaf_rn(-2.f, a0, s);
     a0 = b0; a1 = b1; a2 = b2; a3 = b3;
   } else {
     float b0 = __fsub_rn(__fadd_rn(__fadd_rn(a0, a1), a2), a3);
@@ -73,14 +77,14 @@ __device__ __forceinline__ void h4_inreg(float& a0, float& a1, float& a2, float&
   }
 }
 
-// Digit 3: lane j of a quad holds a_j; returns out_j.
+// Digit 3: lane j of a quad holds a_j; returns out_j (not yet multiplied by 1/16).
 template <int ORDER>
 __device__ __forceinline__ float h4_quad(float a, int j) {
   if (ORDER == 2) {
     float s1 = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 1));
     float s = __fadd_rn(s1, __shfl_xor_sync(0xffffffffu, s1, 2));
     float p = __shfl_xor_sync(0xffffffffu, a, 3);
-    return __fsub_rn(s, __fmul_rn(2.f, p));
+    return __fmaf_rn(-2.f, p, s);
   } else {
     float x1 = __shfl_xor_sync(0xffffffffu, a, 1);
     float x2 = __shfl_xor_sync(0xffffffffu, a, 2);
@@ -94,79 +98,142 @@ __device__ __forceinline__ float h4_quad(float a, int j) {
   }
 }
 
-// int8 code of t = v * inv: nearest-even integer through t + 1.5*2^23 (exact for |t| < 2^22; |t| <= 127 here
-// by construction of inv), NaN -> 0 (order 2) or -128 (orders 0/1).
+// int8 code of t = v * inv as a byte: nearest-even integer through t + 1.5*2^23 (exact for |t| < 2^22; |t| <=
+// 127 here by construction of inv).  NaN -> 0 (order 2, cvt.rni) or -128 (orders 0/1, fmaxf(rintf(t), -128)).
 template <int ORDER>
 __device__ __forceinline__ uint32_t code_of(float t) {
-  const float r = __fadd_rn(t, 12582912.0f);
-  uint32_t b = (uint32_t)(__float_as_int(r) - 0x4B400000) & 0xffu;
-  if (t != t) b = ORDER == 2 ? 0u : 0x80u;
-  return b;
+  if (ORDER != 2) t = fmaxf(t, -128.f);
+  const uint32_t b = (uint32_t)__float_as_int(__fadd_rn(t, 12582912.0f)) & 0xffu;
+  return (ORDER == 2 && t != t) ? 0u : b;
 }
 
-template <int ORDER, typename Tin>
-__global__ void __launch_bounds__(256, 2) quant_rows_kernel(const Tin* __restrict__ x, int8_t* __restrict__ q,
-                                                          float* __restrict__ scale, int64_t M, int K, int tpr,
-                                                          int rows_per_block) {
-  __shared__ unsigned s_max[32];
-  const int G = K >> 8;
-  const int rl = threadIdx.x / tpr, t = threadIdx.x % tpr;
-  const int64_t row = (int64_t)blockIdx.x * rows_per_block + rl;
-  const bool active = (row < M) && (t < 4 * G);
-  const int g = t >> 2, j = t & 3;
-  if (threadIdx.x < 32) s_max[threadIdx.x] = 0u;
-
-  constexpr int V = In<Tin>::kVec;
-  float v[64];
-  if (active) {
-    const uint4* src = reinterpret_cast<const uint4*>(x + row * (int64_t)K + g * 256 + j * 64);
-    uint4 raw[64 / V];
+// 64 values of one thread: rotated in place (digits 0..2 in registers, digit 3 across the lane quad), without
+// the final 1/16 (applied exactly through the scale: both are powers of two).
+template <int ORDER>
+__device__ __forceinline__ void rotate64(float (&v)[64], int j) {
+  if (ORDER == 0) return;
 #pragma unroll
-    for (int i = 0; i < 64 / V; ++i) raw[i] = __ldg(src + i);
+  for (int d = 0, st = 1; d < 3; ++d, st *= 4) {
 #pragma unroll
-    for (int i = 0; i < 64 / V; ++i) In<Tin>::cvt(raw[i], v + i * V);
-  } else {
-#pragma unroll
-    for (int i = 0; i < 64; ++i) v[i] = 0.f;
+    for (int b = 0; b < 64; ++b) {
+      if ((b / st) % 4 != 0) continue;
+      h4_inreg<ORDER>(v[b], v[b + st], v[b + 2 * st], v[b + 3 * st], d == 0);
+    }
   }
+#pragma unroll
+  for (int c = 0; c < 64; ++c) v[c] = h4_quad<ORDER>(v[c], j);
+}
 
-  if (ORDER != 0) {
-    // digits 0, 1, 2 in registers (element c of the thread has digits c&3, (c>>2)&3, (c>>4)&3)
+// Persistent row quantizer.  One CTA = one team of roundup(4G, 32) threads working through rows
+// blockIdx.x, blockIdx.x + gridDim.x, ...; thread t < 4G owns elements [64t, 64t + 64) of the row.  Rows arrive
+// by TMA (the row viewed as [K*es/128] x 128-byte lines, 128-byte swizzle) into a 3-stage ring, two rows ahead
+// of the compute; with the swizzle each thread's 16-byte reads of its own line are bank-conflict free.
+constexpr int kQStages = 3;
+
+template <int ORDER, typename Tin>
+__global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__ CUtensorMap tmx,
+                                                         int8_t* __restrict__ q, float* __restrict__ scale,
+                                                         int64_t M, int K, int box_rows, int boxes_per_row,
+                                                         int* err) {
+  extern __shared__ uint8_t qsm_raw[];
+  uint8_t* qsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(qsm_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t full[kQStages];
+  __shared__ unsigned s_max[3];
+  __shared__ int s_abort;
+  constexpr int ES = sizeof(Tin);
+  constexpr int LINES = 64 * ES / 128;  // 128-byte lines per thread: 1 (16-bit) or 2 (f32)
+  const int G = K >> 8;
+  const int t = threadIdx.x, j = t & 3;
+  const bool owner = t < 4 * G;
+  const uint32_t row_bytes = (uint32_t)K * ES;
+  const uint32_t stage_bytes = (row_bytes + 1023u) & ~1023u;
+
+  if (t == 0) {
+    for (int s = 0; s < kQStages; ++s) mbar_init(&full[s], 1);
+    s_max[0] = s_max[1] = s_max[2] = 0u;
+    s_abort = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  auto issue = [&](int64_t row, int stage) {
+    mbar_arrive_expect_tx(&full[stage], row_bytes);
+    for (int b = 0; b < boxes_per_row; ++b)
+      tma_load_2d(qsm + (size_t)stage * stage_bytes + (size_t)b * box_rows * 128, &tmx, &full[stage], 0,
+                  (int32_t)(row * box_rows * boxes_per_row + b * box_rows));
+  };
+  if (t == 0) {
+    tma_prefetch_desc(&tmx);
+    for (int s = 0; s < kQStages; ++s) {
+      const int64_t r = blockIdx.x + (int64_t)s * gridDim.x;
+      if (r < M) issue(r, s);
+    }
+  }
+  int it = 0;
+  for (int64_t row = blockIdx.x; row < M; row += gridDim.x, ++it) {
+    const int stage = it % kQStages;
+    if (!mbar_wait_bounded(&full[stage], (uint32_t)(it / kQStages) & 1u, &s_abort, err, kDevTimeoutFull)) break;
+    float v[64];
+    if (owner) {
+      const uint8_t* base = qsm + (size_t)stage * stage_bytes;
 #pragma unroll
-    for (int d = 0, st = 1; d < 3; ++d, st *= 4) {
+      for (int l = 0; l < LINES; ++l) {
+        const int line = t * LINES + l;
 #pragma unroll
-      for (int b = 0; b < 64; ++b) {
-        if ((b / st) % 4 != 0) continue;
-        h4_inreg<ORDER>(v[b], v[b + st], v[b + 2 * st], v[b + 3 * st], d == 0);
+        for (int c = 0; c < 8; ++c) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(base + line * 128 + ((c ^ (line & 7)) << 4));
+          In<Tin>::cvt(raw, v + (l * 8 + c) * In<Tin>::kVec);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < 64; ++c) v[c] = 0.f;
+    }
+    rotate64<ORDER>(v, j);
+    float m = 0.f;
+#pragma unroll
+    for (int c = 0; c < 64; ++c) m = fmaxf(m, fabsf(v[c]));
+    const unsigned mw = __reduce_max_sync(0xffffffffu, __float_as_uint(m));
+    const int slot = it % 3;
+    if ((t & 31) == 0) atomicMax(&s_max[slot], mw);
+    __syncthreads();  // the whole row is read out of `stage` and its max is complete
+    if (t == 0) {
+      s_max[(it + 1) % 3] = 0u;
+      const int64_t nr = row + (int64_t)kQStages * gridDim.x;
+      if (nr < M) {
+        fence_proxy_async_smem();
+        issue(nr, stage);
       }
     }
-    // digit 3 across the quad, then the 1/16 normalisation
+    // scale from the true max (the 1/16 of the rotation is folded in exactly: powers of two)
+    const float mx = ORDER == 0 ? __uint_as_float(s_max[slot]) : __fmul_rn(__uint_as_float(s_max[slot]), 0.0625f);
+    const float s = fmaxf(__fdiv_rn(mx, 127.f), 1e-30f);
+    const float inv = ORDER == 0 ? __fdiv_rn(1.f, s) : __fmul_rn(__fdiv_rn(1.f, s), 0.0625f);
+    if (t == 0) scale[row] = s;
+    if (owner) {
+      uint32_t w[16];
 #pragma unroll
-    for (int c = 0; c < 64; ++c) v[c] = __fmul_rn(h4_quad<ORDER>(v[c], j), 0.0625f);
+      for (int i = 0; i < 16; ++i)
+        w[i] = __byte_perm(__byte_perm(code_of<ORDER>(__fmul_rn(v[4 * i], inv)),
+                                       code_of<ORDER>(__fmul_rn(v[4 * i + 1], inv)), 0x0040),
+                           __byte_perm(code_of<ORDER>(__fmul_rn(v[4 * i + 2], inv)),
+                                       code_of<ORDER>(__fmul_rn(v[4 * i + 3], inv)), 0x0040),
+                           0x5410);
+      uint4* dst = reinterpret_cast<uint4*>(q + row * (int64_t)K + t * 64);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+    }
   }
-
-  float m = 0.f;
-#pragma unroll
-  for (int c = 0; c < 64; ++c) m = fmaxf(m, fabsf(v[c]));
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  // drain: a CTA that stopped early must not exit with its own row loads in flight
   __syncthreads();
-  if ((threadIdx.x & 31) == 0) atomicMax(&s_max[rl], __float_as_uint(m));
-  __syncthreads();
-  const float mx = __uint_as_float(s_max[rl]);
-  const float s = fmaxf(__fdiv_rn(mx, 127.f), 1e-30f);
-  const float inv = __fdiv_rn(1.f, s);
-  if (!active) return;
-  if (t == 0) scale[row] = s;
-  uint32_t w[16];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    w[i] = code_of<ORDER>(__fmul_rn(v[4 * i], inv)) | (code_of<ORDER>(__fmul_rn(v[4 * i + 1], inv)) << 8) |
-           (code_of<ORDER>(__fmul_rn(v[4 * i + 2], inv)) << 16) | (code_of<ORDER>(__fmul_rn(v[4 * i + 3], inv)) << 24);
+  if (t == 0) {
+    int dummy = 0;
+    for (int k = 0; k < kQStages; ++k) {
+      const int i2 = it + k;  // loads issued for iterations it .. it+kQStages-1 may be pending
+      const int64_t r = blockIdx.x + (int64_t)i2 * gridDim.x;
+      if (r < M) mbar_wait_bounded(&full[i2 % kQStages], (uint32_t)(i2 / kQStages) & 1u, &dummy, err, kDevTimeoutDrain);
+    }
   }
-  uint4* dst = reinterpret_cast<uint4*>(q + row * (int64_t)K + g * 256 + j * 64);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+  __syncthreads();
 }
 
 // Unrotated per-row quantization for any K (quant_rows_i8, kernels.rs:296-318): one 256-thread block per row,
@@ -199,20 +266,71 @@ __global__ void __launch_bounds__(256) quant_rows_plain_kernel(const Tin* __rest
   for (int i = threadIdx.x; i < K; i += 256) qr[i] = (int8_t)code_of<0>(__fmul_rn(ld(i), inv));
 }
 
+static PFN_cuTensorMapEncodeTiled_v12000 q_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult qr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &qr) == cudaSuccess &&
+        qr == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  }
+  return fn;
+}
+
 template <int ORDER, typename Tin>
-static cudaError_t launch_rows(const void* x, int8_t* q, float* scale, int64_t M, int K, cudaStream_t st) {
+static cudaError_t launch_rows(const void* x, int8_t* q, float* scale, int64_t M, int K, int* err, cudaStream_t st) {
+  constexpr int ES = sizeof(Tin);
   const int G = K / 256;
-  const int tpr = ((4 * G + 31) / 32) * 32;
-  int rpb = 1;
-  while (rpb * 2 * tpr <= 256 && rpb * 2 <= 32) rpb *= 2;
-  const int64_t blocks = (M + rpb - 1) / rpb;
-  quant_rows_kernel<ORDER, Tin><<<(unsigned)blocks, tpr * rpb, 0, st>>>(static_cast<const Tin*>(x), q, scale, M, K,
-                                                                        tpr, rpb);
-  return cudaGetLastError();
+  const int threads = ((4 * G + 31) / 32) * 32;
+  const int lines = K * ES / 128;  // 128-byte lines per row (4G for 16-bit input, 8G for f32)
+  // TMA boxes hold at most 256 lines; each box must start on a 1024-byte (8-line) swizzle atom
+  int box_rows = lines;
+  if (lines > 256) {
+    int d = G < 32 ? G : 32;
+    while (G % d != 0) --d;
+    box_rows = 8 * d;
+  }
+  const int boxes = lines / box_rows;
+  auto fn = q_encode_fn();
+  if (!fn) return cudaErrorInvalidValue;
+  const size_t stage_bytes = ((size_t)K * ES + 1023) / 1024 * 1024;
+  const size_t smem = 1024 + kQStages * stage_bytes;
+  auto kern = quant_rows_kernel<ORDER, Tin>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  int dev = 0, per_sm = 0;
+  cudaGetDevice(&dev);
+  e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem);
+  if (e != cudaSuccess) return e;
+  if (per_sm < 1) per_sm = 1;
+  const int64_t want = (int64_t)per_sm * sm_count(dev);
+  // TMA row coordinates are int32: launch in chunks of rows whose line index stays below 2^31
+  const int64_t chunk = ((int64_t)INT32_MAX - 256) / lines;
+  for (int64_t r0 = 0; r0 < M; r0 += chunk) {
+    const int64_t mc = (M - r0) < chunk ? (M - r0) : chunk;
+    // the activation rows [r0, r0 + mc) as [mc * lines] x 128 bytes (elements of ES bytes)
+    CUtensorMap m;
+    cuuint64_t dims[2] = {(cuuint64_t)(128 / ES), (cuuint64_t)mc * lines};
+    cuuint64_t strides[1] = {128};
+    cuuint32_t box[2] = {(cuuint32_t)(128 / ES), (cuuint32_t)box_rows};
+    cuuint32_t es[2] = {1, 1};
+    const CUtensorMapDataType dt = ES == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+    const char* xb = static_cast<const char*>(x) + r0 * (int64_t)K * ES;
+    if (fn(&m, dt, 2, const_cast<char*>(xb), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+    const unsigned grid = (unsigned)(mc < want ? mc : want);
+    kern<<<grid, threads, smem, st>>>(m, q + r0 * (int64_t)K, scale + r0, mc, K, box_rows, boxes, err);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
 }
 
 cudaError_t launch_quant_rows(const void* x, int kind, int8_t* q, float* scale, int64_t M, int64_t K, int order,
-                              cudaStream_t st) {
+                              int* err, cudaStream_t st) {
   if (M == 0) return cudaSuccess;
   if (order < 0 || (order == 0 && (K % 256 != 0 || K / 256 > 64))) {
     if (kind == 0) quant_rows_plain_kernel<float><<<(unsigned)M, 256, 0, st>>>((const float*)x, q, scale, (int)K);
@@ -226,9 +344,9 @@ cudaError_t launch_quant_rows(const void* x, int kind, int8_t* q, float* scale, 
     return cudaGetLastError();
   }
 #define H3Q_Q(O)                                                                        \
-  if (kind == 0) return launch_rows<O, float>(x, q, scale, M, (int)K, st);               \
-  if (kind == 1) return launch_rows<O, __half>(x, q, scale, M, (int)K, st);              \
-  return launch_rows<O, __nv_bfloat16>(x, q, scale, M, (int)K, st);
+  if (kind == 0) return launch_rows<O, float>(x, q, scale, M, (int)K, err, st);          \
+  if (kind == 1) return launch_rows<O, __half>(x, q, scale, M, (int)K, err, st);         \
+  return launch_rows<O, __nv_bfloat16>(x, q, scale, M, (int)K, err, st);
   if (order == 2) { H3Q_Q(2) }
   if (order == 1) { H3Q_Q(1) }
   H3Q_Q(0)

@@ -393,10 +393,11 @@ static float gelu_tanh_f(float y) {
  * epi 0: out[m,n] = bf16(v)
  * epi 1: SwiGLU over interleaved (gate, up) column pairs (attn8.rs:334-337):
  *        gt = bf16r(v0), up = bf16r(v1), sg = bf16r(gt / (1 + exp(-gt))), out[m,n/2] = bf16(sg * up)
- * epi 2: out = bf16(gelu_tanh(bf16r(v)))  (candle gelu applied to the bf16 linear output, ops.rs:46-48)
- * epi 3: out = bf16(fmaf(bf16r(v), bf16r(gate[idx[m], n]), resid[m,n]))  (gate_add on the bf16 output,
+ * epi 3: out = bf16(gelu_tanh(bf16r(v)))  (candle gelu applied to the bf16 linear output, ops.rs:46-48)
+ * epi 4: out = bf16(fmaf(bf16r(v), bf16r(gate[idx[m], n]), resid[m,n]))  (gate_add on the bf16 output,
  *        kernels.rs:418-428; `x + y * g` contracted)
  * ws_per_row: ws has N entries, else ws[0] for every column (attn8.rs:553).  bias may be NULL.
+ * The epi numbers are the H3Q_EPI_* values of include/h3q.h.
  */
 H3O_API void h3o_gemm_s8_epilogue(const int32_t* acc, const float* xs, const float* ws, int ws_per_row,
                                   const float* bias, uint16_t* out, int64_t M, int64_t N, int epi,
@@ -418,9 +419,9 @@ H3O_API void h3o_gemm_s8_epilogue(const int32_t* acc, const float* xs, const flo
             float w = ws_per_row ? ws[n] : ws[0];
             float v = fmaf((float)acc[m * N + n] * x, w, bias ? bias[n] : 0.f);
             float o;
-            if (epi == 2) {
+            if (epi == 3) {
                 o = gelu_tanh_f(bf16r(v));
-            } else if (epi == 3) {
+            } else if (epi == 4) {
                 uint32_t gi = gate_idx ? gate_idx[m] : 0u;
                 float g = bf16r(gate[(size_t)gi * N + n]);
                 o = fmaf(bf16r(v), g, bf2f(resid[m * N + n]));

@@ -230,20 +230,23 @@ def gate_add(x, y, kind: int, gate, idx) -> np.ndarray:
 
 # ----------------------------------------------------------------------------- the reference's CPU path
 
-def cpu_int8_linear(x_bf16: np.ndarray, w: np.ndarray, scale: np.ndarray, bias, rotate: bool, swiglu: bool = False):
-    """portable::int8_linear_ex (portable/kernels.rs:220-242) on bf16 activations: rotate_activation as a
-    matmul with the Hadamard in the activation dtype (weights.rs:482-489; result rounded to bf16), dequant_i8
-    to bf16 (portable/kernels.rs:14-27), float matmul (f32 accumulation here), + bias, optional split-half
-    SwiGLU (ops.rs:39-44), bf16 output.  No activation quantization: this is the reference's CPU semantics
-    and the timed CPU baseline.  Returns bf16 bits."""
+def cpu_dequant_weight(w: np.ndarray, scale: np.ndarray) -> np.ndarray:
+    """dequant_i8 to the activation dtype (bf16, held as f32 values): the per-call weight decode of the
+    reference's CPU path (portable/kernels.rs:14-27 via weights.rs:598-604)."""
+    return bf16_bits_to_f32(dequant_i8(w, scale, 2))
+
+
+def cpu_linear_rows(x_bf16: np.ndarray, wd: np.ndarray, bias, rotate: bool, swiglu: bool = False) -> np.ndarray:
+    """The row-dependent part of portable::int8_linear_ex (portable/kernels.rs:220-242) on bf16 activations:
+    rotate_activation as a matmul with the Hadamard in the activation dtype (weights.rs:482-489; result rounded
+    to bf16), float matmul with the dequantised weight (f32 accumulation here), + bias, optional split-half
+    SwiGLU (ops.rs:39-44), bf16 output (bits).  No activation quantization."""
     x = bf16_bits_to_f32(x_bf16)
     M, K = x.shape
     if rotate:
         h = bf16_round(hadamard(256))
         x = bf16_round((x.reshape(-1, 256) @ h).reshape(M, K))
-    wd = bf16_round(dequant_i8(w, scale, 0))
-    y = x @ wd.T
-    y = bf16_round(y)
+    y = bf16_round(x @ wd.T)
     if bias is not None:
         y = bf16_round(y + bf16_round(np.asarray(bias, dtype=np.float32))[None, :])
     if swiglu:
@@ -251,6 +254,12 @@ def cpu_int8_linear(x_bf16: np.ndarray, w: np.ndarray, scale: np.ndarray, bias, 
         g, u = y[:, :f], y[:, f:]
         y = bf16_round(bf16_round(g / (1.0 + np.exp(-g))) * u)
     return f32_to_bf16_bits(y)
+
+
+def cpu_int8_linear(x_bf16: np.ndarray, w: np.ndarray, scale: np.ndarray, bias, rotate: bool, swiglu: bool = False):
+    """portable::int8_linear_ex (portable/kernels.rs:220-242): dequantise, then the float linear.  This is the
+    reference's CPU semantics and the timed CPU baseline.  Returns bf16 bits."""
+    return cpu_linear_rows(x_bf16, cpu_dequant_weight(w, scale), bias, rotate, swiglu)
 
 
 def max_abs_rel(y: np.ndarray, r: np.ndarray) -> float:
