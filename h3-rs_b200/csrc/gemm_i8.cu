@@ -23,16 +23,28 @@
 namespace h3q {
 
 namespace {
-constexpr int BM = 128, BN = 256, BK = 128, STAGES = 4;
-constexpr int A_STAGE = BM * BK;              // 16 KiB
-constexpr int B_STAGE = BN * BK;              // 32 KiB
-constexpr int STAGE_BYTES = A_STAGE + B_STAGE;
+constexpr int BK = 128;                       // K bytes per pipeline stage (one 128-byte swizzle row)
 constexpr int THREADS = 192;
-constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t TMEM_COLS = 512;           // two 256-column int32 accumulators
 constexpr int GROUP_M = 16;                   // tile-rows swept together across N (L2 reuse of B)
-constexpr size_t SMEM_BYTES = 1024 + (size_t)STAGES * STAGE_BYTES + 256;
-constexpr uint32_t IDESC = idesc_i8(BM, BN);
+constexpr int EPI_BUF = 4096;                 // one staging buffer: 32 rows x up to 128 bytes
+constexpr int EPI_SMEM = 4 * 2 * EPI_BUF;     // 4 epilogue warps, double buffered
 }  // namespace
+
+// Compile-time shape of the two kernel variants.  PAIR: a CTA pair (cluster of 2) computes a 256 x 256 tile with
+// tcgen05.mma.cta_group::2, each CTA loading 128 rows of A and 128 rows of B; single: one CTA computes 128 x 256.
+template <bool PAIR>
+struct GemmCfg {
+  static constexpr int kStages = PAIR ? 6 : 4;
+  static constexpr int kBRows = PAIR ? 128 : 256;   // B rows held by one CTA
+  static constexpr int kAStage = 128 * BK;          // 16 KiB
+  static constexpr int kBStage = kBRows * BK;
+  static constexpr int kStageBytes = kAStage + kBStage;
+  static constexpr int kTileM = PAIR ? 256 : 128;   // output rows per tile
+  static constexpr uint32_t kTxBytes = PAIR ? 2 * kStageBytes : kStageBytes;  // bytes landing per stage
+  static constexpr uint32_t kIdesc = idesc_i8(PAIR ? 256 : 128, 256);
+  static constexpr size_t kSmem = 1024 + (size_t)kStages * kStageBytes + EPI_SMEM + 256;
+};
 
 __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
   const int per_group = GROUP_M * num_n;
@@ -61,40 +73,18 @@ __device__ __forceinline__ void load_vec32(const float* p, int64_t col0, int val
   }
 }
 
-// Store n (<= 32) f32 values to row `dst` in the output kind; vector stores when all 32 fit.
-__device__ __forceinline__ void store_row(void* out, int kind, int64_t off, const float (&v)[32], int n, int valid) {
+// 32 f32 values -> packed words of the output kind (0 f32, 1 f16, 2 bf16); returns the row-chunk width in bytes.
+__device__ __forceinline__ int pack_out(const float (&v)[32], int kind, uint32_t (&w)[32]) {
   if (kind == 0) {
-    float* d = reinterpret_cast<float*>(out) + off;
-    if (valid == n) {
 #pragma unroll
-      for (int i = 0; i < 32; i += 4)
-        if (i < n) *reinterpret_cast<float4*>(d + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-    } else {
-      for (int i = 0; i < valid; ++i) d[i] = v[i];
-    }
-    return;
+    for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(v[i]);
+    return 128;
   }
-  uint16_t* d = reinterpret_cast<uint16_t*>(out) + off;
-  if (valid == n) {
 #pragma unroll
-    for (int i = 0; i < 32; i += 8) {
-      if (i < n) {
-        uint4 w;
-        if (kind == 2) {
-          w.x = pack_bf2(v[i], v[i + 1]); w.y = pack_bf2(v[i + 2], v[i + 3]);
-          w.z = pack_bf2(v[i + 4], v[i + 5]); w.w = pack_bf2(v[i + 6], v[i + 7]);
-        } else {
-          w.x = (uint32_t)f2h(v[i]) | ((uint32_t)f2h(v[i + 1]) << 16);
-          w.y = (uint32_t)f2h(v[i + 2]) | ((uint32_t)f2h(v[i + 3]) << 16);
-          w.z = (uint32_t)f2h(v[i + 4]) | ((uint32_t)f2h(v[i + 5]) << 16);
-          w.w = (uint32_t)f2h(v[i + 6]) | ((uint32_t)f2h(v[i + 7]) << 16);
-        }
-        *reinterpret_cast<uint4*>(d + i) = w;
-      }
-    }
-  } else {
-    for (int i = 0; i < valid; ++i) d[i] = kind == 2 ? (uint16_t)f2bf(v[i]) : f2h(v[i]);
-  }
+  for (int i = 0; i < 16; ++i)
+    w[i] = kind == 2 ? pack_bf2(v[2 * i], v[2 * i + 1])
+                     : ((uint32_t)f2h(v[2 * i]) | ((uint32_t)f2h(v[2 * i + 1]) << 16));
+  return 64;
 }
 
 __device__ __forceinline__ float gelu_tanh(float y) {
@@ -102,11 +92,41 @@ __device__ __forceinline__ float gelu_tanh(float y) {
   return 0.5f * y * (1.f + tanhf(c * (y + 0.044715f * y * y * y)));
 }
 
-// Epilogue of one 128 x 256 accumulator tile; this thread owns tile row `lr` (TMEM lane) = output row `row`.
+// One warp's TMA-store epilogue: each lane stages its row of a 32-row box into a swizzled shared-memory buffer
+// (the TMA swizzle of the box's row width W, which also makes the 16-byte writes bank-conflict free), then lane
+// 0 stores the box.  Two buffers alternate; a buffer is rewritten only after its previous store has read it.
+struct EpiWarp {
+  const CUtensorMap* map;
+  uint8_t* buf;  // 2 * EPI_BUF bytes, 1024-aligned
+  int sel;
+  int lane;
+
+  __device__ __forceinline__ void store(const uint32_t (&w)[32], int W, int32_t x, int32_t y, bool do_store) {
+    if (lane == 0) bulk_wait_read<1>();
+    __syncwarp();
+    uint8_t* b = buf + sel * EPI_BUF + lane * W;
+    const int sw = W == 128 ? (lane & 7) : (W == 64 ? ((lane >> 1) & 3) : ((lane >> 2) & 1));
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (i < W / 16)
+        *reinterpret_cast<uint4*>(b + ((i ^ sw) << 4)) = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0 && do_store) {
+      tma_store_2d(map, buf + sel * EPI_BUF, x, y);
+      bulk_commit();
+    }
+    sel ^= 1;
+  }
+};
+
+// Epilogue of one accumulator tile for the 32 output rows of this warp (TMEM lanes 32q..32q+31 of `tacc`).
+// `row` is this lane's output row, `row0` the warp's first row, `nb` the tile column.
 template <int EPI>
-__device__ __forceinline__ void epilogue_tile(const GemmArgs& p, uint32_t tacc, int64_t row, int nb, bool kzero,
-                                              bool ws_al, bool b_al) {
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& p, EpiWarp& ew, uint32_t tacc, int64_t row,
+                                              int64_t row0, int nb, bool kzero, bool ws_al, bool b_al) {
   const bool rv = row < p.M;
+  const bool wv = row0 < p.M;  // any row of this warp's box inside the output
   const float xs = (EPI != kEpiAccI32 && rv) ? __ldg(p.xs + row) : 0.f;
   const float ws0 = (EPI == kEpiAccI32 || p.ws_per_row) ? 0.f : __ldg(p.ws);
   if (EPI == kEpiSwigluHalves) {
@@ -146,7 +166,9 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& p, uint32_t tacc, 
         if (p.out_kind == 2) { s = bf16r(s); u = bf16r(u); }
         o[i] = __fmul_rn(s, u);
       }
-      if (rv && valid > 0) store_row(p.out, p.out_kind, row * F + j0, o, 32, valid);
+      uint32_t w[32];
+      const int W = pack_out(o, p.out_kind, w);
+      ew.store(w, W, (int32_t)j0, (int32_t)row0, wv && valid > 0);
     }
     return;
   }
@@ -160,20 +182,13 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& p, uint32_t tacc, 
 #pragma unroll
       for (int i = 0; i < 32; ++i) r[i] = 0u;
     }
-    const int64_t col0 = (int64_t)nb * BN + 32 * c;
+    const int64_t col0 = (int64_t)nb * 256 + 32 * c;
     const int valid = clamp32(p.N - col0);
+    const bool st = wv && valid > 0;
     if (EPI == kEpiAccI32) {
-      if (rv && valid > 0) {
-        int32_t* d = reinterpret_cast<int32_t*>(p.out) + row * p.N + col0;
-        if (valid == 32) {
-#pragma unroll
-          for (int i = 0; i < 32; i += 4)
-            *reinterpret_cast<int4*>(d + i) = make_int4((int)r[i], (int)r[i + 1], (int)r[i + 2], (int)r[i + 3]);
-        } else {
-          for (int i = 0; i < valid; ++i) d[i] = (int)r[i];
-        }
-      }
-    } else {
+      ew.store(r, 128, (int32_t)col0, (int32_t)row0, st);
+      continue;
+    }
     float w[32], b[32];
     if (p.ws_per_row) load_vec32(p.ws, col0, valid, ws_al, w);
     else {
@@ -188,70 +203,81 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& p, uint32_t tacc, 
     float v[32];
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __fmaf_rn(__fmul_rn((float)(int)r[i], xs), w[i], b[i]);
-    if (!rv || valid <= 0) {
-    } else if (EPI == kEpiSwigluPairs) {
-      float o[32];
+    uint32_t o[32];
+    if (EPI == kEpiSwigluPairs) {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float gt = bf16r(v[2 * i]), up = bf16r(v[2 * i + 1]);
-        const float sg = bf16r(__fdiv_rn(gt, __fadd_rn(1.f, __expf(-gt))));
-        o[i] = __fmul_rn(sg, up);
+      for (int i = 0; i < 8; ++i) {
+        float h[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const float gt = bf16r(v[4 * i + 2 * k]), up = bf16r(v[4 * i + 2 * k + 1]);
+          const float sg = bf16r(__fdiv_rn(gt, __fadd_rn(1.f, __expf(-gt))));
+          h[k] = __fmul_rn(sg, up);
+        }
+        o[i] = pack_bf2(h[0], h[1]);
       }
-#pragma unroll
-      for (int i = 16; i < 32; ++i) o[i] = 0.f;
-      store_row(p.out, 2, row * (p.N / 2) + col0 / 2, o, 16, valid / 2);
+      ew.store(o, 32, (int32_t)(col0 / 2), (int32_t)row0, st);
     } else if (EPI == kEpiGelu) {
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = gelu_tanh(bf16r(v[i]));
-      store_row(p.out, 2, row * p.N + col0, v, 32, valid);
+      ew.store(o, pack_out(v, 2, o), (int32_t)col0, (int32_t)row0, st);
     } else if (EPI == kEpiGateResid) {
-      const uint32_t gi = p.gate_idx ? __ldg(p.gate_idx + row) : 0u;
       float g[32];
-      load_vec32(p.gate + (int64_t)gi * p.N, col0, valid, false, g);
-      const uint16_t* rs = p.resid + row * p.N + col0;
       uint16_t rr[32];
-      if (valid == 32) {
+      if (rv) {
+        const uint32_t gi = p.gate_idx ? __ldg(p.gate_idx + row) : 0u;
+        load_vec32(p.gate + (int64_t)gi * p.N, col0, valid, false, g);
+        const uint16_t* rs = p.resid + row * p.N + col0;
+        if (valid == 32) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) *reinterpret_cast<uint4*>(rr + 8 * i) = __ldg(reinterpret_cast<const uint4*>(rs) + i);
+          for (int i = 0; i < 4; ++i)
+            *reinterpret_cast<uint4*>(rr + 8 * i) = __ldg(reinterpret_cast<const uint4*>(rs) + i);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) rr[i] = i < valid ? rs[i] : (uint16_t)0;
+        }
       } else {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) rr[i] = i < valid ? rs[i] : (uint16_t)0;
+        for (int i = 0; i < 32; ++i) { g[i] = 0.f; rr[i] = 0; }
       }
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = __fmaf_rn(bf16r(v[i]), bf16r(g[i]), bf2f(rr[i]));
-      store_row(p.out, 2, row * p.N + col0, v, 32, valid);
+      ew.store(o, pack_out(v, 2, o), (int32_t)col0, (int32_t)row0, st);
     } else {
-      store_row(p.out, p.out_kind, row * p.N + col0, v, 32, valid);
-    }
+      ew.store(o, pack_out(v, p.out_kind, o), (int32_t)col0, (int32_t)row0, st);
     }
   }
 }
 
-template <int EPI>
+template <int EPI, bool PAIR>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const GemmArgs p, int num_m, int num_n, int nk) {
+                   const __grid_constant__ CUtensorMap tmO, const GemmArgs p, int num_m, int num_n, int nk) {
+  using C = GemmCfg<PAIR>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * A_STAGE;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_STAGE);
-  uint64_t* empty = full + STAGES;
-  uint64_t* accf = empty + STAGES;
+  uint8_t* sB = smem + C::kStages * C::kAStage;
+  uint8_t* sE = sB + C::kStages * C::kBStage;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sE + EPI_SMEM);
+  uint64_t* empty = full + C::kStages;
+  uint64_t* accf = empty + C::kStages;
   uint64_t* acce = accf + 2;
   uint64_t* mma_done = acce + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&accf[a], 1);
-      mbar_init(&acce[a], 128);
+      mbar_init(&acce[a], PAIR ? 8 : 4);
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -260,108 +286,149 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 0 && lane == 0 && nk > 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmO);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
-    tmem_relinquish();
+    if (PAIR) {
+      tmem_alloc_pair(tmem_slot, TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if (PAIR) cluster_sync(); else __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int num_tiles = num_m * num_n;
+  const int unit = PAIR ? (int)(blockIdx.x >> 1) : (int)blockIdx.x;
+  const int units = PAIR ? (int)(gridDim.x >> 1) : (int)gridDim.x;
   const bool halves = (EPI == kEpiSwigluHalves);
   const int64_t F = p.N / 2;
 
   if (warp == 0) {
     if (elect_one()) {
-      // ---------------------------------------------------------------- TMA producer
+      // ------------------------------------------------------------------ TMA producer (both CTAs of a pair)
       int stage = 0;
       uint32_t phase = 0;
       uint32_t issued_mask = 0, issued_par = 0;
-      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
+      for (int t = unit; t < num_tiles; t += units) {
         int mb, nb;
         tile_coords(t, num_m, num_n, mb, nb);
-        const int32_t b0 = halves ? nb * 128 : nb * BN;
-        const int32_t b1 = halves ? (int32_t)(F + nb * 128) : nb * BN + 128;
+        const int32_t arow = mb * C::kTileM + (int32_t)rank * 128;
+        int32_t b0, b1;
+        if (PAIR) {
+          b0 = halves ? (rank == 0 ? nb * 128 : (int32_t)(F + nb * 128)) : nb * 256 + (int32_t)rank * 128;
+          b1 = b0;
+        } else {
+          b0 = halves ? nb * 128 : nb * 256;
+          b1 = halves ? (int32_t)(F + nb * 128) : nb * 256 + 128;
+        }
         bool ok = true;
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag, p.err, kDevTimeoutEmpty)) { ok = false; break; }
-          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
-          tma_load_2d(sA + stage * A_STAGE, &tmA, &full[stage], kb * BK, mb * BM);
-          tma_load_2d(sB + stage * B_STAGE, &tmB, &full[stage], kb * BK, b0);
-          tma_load_2d(sB + stage * B_STAGE + B_STAGE / 2, &tmB, &full[stage], kb * BK, b1);
+          if (leader) mbar_arrive_expect_tx(&full[stage], C::kTxBytes);
+          uint8_t* a_dst = sA + stage * C::kAStage;
+          uint8_t* b_dst = sB + stage * C::kBStage;
+          if (PAIR) {
+            const uint32_t fb = mapa_shared(&full[stage], 0);
+            tma_load_2d_pair(a_dst, &tmA, fb, kb * BK, arow);
+            tma_load_2d_pair(b_dst, &tmB, fb, kb * BK, b0);
+          } else {
+            tma_load_2d(a_dst, &tmA, &full[stage], kb * BK, arow);
+            tma_load_2d(b_dst, &tmB, &full[stage], kb * BK, b0);
+            tma_load_2d(b_dst + C::kBStage / 2, &tmB, &full[stage], kb * BK, b1);
+          }
           issued_mask |= 1u << stage;
           issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          if (++stage == C::kStages) { stage = 0; phase ^= 1; }
         }
         if (!ok) break;
       }
-      // drain: every load this thread issued must land before the CTA may exit
-      for (int s = 0; s < STAGES; ++s) {
-        if (!(issued_mask & (1u << s))) continue;
-        int dummy = 0;
-        mbar_wait_bounded(&full[s], (issued_par >> s) & 1u, &dummy, p.err, kDevTimeoutDrain);
-      }
+      // drain: the loads of every stage must land before the pair may exit (the leader's barriers count both
+      // CTAs' bytes, so the leader's drain covers the peer's loads too; the final cluster barrier holds the peer)
+      if (leader)
+        for (int s = 0; s < C::kStages; ++s)
+          if (issued_mask & (1u << s)) mbar_drain(&full[s], (issued_par >> s) & 1u, p.err, kDevTimeoutDrain);
     }
   } else if (warp == 1) {
-    if (elect_one()) {
-      // ---------------------------------------------------------------- MMA issuer
+    if (leader && elect_one()) {
+      // ------------------------------------------------------------------ MMA issuer (pair leader only)
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
-      for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+      for (int t = unit; t < num_tiles; t += units, ++it) {
         const int acc = it & 1;
         const uint32_t accph = (it >> 1) & 1;
         if (!mbar_wait_bounded(&acce[acc], accph ^ 1, abort_flag, p.err, kDevTimeoutAccEmpty)) break;
         tc_fence_after();
-        const uint32_t d = tmem_base + acc * BN;
+        const uint32_t d = tmem_base + acc * 256;
         bool ok = true;
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait_bounded(&full[stage], phase, abort_flag, p.err, kDevTimeoutFull)) { ok = false; break; }
           tc_fence_after();
-          const uint64_t da = smem_desc_k128(smem_u32(sA + stage * A_STAGE));
-          const uint64_t db = smem_desc_k128(smem_u32(sB + stage * B_STAGE));
+          const uint64_t da = smem_desc_k128(smem_u32(sA + stage * C::kAStage));
+          const uint64_t db = smem_desc_k128(smem_u32(sB + stage * C::kBStage));
 #pragma unroll
-          for (int k = 0; k < BK / 32; ++k)
-            mma_i8(d, da + (uint64_t)(k * 2), db + (uint64_t)(k * 2), IDESC, (kb | k) != 0);
-          mma_commit(&empty[stage]);
-          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+          for (int k = 0; k < BK / 32; ++k) {
+            if (PAIR) mma_i8_pair(d, da + (uint64_t)(k * 2), db + (uint64_t)(k * 2), C::kIdesc, (kb | k) != 0);
+            else mma_i8(d, da + (uint64_t)(k * 2), db + (uint64_t)(k * 2), C::kIdesc, (kb | k) != 0);
+          }
+          if (PAIR) {
+            mma_commit_pair(mapa_shared(&empty[stage], 0));
+            mma_commit_pair(mapa_shared(&empty[stage], 1));
+          } else {
+            mma_commit(&empty[stage]);
+          }
+          if (++stage == C::kStages) { stage = 0; phase ^= 1; }
         }
         if (!ok) break;
-        mma_commit(&accf[acc]);
+        if (PAIR) {
+          mma_commit_pair(mapa_shared(&accf[acc], 0));
+          mma_commit_pair(mapa_shared(&accf[acc], 1));
+        } else {
+          mma_commit(&accf[acc]);
+        }
       }
       // every MMA this thread issued must complete before TMEM is released
-      mma_commit(mma_done);
-      int dummy = 0;
-      mbar_wait_bounded(mma_done, 0, &dummy, p.err, kDevTimeoutDrain);
+      if (PAIR) mma_commit_pair(mapa_shared(mma_done, 0));
+      else mma_commit(mma_done);
+      mbar_drain(mma_done, 0, p.err, kDevTimeoutDrain);
     }
   } else {
-    // ------------------------------------------------------------------ epilogue warps 2..5
+    // -------------------------------------------------------------------- epilogue warps 2..5 (both CTAs)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const bool ws_al = (reinterpret_cast<uintptr_t>(p.ws) & 15) == 0;
     const bool b_al = p.bias && (reinterpret_cast<uintptr_t>(p.bias) & 15) == 0;
+    EpiWarp ew{&tmO, sE + (warp - 2) * 2 * EPI_BUF, 0, lane};
     int it = 0;
-    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++it) {
+    for (int t = unit; t < num_tiles; t += units, ++it) {
       const int acc = it & 1;
       const uint32_t accph = (it >> 1) & 1;
       int mb, nb;
       tile_coords(t, num_m, num_n, mb, nb);
       if (!mbar_wait_bounded(&accf[acc], accph, abort_flag, p.err, kDevTimeoutAccFull)) break;
       tc_fence_after();
-      const int64_t row = (int64_t)mb * BM + 32 * q + lane;
-      const uint32_t tacc = tmem_base + ((uint32_t)(32 * q) << 16) + acc * BN;
-      epilogue_tile<EPI>(p, tacc, row, nb, nk == 0, ws_al, b_al);
+      const int64_t row0 = (int64_t)mb * C::kTileM + (int64_t)rank * 128 + 32 * q;
+      const uint32_t tacc = tmem_base + ((uint32_t)(32 * q) << 16) + acc * 256;
+      epilogue_tile<EPI>(p, ew, tacc, row0 + lane, row0, nb, nk == 0, ws_al, b_al);
       tc_fence_before();
-      mbar_arrive(&acce[acc]);
+      __syncwarp();
+      if (lane == 0) {
+        if (PAIR) mbar_arrive_cluster(mapa_shared(&acce[acc], 0));
+        else mbar_arrive(&acce[acc]);
+      }
     }
+    if (lane == 0) bulk_wait_all();
   }
   __syncwarp();
   tc_fence_before();
-  __syncthreads();
+  if (PAIR) cluster_sync(); else __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if (PAIR) tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 
@@ -404,52 +471,115 @@ int sm_count(int device) {
   return cache[device];
 }
 
-template <int EPI>
-static cudaError_t launch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int num_m, int num_n,
-                              int nk, int grid, cudaStream_t st) {
-  static bool attr_set[64] = {false};
+// Output tensor map for the epilogue's TMA stores: [M, nout] row-major, box = (W / es) columns x 32 rows,
+// swizzle matching the box's row width W.
+static bool make_tmap_out(CUtensorMap* m, void* base, uint64_t rows, uint64_t cols, int es, int W) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * (uint64_t)es};
+  cuuint32_t box[2] = {(cuuint32_t)(W / es), 32};
+  cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType dt =
+      es == 4 ? CU_TENSOR_MAP_DATA_TYPE_UINT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
+  const CUtensorMapSwizzle sw =
+      W == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : (W == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+  return fn(m, dt, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int EPI, bool PAIR>
+static cudaError_t launch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+                              const GemmArgs& a, int num_m, int num_n, int nk, cudaStream_t st) {
+  using C = GemmCfg<PAIR>;
+  auto kern = gemm_i8_kernel<EPI, PAIR>;
+  static int grid_cache[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_i8_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)SMEM_BYTES);
-    if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.blockDim = dim3(THREADS, 1, 1);
+  cfg.dynamicSmemBytes = C::kSmem;
+  cfg.stream = st;
+  if (PAIR) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
   }
-  gemm_i8_kernel<EPI><<<grid, THREADS, SMEM_BYTES, st>>>(ta, tb, a, num_m, num_n, nk);
-  return cudaGetLastError();
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!grid_cache[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)C::kSmem);
+    if (e != cudaSuccess) return e;
+    int units = sm_count(dev);
+    if (PAIR) {
+      // size the persistent grid by the clusters that can be co-resident, so no pair waits for another to finish
+      int clusters = 0;
+      cfg.gridDim = dim3(2 * (sm_count(dev) / 2), 1, 1);
+      e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+      if (e != cudaSuccess) return e;
+      units = clusters > 0 ? clusters : 1;
+    }
+    grid_cache[dev] = units;
+  }
+  const int64_t tiles = (int64_t)num_m * num_n;
+  const int units = (int)(tiles < grid_cache[dev] ? tiles : grid_cache[dev]);
+  cfg.gridDim = dim3(PAIR ? 2 * units : units, 1, 1);
+  return cudaLaunchKernelEx(&cfg, kern, ta, tb, to, a, num_m, num_n, nk);
+}
+
+// Row-chunk width (bytes) of the staged output and the output element size, by epilogue.
+static void out_geometry(const GemmArgs& a, int& es, int& W, int64_t& nout) {
+  const int kes = a.out_kind == 0 ? 4 : 2;
+  switch (a.epi) {
+    case kEpiSwigluPairs: es = 2; W = 32; nout = a.N / 2; break;
+    case kEpiSwigluHalves: es = kes; W = 32 * kes; nout = a.N / 2; break;
+    case kEpiGelu:
+    case kEpiGateResid: es = 2; W = 64; nout = a.N; break;
+    case kEpiAccI32: es = 4; W = 128; nout = a.N; break;
+    default: es = kes; W = 32 * kes; nout = a.N; break;
+  }
+}
+
+template <bool PAIR>
+static cudaError_t launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+                                  const GemmArgs& a, int num_n, int nk, cudaStream_t st) {
+  const int num_m = (int)((a.M + GemmCfg<PAIR>::kTileM - 1) / GemmCfg<PAIR>::kTileM);
+  switch (a.epi) {
+    case kEpiLinear: return launch_epi<kEpiLinear, PAIR>(ta, tb, to, a, num_m, num_n, nk, st);
+    case kEpiSwigluPairs: return launch_epi<kEpiSwigluPairs, PAIR>(ta, tb, to, a, num_m, num_n, nk, st);
+    case kEpiSwigluHalves: return launch_epi<kEpiSwigluHalves, PAIR>(ta, tb, to, a, num_m, num_n, nk, st);
+    case kEpiGelu: return launch_epi<kEpiGelu, PAIR>(ta, tb, to, a, num_m, num_n, nk, st);
+    case kEpiGateResid: return launch_epi<kEpiGateResid, PAIR>(ta, tb, to, a, num_m, num_n, nk, st);
+    case kEpiAccI32: return launch_epi<kEpiAccI32, PAIR>(ta, tb, to, a, num_m, num_n, nk, st);
+    default: return cudaErrorInvalidValue;
+  }
 }
 
 cudaError_t launch_gemm_i8(const int8_t* A, const int8_t* B, const GemmArgs& a, cudaStream_t st) {
   if (a.M == 0) return cudaSuccess;
   const bool halves = a.epi == kEpiSwigluHalves;
-  const int64_t ncols_tiles = halves ? (a.N / 2 + 127) / 128 : (a.N + BN - 1) / BN;
+  const int64_t ncols_tiles = halves ? (a.N / 2 + 127) / 128 : (a.N + 255) / 256;
   if (ncols_tiles == 0) return cudaSuccess;
-  CUtensorMap ta, tb;
+  int es, W;
+  int64_t nout;
+  out_geometry(a, es, W, nout);
+  CUtensorMap ta, tb, to;
+  if (!make_tmap_out(&to, a.out, (uint64_t)a.M, (uint64_t)nout, es, W)) return cudaErrorInvalidValue;
   if (a.K > 0) {
-    if (!make_tmap_i8(&ta, A, (uint64_t)a.M, (uint64_t)a.K, BM)) return cudaErrorInvalidValue;
+    if (!make_tmap_i8(&ta, A, (uint64_t)a.M, (uint64_t)a.K, 128)) return cudaErrorInvalidValue;
     if (!make_tmap_i8(&tb, B, (uint64_t)a.N, (uint64_t)a.K, 128)) return cudaErrorInvalidValue;
   } else {
     // K == 0: no tile is ever loaded (the epilogue sees zero accumulators); the maps only need to be valid
-    if (!make_tmap_i8(&ta, a.out, 1, 16, BM)) return cudaErrorInvalidValue;
+    if (!make_tmap_i8(&ta, a.out, 1, 16, 128)) return cudaErrorInvalidValue;
     tb = ta;
   }
-  const int num_m = (int)((a.M + BM - 1) / BM);
-  const int num_n = (int)ncols_tiles;
   const int nk = (int)((a.K + BK - 1) / BK);
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const int64_t tiles = (int64_t)num_m * num_n;
-  const int grid = (int)(tiles < sm_count(dev) ? tiles : sm_count(dev));
-  switch (a.epi) {
-    case kEpiLinear: return launch_epi<kEpiLinear>(ta, tb, a, num_m, num_n, nk, grid, st);
-    case kEpiSwigluPairs: return launch_epi<kEpiSwigluPairs>(ta, tb, a, num_m, num_n, nk, grid, st);
-    case kEpiSwigluHalves: return launch_epi<kEpiSwigluHalves>(ta, tb, a, num_m, num_n, nk, grid, st);
-    case kEpiGelu: return launch_epi<kEpiGelu>(ta, tb, a, num_m, num_n, nk, grid, st);
-    case kEpiGateResid: return launch_epi<kEpiGateResid>(ta, tb, a, num_m, num_n, nk, grid, st);
-    case kEpiAccI32: return launch_epi<kEpiAccI32>(ta, tb, a, num_m, num_n, nk, grid, st);
-    default: return cudaErrorInvalidValue;
-  }
+  // 256-row pair tiles when there are at least two 128-row tiles of work, else one CTA per 128 x 256 tile
+  if (a.M > 128) return launch_variant<true>(ta, tb, to, a, (int)ncols_tiles, nk, st);
+  return launch_variant<false>(ta, tb, to, a, (int)ncols_tiles, nk, st);
 }
 
 }  // namespace h3q
