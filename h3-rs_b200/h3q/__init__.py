@@ -37,6 +37,7 @@ SIGNATURES = {
     "h3q_dequant_i8": (_int, [_vp, _vp, _i64, _vp, _int, _i64, _i64, _vp]),
     "h3q_dequant_nvfp4": (_int, [_vp, _vp, _vp, _vp, _int, _i64, _i64, _vp]),
     "h3q_gate_add": (_int, [_vp, _vp, _int, _vp, _vp, _vp, _i64, _i64, _vp]),
+    "h3q_gemm_s8_static": (_int, [_vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _int, _int, _vp]),
 }
 
 

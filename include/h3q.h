@@ -123,6 +123,19 @@ h3q_status h3q_dequant_nvfp4(const uint8_t* q, const uint8_t* block_scale, const
 h3q_status h3q_gate_add(const void* x, const void* y, int kind, const float* gate, const uint32_t* idx, void* out,
                         int64_t s, int64_t c, void* stream);
 
+/* h3q_gemm_s8 for callers that cannot allocate device memory (no counterpart in the reference).  Some callers
+ * cannot call cudaMalloc: a plugin inside a host that has already reserved the GPU's whole memory for its own
+ * pool, or code where cudaMalloc's implicit synchronisation or failure under memory pressure is not acceptable.
+ * This entry point takes no workspace: the quantized activations live in a fixed 64 MiB device array inside the
+ * library, held on every GPU that loads the library until the process exits, and the call allocates nothing.
+ * Same arguments and results as h3q_gemm_s8 (bit-identical outputs).  Limits: 256 + roundup(m*k, 256) + 4*m
+ * bytes must fit in the 64 MiB (else H3Q_ERR_ARG); the first call on a device looks up the array's address and
+ * should come before any stream capture; all calls on a device share the array, so calls that overlap on the GPU
+ * race; kernel time-outs are latched in the array's own status word, not the one h3q_device_status reads. */
+h3q_status h3q_gemm_s8_static(const uint16_t* x, const int8_t* w, const float* ws, int64_t ws_numel,
+                              const float* bias, uint16_t* out, int64_t m, int64_t n, int64_t k, int swiglu,
+                              int rotate, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
