@@ -77,26 +77,61 @@ __device__ __forceinline__ void h4_inreg(float& a0, float& a1, float& a2, float&
   }
 }
 
-// Digit 3: lane j of a quad holds a_j; returns out_j (not yet multiplied by 1/16).
+// Paired f32 arithmetic (sm_100 add/sub/mul/fma.f32x2): two independent IEEE-rounded operations per
+// instruction, each lane rounded exactly like the scalar instruction.
+struct f2 {
+  uint64_t v;
+};
+__device__ __forceinline__ f2 pk(float lo, float hi) {
+  f2 r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r.v) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void upk(f2 a, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(a.v));
+}
+__device__ __forceinline__ f2 add2(f2 a, f2 b) {
+  f2 r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+  return r;
+}
+__device__ __forceinline__ f2 sub2(f2 a, f2 b) {
+  f2 r;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+  return r;
+}
+__device__ __forceinline__ f2 mul2(f2 a, f2 b) {
+  f2 r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
+  return r;
+}
+__device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) {
+  f2 r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r.v) : "l"(a.v), "l"(b.v), "l"(c.v));
+  return r;
+}
+
+// Digit-3 butterfly of two columns at once: a_p holds (column c, column c+1) for digit-3 value p.
 template <int ORDER>
-__device__ __forceinline__ float h4_quad(float a, int j) {
+__device__ __forceinline__ void h4_pair(f2& a0, f2& a1, f2& a2, f2& a3) {
   if (ORDER == 2) {
-    float s1 = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, 1));
-    float s = __fadd_rn(s1, __shfl_xor_sync(0xffffffffu, s1, 2));
-    float p = __shfl_xor_sync(0xffffffffu, a, 3);
-    return __fmaf_rn(-2.f, p, s);
+    const f2 s = add2(add2(a0, a1), add2(a2, a3));
+    const f2 m2 = pk(-2.f, -2.f);
+    const f2 b0 = fma2(m2, a3, s), b1 = fma2(m2, a2, s), b2 = fma2(m2, a1, s), b3 = fma2(m2, a0, s);
+    a0 = b0; a1 = b1; a2 = b2; a3 = b3;
   } else {
-    float x1 = __shfl_xor_sync(0xffffffffu, a, 1);
-    float x2 = __shfl_xor_sync(0xffffffffu, a, 2);
-    float x3 = __shfl_xor_sync(0xffffffffu, a, 3);
-    // ((P + Q) + R) + S reproduces each lane's left-to-right formula exactly (x+y == y+x, x-y == x+(-y)).
-    float P = j < 2 ? a : x2;
-    float Q = j < 2 ? x1 : -x3;
-    float R = j == 0 ? x2 : (j == 1 ? -x3 : (j == 2 ? a : x1));
-    float S = j == 0 ? -x3 : (j == 1 ? x2 : (j == 2 ? x1 : a));
-    return __fadd_rn(__fadd_rn(__fadd_rn(P, Q), R), S);
+    const f2 b0 = sub2(add2(add2(a0, a1), a2), a3);
+    const f2 b1 = add2(sub2(add2(a0, a1), a2), a3);
+    const f2 b2 = add2(add2(sub2(a0, a1), a2), a3);
+    const f2 b3 = add2(add2(sub2(a1, a0), a2), a3);
+    a0 = b0; a1 = b1; a2 = b2; a3 = b3;
   }
 }
+
+// Slot of a thread's 16-byte chunk c inside its exchange line: c ^ f(t).  With f(t) = (t & 7) ^ bit2(t), the
+// 8 lanes of a shared-memory phase hit 8 different bank groups both when each writes its own line and when the
+// lanes of two quads read chunks 2j, 2j+1 of one quad member's line.
+__device__ __forceinline__ int xslot(int t) { return (t & 7) ^ ((t >> 2) & 1); }
 
 // int8 code of t = v * inv as a byte: nearest-even integer through t + 1.5*2^23 (exact for |t| < 2^22; |t| <=
 // 127 here by construction of inv).  NaN -> 0 (order 2, cvt.rni) or -128 (orders 0/1, fmaxf(rintf(t), -128)).
@@ -107,11 +142,9 @@ __device__ __forceinline__ uint32_t code_of(float t) {
   return (ORDER == 2 && t != t) ? 0u : b;
 }
 
-// 64 values of one thread: rotated in place (digits 0..2 in registers, digit 3 across the lane quad), without
-// the final 1/16 (applied exactly through the scale: both are powers of two).
+// Digits 0..2 of the thread's 64 values, in registers (element c has digits c&3, (c>>2)&3, (c>>4)&3).
 template <int ORDER>
-__device__ __forceinline__ void rotate64(float (&v)[64], int j) {
-  if (ORDER == 0) return;
+__device__ __forceinline__ void rotate_inreg(float (&v)[64]) {
 #pragma unroll
   for (int d = 0, st = 1; d < 3; ++d, st *= 4) {
 #pragma unroll
@@ -120,8 +153,6 @@ __device__ __forceinline__ void rotate64(float (&v)[64], int j) {
       h4_inreg<ORDER>(v[b], v[b + st], v[b + 2 * st], v[b + 3 * st], d == 0);
     }
   }
-#pragma unroll
-  for (int c = 0; c < 64; ++c) v[c] = h4_quad<ORDER>(v[c], j);
 }
 
 // Persistent row quantizer.  One CTA = one team of roundup(4G, 32) threads working through rows
@@ -188,10 +219,65 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
 #pragma unroll
       for (int c = 0; c < 64; ++c) v[c] = 0.f;
     }
-    rotate64<ORDER>(v, j);
+    // Digit 3 crosses the quad.  Transpose through shared memory in two rounds of 32 columns, each thread
+    // writing into its own (already consumed) 128-byte line of this stage: afterwards thread j holds, for all
+    // four digit-3 values, columns 8j..8j+7 (round 0) and 32+8j..32+8j+7 (round 1) of its group.
+    float u[4][16];  // u[d3][i]
+    if (ORDER != 0) {
+      rotate_inreg<ORDER>(v);
+      uint8_t* xb = qsm + (size_t)stage * stage_bytes;
+      uint8_t* own = xb + (size_t)t * LINES * 128;
+      const int fo = xslot(t);
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        if (owner) {
+#pragma unroll
+          for (int c = 0; c < 8; ++c)
+            *reinterpret_cast<float4*>(own + ((c ^ fo) << 4)) =
+                make_float4(v[32 * r + 4 * c], v[32 * r + 4 * c + 1], v[32 * r + 4 * c + 2], v[32 * r + 4 * c + 3]);
+        }
+        __syncwarp();
+        if (owner) {
+#pragma unroll
+          for (int d3 = 0; d3 < 4; ++d3) {
+            const int tp = (t & ~3) | d3;
+            const uint8_t* line = xb + (size_t)tp * LINES * 128;
+            const int fp = xslot(tp);
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const float4 f = *reinterpret_cast<const float4*>(line + (((2 * j + e) ^ fp) << 4));
+              u[d3][8 * r + 4 * e] = f.x; u[d3][8 * r + 4 * e + 1] = f.y;
+              u[d3][8 * r + 4 * e + 2] = f.z; u[d3][8 * r + 4 * e + 3] = f.w;
+            }
+          }
+        } else {
+#pragma unroll
+          for (int d3 = 0; d3 < 4; ++d3)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) u[d3][8 * r + i] = 0.f;
+        }
+        __syncwarp();
+      }
+      fence_proxy_async_smem();  // these generic writes precede a later TMA refill of the stage
+#pragma unroll
+      for (int i = 0; i < 16; i += 2) {
+        f2 a0 = pk(u[0][i], u[0][i + 1]), a1 = pk(u[1][i], u[1][i + 1]);
+        f2 a2 = pk(u[2][i], u[2][i + 1]), a3 = pk(u[3][i], u[3][i + 1]);
+        h4_pair<ORDER>(a0, a1, a2, a3);
+        upk(a0, u[0][i], u[0][i + 1]); upk(a1, u[1][i], u[1][i + 1]);
+        upk(a2, u[2][i], u[2][i + 1]); upk(a3, u[3][i], u[3][i + 1]);
+      }
+    } else {
+#pragma unroll
+      for (int d3 = 0; d3 < 4; ++d3)
+#pragma unroll
+        for (int i = 0; i < 16; ++i) u[d3][i] = v[16 * d3 + i];
+    }
     float m = 0.f;
 #pragma unroll
-    for (int c = 0; c < 64; ++c) m = fmaxf(m, fabsf(v[c]));
+    for (int d3 = 0; d3 < 4; ++d3)
+#pragma unroll
+      for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(u[d3][i]));
     const unsigned mw = __reduce_max_sync(0xffffffffu, __float_as_uint(m));
     const int slot = it % 3;
     if ((t & 31) == 0) atomicMax(&s_max[slot], mw);
@@ -210,17 +296,35 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
     const float inv = ORDER == 0 ? __fdiv_rn(1.f, s) : __fmul_rn(__fdiv_rn(1.f, s), 0.0625f);
     if (t == 0) scale[row] = s;
     if (owner) {
-      uint32_t w[16];
+      const f2 inv2 = pk(inv, inv), rnd2 = pk(12582912.0f, 12582912.0f);
+      uint32_t w[16];  // w[2*h + k]: bytes of u[d3 = h>>1][8*(h&1) + 4k .. +3]
 #pragma unroll
-      for (int i = 0; i < 16; ++i)
-        w[i] = __byte_perm(__byte_perm(code_of<ORDER>(__fmul_rn(v[4 * i], inv)),
-                                       code_of<ORDER>(__fmul_rn(v[4 * i + 1], inv)), 0x0040),
-                           __byte_perm(code_of<ORDER>(__fmul_rn(v[4 * i + 2], inv)),
-                                       code_of<ORDER>(__fmul_rn(v[4 * i + 3], inv)), 0x0040),
-                           0x5410);
-      uint4* dst = reinterpret_cast<uint4*>(q + row * (int64_t)K + t * 64);
+      for (int h = 0; h < 8; ++h) {
+        const int d3 = h >> 1, i0 = 8 * (h & 1);
+        uint32_t b[8];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+        for (int e = 0; e < 8; e += 2) {
+          float t0, t1, r0, r1;
+          const f2 tt = mul2(pk(u[d3][i0 + e], u[d3][i0 + e + 1]), inv2);
+          upk(tt, t0, t1);
+          if (ORDER != 2) { t0 = fmaxf(t0, -128.f); t1 = fmaxf(t1, -128.f); }
+          upk(add2(pk(t0, t1), rnd2), r0, r1);
+          b[e] = (ORDER == 2 && t0 != t0) ? 0u : (__float_as_uint(r0) & 0xffu);
+          b[e + 1] = (ORDER == 2 && t1 != t1) ? 0u : (__float_as_uint(r1) & 0xffu);
+        }
+        w[2 * h] = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
+        w[2 * h + 1] = __byte_perm(__byte_perm(b[4], b[5], 0x0040), __byte_perm(b[6], b[7], 0x0040), 0x5410);
+      }
+      if (ORDER != 0) {
+        int8_t* dst = q + row * (int64_t)K + (t >> 2) * 256 + 8 * j;
+#pragma unroll
+        for (int h = 0; h < 8; ++h)
+          *reinterpret_cast<uint2*>(dst + 64 * (h >> 1) + 32 * (h & 1)) = make_uint2(w[2 * h], w[2 * h + 1]);
+      } else {
+        uint4* dst = reinterpret_cast<uint4*>(q + row * (int64_t)K + t * 64);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+      }
     }
   }
   // drain: a CTA that stopped early must not exit with its own row loads in flight
