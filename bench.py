@@ -288,6 +288,13 @@ def main() -> None:
     gemm_avg_ms = gemm_ms / launches
     quant_bytes_launch = sum(3.0 * M * k + 4.0 * M for _, k, _ in LINEARS) / len(LINEARS)
     quant_avg_ms = quant_ms / launches
+    per_linear = []
+    for i, (nm, k, n) in enumerate(LINEARS):
+        g_ms = sum(ev[s][i][1].elapsed_time(ev[s][i][2]) for s in range(args.steps)) / args.steps
+        q_ms = sum(ev[s][i][0].elapsed_time(ev[s][i][1]) for s in range(args.steps)) / args.steps
+        per_linear.append({"linear": f"{nm}:{k}x{n}", "gemm_ms": round(g_ms, 4),
+                           "gemm_tops": round(2.0 * M * k * n / (g_ms * 1e-3) / 1e12, 1), "quant_ms": round(q_ms, 4),
+                           "quant_gbs": round((3.0 * M * k + 4.0 * M) / (q_ms * 1e-3) / 1e9, 1)})
     peaks = load_peaks()
     int8_peak = 2.0 * peaks["bf16_tflops"]
     achieved = gemm_ops_launch / (gemm_avg_ms * 1e-3) / 1e12
@@ -358,6 +365,7 @@ def main() -> None:
                            "achieved": q_achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                            "frac": q_achieved / peaks["hbm_gbs"], "avg_launch_ms": quant_avg_ms,
                            "bytes_per_launch": quant_bytes_launch},
+        "per_linear": per_linear,
         "cpu_baseline": cb, "e2e": e2e, "clocks": clk.summary(),
         "gpu_launches": 2 * launches,
     }

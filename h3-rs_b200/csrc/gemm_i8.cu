@@ -26,7 +26,6 @@ namespace {
 constexpr int BK = 128;                       // K bytes per pipeline stage (one 128-byte swizzle row)
 constexpr int THREADS = 192;
 constexpr uint32_t TMEM_COLS = 512;           // two 256-column int32 accumulators
-constexpr int GROUP_M = 16;                   // tile-rows swept together across N (L2 reuse of B)
 constexpr int EPI_BUF = 4096;                 // one staging buffer: 32 rows x up to 128 bytes
 constexpr int EPI_SMEM = 4 * 2 * EPI_BUF;     // 4 epilogue warps, double buffered
 }  // namespace
@@ -46,11 +45,13 @@ struct GemmCfg {
   static constexpr size_t kSmem = 1024 + (size_t)kStages * kStageBytes + EPI_SMEM + 256;
 };
 
-__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& mb, int& nb) {
-  const int per_group = GROUP_M * num_n;
+// Tile order: groups of `group_m` tile-rows sweep all tile-columns, column-fastest inside a group when
+// group_m == 1.  The host picks group_m so the operands re-read across the sweep stay in L2.
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int group_m, int& mb, int& nb) {
+  const int per_group = group_m * num_n;
   const int group = t / per_group;
-  const int first_m = group * GROUP_M;
-  const int gsz = min(num_m - first_m, GROUP_M);
+  const int first_m = group * group_m;
+  const int gsz = min(num_m - first_m, group_m);
   const int local = t - group * per_group;
   mb = first_m + local % gsz;
   nb = local / gsz;
@@ -252,7 +253,8 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& p, EpiWarp& ew, ui
 template <int EPI, bool PAIR>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmO, const GemmArgs p, int num_m, int num_n, int nk) {
+                   const __grid_constant__ CUtensorMap tmO, const GemmArgs p, int num_m, int num_n, int nk,
+                   int group_m) {
   using C = GemmCfg<PAIR>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -315,7 +317,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t issued_mask = 0, issued_par = 0;
       for (int t = unit; t < num_tiles; t += units) {
         int mb, nb;
-        tile_coords(t, num_m, num_n, mb, nb);
+        tile_coords(t, num_m, num_n, group_m, mb, nb);
         const int32_t arow = mb * C::kTileM + (int32_t)rank * 128;
         int32_t b0, b1;
         if (PAIR) {
@@ -407,7 +409,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int acc = it & 1;
       const uint32_t accph = (it >> 1) & 1;
       int mb, nb;
-      tile_coords(t, num_m, num_n, mb, nb);
+      tile_coords(t, num_m, num_n, group_m, mb, nb);
       if (!mbar_wait_bounded(&accf[acc], accph, abort_flag, p.err, kDevTimeoutAccFull)) break;
       tc_fence_after();
       const int64_t row0 = (int64_t)mb * C::kTileM + (int64_t)rank * 128 + 32 * q;
@@ -490,7 +492,7 @@ static bool make_tmap_out(CUtensorMap* m, void* base, uint64_t rows, uint64_t co
 
 template <int EPI, bool PAIR>
 static cudaError_t launch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
-                              const GemmArgs& a, int num_m, int num_n, int nk, cudaStream_t st) {
+                              const GemmArgs& a, int num_m, int num_n, int nk, int group_m, cudaStream_t st) {
   using C = GemmCfg<PAIR>;
   auto kern = gemm_i8_kernel<EPI, PAIR>;
   static int grid_cache[64] = {0};
@@ -527,7 +529,7 @@ static cudaError_t launch_epi(const CUtensorMap& ta, const CUtensorMap& tb, cons
   const int64_t tiles = (int64_t)num_m * num_n;
   const int units = (int)(tiles < grid_cache[dev] ? tiles : grid_cache[dev]);
   cfg.gridDim = dim3(PAIR ? 2 * units : units, 1, 1);
-  return cudaLaunchKernelEx(&cfg, kern, ta, tb, to, a, num_m, num_n, nk);
+  return cudaLaunchKernelEx(&cfg, kern, ta, tb, to, a, num_m, num_n, nk, group_m);
 }
 
 // Row-chunk width (bytes) of the staged output and the output element size, by epilogue.
@@ -547,13 +549,24 @@ template <bool PAIR>
 static cudaError_t launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
                                   const GemmArgs& a, int num_n, int nk, cudaStream_t st) {
   const int num_m = (int)((a.M + GemmCfg<PAIR>::kTileM - 1) / GemmCfg<PAIR>::kTileM);
+  // L2 reuse: when the whole weight fits comfortably in L2 (126 MB), sweep tile-columns fastest so the weight
+  // stays resident and every operand is read from DRAM about once; otherwise take groups of tile-rows whose
+  // activation block stays near 40 MB while the weight streams past it.
+  const double weight_bytes = (double)a.N * (double)a.K;
+  int group_m = 1;
+  if (weight_bytes > 96e6) {
+    const double rows_bytes = (double)GemmCfg<PAIR>::kTileM * (double)(a.K > 0 ? a.K : 1);
+    group_m = (int)(40e6 / rows_bytes);
+    if (group_m < 1) group_m = 1;
+    if (group_m > num_m) group_m = num_m;
+  }
   switch (a.epi) {
-    case kEpiLinear: return launch_epi<kEpiLinear, PAIR>(ta, tb, to, a, num_m, num_n, nk, st);
-    case kEpiSwigluPairs: return launch_epi<kEpiSwigluPairs, PAIR>(ta, tb, to, a, num_m, num_n, nk, st);
-    case kEpiSwigluHalves: return launch_epi<kEpiSwigluHalves, PAIR>(ta, tb, to, a, num_m, num_n, nk, st);
-    case kEpiGelu: return launch_epi<kEpiGelu, PAIR>(ta, tb, to, a, num_m, num_n, nk, st);
-    case kEpiGateResid: return launch_epi<kEpiGateResid, PAIR>(ta, tb, to, a, num_m, num_n, nk, st);
-    case kEpiAccI32: return launch_epi<kEpiAccI32, PAIR>(ta, tb, to, a, num_m, num_n, nk, st);
+    case kEpiLinear: return launch_epi<kEpiLinear, PAIR>(ta, tb, to, a, num_m, num_n, nk, group_m, st);
+    case kEpiSwigluPairs: return launch_epi<kEpiSwigluPairs, PAIR>(ta, tb, to, a, num_m, num_n, nk, group_m, st);
+    case kEpiSwigluHalves: return launch_epi<kEpiSwigluHalves, PAIR>(ta, tb, to, a, num_m, num_n, nk, group_m, st);
+    case kEpiGelu: return launch_epi<kEpiGelu, PAIR>(ta, tb, to, a, num_m, num_n, nk, group_m, st);
+    case kEpiGateResid: return launch_epi<kEpiGateResid, PAIR>(ta, tb, to, a, num_m, num_n, nk, group_m, st);
+    case kEpiAccI32: return launch_epi<kEpiAccI32, PAIR>(ta, tb, to, a, num_m, num_n, nk, group_m, st);
     default: return cudaErrorInvalidValue;
   }
 }
