@@ -120,6 +120,23 @@ __global__ void gate_add_kernel(const void* __restrict__ x, const void* __restri
   }
 }
 
+// silu(g) * u over interleaved (g, u) pairs or split halves; silu and the product are each rounded to the
+// tensor kind, as the reference's candle ops on bf16 / f16 tensors round every op (weights.rs:806-816, ops.rs:39-44)
+__global__ void swiglu_kernel(const void* __restrict__ y, void* __restrict__ out, int kind, int64_t rows, int64_t F,
+                              int interleaved) {
+  const int64_t n = rows * F;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / F, j = i % F;
+    const int64_t gi = interleaved ? r * 2 * F + 2 * j : r * 2 * F + j;
+    const int64_t ui = interleaved ? gi + 1 : gi + F;
+    const float g = ld_kind(y, kind, gi), u = ld_kind(y, kind, ui);
+    float s = __fdiv_rn(g, __fadd_rn(1.f, __expf(-g)));
+    if (kind == 2) s = bf16r(s);
+    else if (kind == 1) s = h2f(f2h(s));
+    st_kind(out, kind, i, __fmul_rn(s, u));
+  }
+}
+
 static unsigned grid_for(int64_t work) {
   int64_t b = (work + 255) / 256;
   const int64_t cap = (int64_t)sm_count(0) * 16;
@@ -145,6 +162,12 @@ cudaError_t launch_gate_add(const void* x, const void* y, int kind, const float*
                             int64_t S, int64_t C, cudaStream_t st) {
   if (S * C == 0) return cudaSuccess;
   gate_add_kernel<<<grid_for(S * C), 256, 0, st>>>(x, y, kind, gate, idx, out, S, C);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_swiglu(const void* y, void* out, int kind, int64_t rows, int64_t F, int interleaved, cudaStream_t st) {
+  if (rows * F == 0) return cudaSuccess;
+  swiglu_kernel<<<grid_for(rows * F), 256, 0, st>>>(y, out, kind, rows, F, interleaved);
   return cudaGetLastError();
 }
 

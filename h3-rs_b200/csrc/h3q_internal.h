@@ -33,6 +33,11 @@ struct GemmArgs {
 cudaError_t launch_quant_rows(const void* x, int kind, int8_t* q, float* scale, int64_t M, int64_t K, int order,
                               int* err, cudaStream_t st);
 void fill_f32(float* p, float v, int64_t n, cudaStream_t st);
+// bf16 x [M,K] -> bf16 rotate_activation(x, 256) (K % 256 == 0, K / 256 <= 64)
+cudaError_t launch_rotate_bf16(const uint16_t* x, uint16_t* y, int64_t M, int64_t K, int* err, cudaStream_t st);
+// out = silu(gate) * up with bf16-style re-rounding (weights.rs:806-816, ops.rs:39-44); y [rows, 2F] of kind
+// `kind`, interleaved (g0,u0,g1,u1,...) or split halves (gates then ups); out [rows, F]
+cudaError_t launch_swiglu(const void* y, void* out, int kind, int64_t rows, int64_t F, int interleaved, cudaStream_t st);
 cudaError_t launch_gemm_i8(const int8_t* A, const int8_t* B, const GemmArgs& a, cudaStream_t st);
 int sm_count(int device);
 

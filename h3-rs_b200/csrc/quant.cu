@@ -161,11 +161,13 @@ __device__ __forceinline__ void rotate_inreg(float (&v)[64]) {
 // of the compute; with the swizzle each thread's 16-byte reads of its own line are bank-conflict free.
 constexpr int kQStages = 3;
 
-template <int ORDER, typename Tin>
+// ROT_ONLY: write bf16(rotated row) to `ybf` instead of codes and scales (rotate_activation, weights.rs:482-489,
+// for the paths that quantize a pre-rotated activation).
+template <int ORDER, typename Tin, bool ROT_ONLY = false>
 __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__ CUtensorMap tmx,
                                                          int8_t* __restrict__ q, float* __restrict__ scale,
                                                          int64_t M, int K, int box_rows, int boxes_per_row,
-                                                         int* err) {
+                                                         int* err, uint16_t* __restrict__ ybf) {
   extern __shared__ uint8_t qsm_raw[];
   uint8_t* qsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(qsm_raw) + 1023) & ~uintptr_t(1023));
   __shared__ uint64_t full[kQStages];
@@ -274,13 +276,15 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
         for (int i = 0; i < 16; ++i) u[d3][i] = v[16 * d3 + i];
     }
     float m = 0.f;
+    if (!ROT_ONLY) {
 #pragma unroll
-    for (int d3 = 0; d3 < 4; ++d3)
+      for (int d3 = 0; d3 < 4; ++d3)
 #pragma unroll
-      for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(u[d3][i]));
+        for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(u[d3][i]));
+    }
     const unsigned mw = __reduce_max_sync(0xffffffffu, __float_as_uint(m));
     const int slot = it % 3;
-    if ((t & 31) == 0) atomicMax(&s_max[slot], mw);
+    if ((t & 31) == 0 && !ROT_ONLY) atomicMax(&s_max[slot], mw);
     __syncthreads();  // the whole row is read out of `stage` and its max is complete
     if (t == 0) {
       s_max[(it + 1) % 3] = 0u;
@@ -294,6 +298,22 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
     const float mx = ORDER == 0 ? __uint_as_float(s_max[slot]) : __fmul_rn(__uint_as_float(s_max[slot]), 0.0625f);
     const float s = fmaxf(__fdiv_rn(mx, 127.f), 1e-30f);
     const float inv = ORDER == 0 ? __fdiv_rn(1.f, s) : __fmul_rn(__fdiv_rn(1.f, s), 0.0625f);
+    if (ROT_ONLY) {
+      if (owner) {
+        uint16_t* dst = ybf + row * (int64_t)K + (t >> 2) * 256 + 8 * j;
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+          const int d3 = h >> 1, i0 = 8 * (h & 1);
+          uint4 o;
+          o.x = pack_bf2(__fmul_rn(u[d3][i0], 0.0625f), __fmul_rn(u[d3][i0 + 1], 0.0625f));
+          o.y = pack_bf2(__fmul_rn(u[d3][i0 + 2], 0.0625f), __fmul_rn(u[d3][i0 + 3], 0.0625f));
+          o.z = pack_bf2(__fmul_rn(u[d3][i0 + 4], 0.0625f), __fmul_rn(u[d3][i0 + 5], 0.0625f));
+          o.w = pack_bf2(__fmul_rn(u[d3][i0 + 6], 0.0625f), __fmul_rn(u[d3][i0 + 7], 0.0625f));
+          *reinterpret_cast<uint4*>(dst + 64 * d3 + 32 * (h & 1)) = o;
+        }
+      }
+      continue;
+    }
     if (t == 0) scale[row] = s;
     if (owner) {
       const f2 inv2 = pk(inv, inv), rnd2 = pk(12582912.0f, 12582912.0f);
@@ -382,8 +402,9 @@ static PFN_cuTensorMapEncodeTiled_v12000 q_encode_fn() {
   return fn;
 }
 
-template <int ORDER, typename Tin>
-static cudaError_t launch_rows(const void* x, int8_t* q, float* scale, int64_t M, int K, int* err, cudaStream_t st) {
+template <int ORDER, typename Tin, bool ROT_ONLY = false>
+static cudaError_t launch_rows(const void* x, int8_t* q, float* scale, int64_t M, int K, int* err, cudaStream_t st,
+                               uint16_t* ybf = nullptr) {
   constexpr int ES = sizeof(Tin);
   const int G = K / 256;
   const int threads = ((4 * G + 31) / 32) * 32;
@@ -400,7 +421,7 @@ static cudaError_t launch_rows(const void* x, int8_t* q, float* scale, int64_t M
   if (!fn) return cudaErrorInvalidValue;
   const size_t stage_bytes = ((size_t)K * ES + 1023) / 1024 * 1024;
   const size_t smem = 1024 + kQStages * stage_bytes;
-  auto kern = quant_rows_kernel<ORDER, Tin>;
+  auto kern = quant_rows_kernel<ORDER, Tin, ROT_ONLY>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   int dev = 0, per_sm = 0;
@@ -426,7 +447,8 @@ static cudaError_t launch_rows(const void* x, int8_t* q, float* scale, int64_t M
            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
     const unsigned grid = (unsigned)(mc < want ? mc : want);
-    kern<<<grid, threads, smem, st>>>(m, q + r0 * (int64_t)K, scale + r0, mc, K, box_rows, boxes, err);
+    kern<<<grid, threads, smem, st>>>(m, ROT_ONLY ? q : q + r0 * (int64_t)K, ROT_ONLY ? scale : scale + r0, mc, K,
+                                      box_rows, boxes, err, ROT_ONLY ? ybf + r0 * (int64_t)K : nullptr);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
@@ -455,6 +477,11 @@ cudaError_t launch_quant_rows(const void* x, int kind, int8_t* q, float* scale, 
   if (order == 1) { H3Q_Q(1) }
   H3Q_Q(0)
 #undef H3Q_Q
+}
+
+cudaError_t launch_rotate_bf16(const uint16_t* x, uint16_t* y, int64_t M, int64_t K, int* err, cudaStream_t st) {
+  if (M == 0 || K == 0) return cudaSuccess;
+  return launch_rows<2, __nv_bfloat16, true>(x, nullptr, nullptr, M, (int)K, err, st, y);
 }
 
 __global__ void fill_f32_kernel(float* p, float v, int64_t n) {

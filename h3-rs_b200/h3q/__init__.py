@@ -18,6 +18,25 @@ EPI_LINEAR, EPI_SWIGLU_PAIRS, EPI_SWIGLU_HALVES, EPI_GELU_TANH, EPI_GATE_RESID, 
 
 _vp, _i64, _int, _sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_size_t
 
+class QLinearDesc(ctypes.Structure):
+    """h3q_qlinear: an int8 layer as weights.rs's QLinear holds it."""
+    _fields_ = [("format", ctypes.c_int), ("convrot", ctypes.c_int), ("interleaved", ctypes.c_int),
+                ("n_loras", ctypes.c_int), ("out_features", ctypes.c_int64), ("in_features", ctypes.c_int64),
+                ("weight", ctypes.c_void_p), ("scale", ctypes.c_void_p), ("scale_numel", ctypes.c_int64),
+                ("bias", ctypes.c_void_p)]
+
+
+class Switches(ctypes.Structure):
+    """h3q_switches: H3_INT8, H3_GEMM, H3_ROT, H3_FUSED_ROT as explicit flags."""
+    _fields_ = [("int8", ctypes.c_int), ("gemm_fused", ctypes.c_int), ("rot_fused", ctypes.c_int),
+                ("fused_rot_linear", ctypes.c_int)]
+
+
+FMT_DENSE, FMT_INT8, FMT_NVFP4 = 0, 1, 2
+PATH_GEMM_S8, PATH_INT8_LINEAR, PATH_ROTATE_FUSED, PATH_ROTATE_SEPARATE, PATH_SWIGLU_FUSED, PATH_SWIGLU_AFTER = (
+    1, 2, 4, 8, 16, 32)
+
+
 # name -> (restype, argtypes) of every symbol include/h3q.h declares
 SIGNATURES = {
     "h3q_last_error": (ctypes.c_char_p, []),
@@ -38,6 +57,11 @@ SIGNATURES = {
     "h3q_dequant_nvfp4": (_int, [_vp, _vp, _vp, _vp, _int, _i64, _i64, _vp]),
     "h3q_gate_add": (_int, [_vp, _vp, _int, _vp, _vp, _vp, _i64, _i64, _vp]),
     "h3q_gemm_s8_static": (_int, [_vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _int, _int, _vp]),
+    "h3q_default_switches": (Switches, []),
+    "h3q_qlinear_plan": (_int, [ctypes.POINTER(QLinearDesc), _int, _i64, _int, ctypes.POINTER(Switches)]),
+    "h3q_qlinear_workspace_size": (_sz, [ctypes.POINTER(QLinearDesc), _int, _i64, _int, ctypes.POINTER(Switches)]),
+    "h3q_qlinear_forward": (_int, [ctypes.POINTER(QLinearDesc), _vp, _int, _i64, _int, _vp, _vp, _sz,
+                                   ctypes.POINTER(Switches), _vp]),
 }
 
 
@@ -231,3 +255,45 @@ def gate_add(x, y, gate, idx):
     out = torch.empty_like(x)
     check(lib().h3q_gate_add(_p(x), _p(y), _kind(x.dtype), _p(gate), _p(idx), _p(out), S, C, _stream(x.device)))
     return out
+
+
+def default_switches() -> Switches:
+    return lib().h3q_default_switches()
+
+
+class QLinear:
+    """weights.rs QLinear for an int8 layer: forward_raw / run and run_swiglu through h3q_qlinear_forward."""
+
+    def __init__(self, weight, scale, bias=None, convrot: int = 256, interleaved: bool = False, n_loras: int = 0,
+                 fmt: int = FMT_INT8):
+        import torch
+        self.weight = weight
+        self.scale = scale.to(torch.float32).reshape(-1).contiguous()
+        self.bias = None if bias is None else bias.to(torch.float32).contiguous()
+        self.desc = QLinearDesc(fmt, convrot, int(interleaved), n_loras, weight.shape[0], weight.shape[1],
+                                weight.data_ptr(), self.scale.data_ptr(), self.scale.numel(),
+                                None if self.bias is None else self.bias.data_ptr())
+
+    def plan(self, x_kind: int, swiglu: bool = False, switches: Switches | None = None) -> int:
+        sw = switches or default_switches()
+        return lib().h3q_qlinear_plan(ctypes.byref(self.desc), x_kind, self.desc.in_features, int(swiglu),
+                                      ctypes.byref(sw))
+
+    def forward(self, x, swiglu: bool = False, switches: Switches | None = None):
+        import torch
+        sw = switches or default_switches()
+        _cuda(x)
+        rows = x.shape[0]
+        kind = _kind(x.dtype)
+        n = self.desc.out_features // 2 if swiglu else self.desc.out_features
+        out = torch.empty((rows, n), dtype=x.dtype, device=x.device)
+        need = lib().h3q_qlinear_workspace_size(ctypes.byref(self.desc), kind, rows, int(swiglu), ctypes.byref(sw))
+        ws = torch.empty(max(need, 1), dtype=torch.uint8, device=x.device)
+        check(lib().h3q_qlinear_forward(ctypes.byref(self.desc), _p(x), kind, rows, int(swiglu), _p(out), _p(ws),
+                                        ws.numel(), ctypes.byref(sw), _stream(x.device)))
+        return out
+
+    run = forward
+
+    def run_swiglu(self, x, switches: Switches | None = None):
+        return self.forward(x, swiglu=True, switches=switches)

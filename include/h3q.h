@@ -123,6 +123,60 @@ h3q_status h3q_dequant_nvfp4(const uint8_t* q, const uint8_t* block_scale, const
 h3q_status h3q_gate_add(const void* x, const void* y, int kind, const float* gate, const uint32_t* idx, void* out,
                         int64_t s, int64_t c, void* stream);
 
+/* ---------------------------------------------------------------------------------------------------------
+ * QLinear: the layer-level dispatch of weights.rs (QLinear::prepare / run / run_swiglu / try_gemm_s8 /
+ * apply_int8, weights.rs:833-947) over the entry points above.  The reference reads its switches from the
+ * environment once (H3_INT8 weights.rs:821, H3_GEMM :891, H3_ROT :899, H3_FUSED_ROT kernels.rs:1083); here they
+ * are an explicit struct, defaults = the reference's defaults with no variable set. */
+enum { H3Q_FMT_DENSE = 0, H3Q_FMT_INT8 = 1, H3Q_FMT_NVFP4 = 2 }; /* QFormat (weights.rs:389-397) */
+
+typedef struct {
+  int format;             /* H3Q_FMT_* */
+  int convrot;            /* ConvRot group size (QFormat::Int8 { convrot }), 0 = none */
+  int interleaved;        /* rows of the weight interleave (gate, up) pairs (QLinear::interleaved) */
+  int n_loras;            /* attached LoRA deltas (the runtime LoRA path is not part of this library) */
+  int64_t out_features, in_features;
+  const int8_t* weight;   /* int8 [out_features, in_features] */
+  const float* scale;     /* f32 [out_features] or scalar */
+  int64_t scale_numel;
+  const float* bias;      /* f32 [out_features] or NULL */
+} h3q_qlinear;
+
+typedef struct {
+  int int8;               /* H3_INT8 != "0": int8 weights run on int8 tensor cores (default 1) */
+  int gemm_fused;         /* H3_GEMM != "cublaslt": the fused gemm_s8 path (default 1) */
+  int rot_fused;          /* H3_ROT != "gemm": ConvRot fused into gemm_s8's quantizer (default 1) */
+  int fused_rot_linear;   /* H3_FUSED_ROT == "1": ConvRot fused into int8_linear_ex's quantizer (default 0) */
+} h3q_switches;
+
+/* Dispatch decision of h3q_qlinear_forward (bit flags). */
+enum {
+  H3Q_PATH_GEMM_S8 = 1,          /* attn8::gemm_s8 (try_gemm_s8 applied) */
+  H3Q_PATH_INT8_LINEAR = 2,      /* kernels::int8_linear_ex (the cuBLASLt-path semantics) */
+  H3Q_PATH_ROTATE_FUSED = 4,     /* ConvRot inside the quantizer */
+  H3Q_PATH_ROTATE_SEPARATE = 8,  /* rotate_activation first (bf16), then an unrotated quantizer */
+  H3Q_PATH_SWIGLU_FUSED = 16,    /* SwiGLU in the GEMM epilogue */
+  H3Q_PATH_SWIGLU_AFTER = 32     /* SwiGLU as a separate pass over the linear output */
+};
+
+/* The reference's defaults (no environment variable set). */
+h3q_switches h3q_default_switches(void);
+
+/* Which path h3q_qlinear_forward takes for this layer, an activation of kind x_kind and swiglu (0 = run,
+ * 1 = run_swiglu); H3Q_PATH_* flags, or a negative h3q_status when the layer is not served here (dense / NVFP4
+ * layers, int8 disabled, LoRA deltas on a path that would need them).  Host logic only, no device work. */
+int h3q_qlinear_plan(const h3q_qlinear* layer, int x_kind, int64_t in_width, int swiglu, const h3q_switches* sw);
+
+/* Workspace bytes h3q_qlinear_forward needs for `rows` activation rows. */
+size_t h3q_qlinear_workspace_size(const h3q_qlinear* layer, int x_kind, int64_t rows, int swiglu,
+                                  const h3q_switches* sw);
+
+/* QLinear::forward_raw / run (swiglu = 0) and run_swiglu (swiglu = 1) for an int8 layer: x [rows, in_features]
+ * of kind x_kind -> out [rows, out_features] (or [rows, out_features / 2] with swiglu) in the activation kind. */
+h3q_status h3q_qlinear_forward(const h3q_qlinear* layer, const void* x, int x_kind, int64_t rows, int swiglu,
+                               void* out, void* workspace, size_t workspace_bytes, const h3q_switches* sw,
+                               void* stream);
+
 /* h3q_gemm_s8 for callers that cannot allocate device memory (no counterpart in the reference).  Some callers
  * cannot call cudaMalloc: a plugin inside a host that has already reserved the GPU's whole memory for its own
  * pool, or code where cudaMalloc's implicit synchronisation or failure under memory pressure is not acceptable.

@@ -366,6 +366,32 @@ H3O_API int h3o_quant_rows(const void* x, int kind, int8_t* q, float* scale, int
     return 0;
 }
 
+/* rotate_activation(x, 256) on bf16 rows, computed in the quant_rows_i8_rot2 butterfly order and rounded to
+ * bf16 (weights.rs:482-489; the reference runs it as a bf16 matmul, whose accumulation order is unpinned) */
+H3O_API int h3o_rotate_bf16(const uint16_t* x, uint16_t* out, int64_t M, int64_t K) {
+    if (K % 256 != 0) return -1;
+    float v[256];
+    for (int64_t r = 0; r < M; ++r)
+        for (int64_t g = 0; g < K / 256; ++g) {
+            for (int i = 0; i < 256; ++i) v[i] = bf2f(x[r * K + g * 256 + i]);
+            rot2_group(v);
+            for (int i = 0; i < 256; ++i) out[r * K + g * 256 + i] = f2bf(v[i]);
+        }
+    return 0;
+}
+
+/* swiglu_interleaved (weights.rs:806-816) / ops::swiglu (ops.rs:39-44) on bf16: silu(g) rounded, times u */
+H3O_API void h3o_swiglu_bf16(const uint16_t* y, uint16_t* out, int64_t rows, int64_t F, int interleaved) {
+    for (int64_t r = 0; r < rows; ++r)
+        for (int64_t j = 0; j < F; ++j) {
+            int64_t gi = interleaved ? r * 2 * F + 2 * j : r * 2 * F + j;
+            int64_t ui = interleaved ? gi + 1 : gi + F;
+            float g = bf2f(y[gi]), u = bf2f(y[ui]);
+            float s = bf16r(g / (1.f + expf(-g)));
+            out[r * F + j] = f2bf(s * u);
+        }
+}
+
 /* ---------------------------------------------------------------- int8 GEMM core and epilogues */
 
 /* acc[m,n] = sum_k A[m,k] * B[n,k] (int32; attn8.rs:258-318 main loop, kernels.rs:1026-1044 cuBLASLt IMMA) */

@@ -137,6 +137,24 @@ def reference_quant_mode(kind: int, K: int, rotate: bool) -> int:
     return QUANT_ROT if rotate else QUANT_PLAIN
 
 
+def rotate_bf16(x_bf16: np.ndarray) -> np.ndarray:
+    """rotate_activation(x, 256) on bf16 rows (weights.rs:482-489) in the rot2 butterfly order, bf16 bits out."""
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
+    out = np.empty_like(x)
+    if lib().h3o_rotate_bf16(_p(x), _p(out), c_i64(x.shape[0]), c_i64(x.shape[1])) != 0:
+        raise ValueError("ConvRot group 256 does not divide K")
+    return out
+
+
+def swiglu_bf16(y_bf16: np.ndarray, interleaved: bool) -> np.ndarray:
+    """swiglu_interleaved (weights.rs:806-816) / ops::swiglu (ops.rs:39-44) on bf16 bits."""
+    y = np.ascontiguousarray(y_bf16, dtype=np.uint16)
+    rows, n = y.shape
+    out = np.empty((rows, n // 2), dtype=np.uint16)
+    lib().h3o_swiglu_bf16(_p(y), _p(out), c_i64(rows), c_i64(n // 2), c_int(1 if interleaved else 0))
+    return out
+
+
 def gemm_s8_acc(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     """int32 accumulators sum_k a[m,k] b[n,k] (exact)."""
     a = np.ascontiguousarray(a, dtype=np.int8)
