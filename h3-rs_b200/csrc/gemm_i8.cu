@@ -19,6 +19,7 @@
 #include <cuda_runtime.h>
 #include "ptx.cuh"
 #include "h3q_internal.h"
+#include "gemm_common.cuh"
 
 namespace h3q {
 
@@ -26,8 +27,6 @@ namespace {
 constexpr int BK = 128;                       // K bytes per pipeline stage (one 128-byte swizzle row)
 constexpr int THREADS = 192;
 constexpr uint32_t TMEM_COLS = 512;           // two 256-column int32 accumulators
-constexpr int EPI_BUF = 4096;                 // one staging buffer: 32 rows x up to 128 bytes
-constexpr int EPI_SMEM = 4 * 2 * EPI_BUF;     // 4 epilogue warps, double buffered
 }  // namespace
 
 // Compile-time shape of the two kernel variants.  PAIR: a CTA pair (cluster of 2) computes a 256 x 256 tile with
@@ -45,81 +44,10 @@ struct GemmCfg {
   static constexpr size_t kSmem = 1024 + (size_t)kStages * kStageBytes + EPI_SMEM + 256;
 };
 
-// Tile order: groups of `group_m` tile-rows sweep all tile-columns, column-fastest inside a group when
-// group_m == 1.  The host picks group_m so the operands re-read across the sweep stay in L2.
-__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int group_m, int& mb, int& nb) {
-  const int per_group = group_m * num_n;
-  const int group = t / per_group;
-  const int first_m = group * group_m;
-  const int gsz = min(num_m - first_m, group_m);
-  const int local = t - group * per_group;
-  mb = first_m + local % gsz;
-  nb = local / gsz;
-}
-
-__device__ __forceinline__ int clamp32(int64_t v) { return v <= 0 ? 0 : (v >= 32 ? 32 : (int)v); }
-
-// 32 consecutive f32 values starting at p[col0] (only `valid` of them exist); broadcast reads.
-__device__ __forceinline__ void load_vec32(const float* p, int64_t col0, int valid, bool aligned, float (&o)[32]) {
-  if (valid == 32 && aligned) {
-    const float4* q = reinterpret_cast<const float4*>(p + col0);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float4 f = __ldg(q + i);
-      o[4 * i] = f.x; o[4 * i + 1] = f.y; o[4 * i + 2] = f.z; o[4 * i + 3] = f.w;
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) o[i] = i < valid ? __ldg(p + col0 + i) : 0.f;
-  }
-}
-
-// 32 f32 values -> packed words of the output kind (0 f32, 1 f16, 2 bf16); returns the row-chunk width in bytes.
-__device__ __forceinline__ int pack_out(const float (&v)[32], int kind, uint32_t (&w)[32]) {
-  if (kind == 0) {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(v[i]);
-    return 128;
-  }
-#pragma unroll
-  for (int i = 0; i < 16; ++i)
-    w[i] = kind == 2 ? pack_bf2(v[2 * i], v[2 * i + 1])
-                     : ((uint32_t)f2h(v[2 * i]) | ((uint32_t)f2h(v[2 * i + 1]) << 16));
-  return 64;
-}
-
 __device__ __forceinline__ float gelu_tanh(float y) {
   const float c = 0.7978845608028654f;  // sqrt(2/pi)
   return 0.5f * y * (1.f + tanhf(c * (y + 0.044715f * y * y * y)));
 }
-
-// One warp's TMA-store epilogue: each lane stages its row of a 32-row box into a swizzled shared-memory buffer
-// (the TMA swizzle of the box's row width W, which also makes the 16-byte writes bank-conflict free), then lane
-// 0 stores the box.  Two buffers alternate; a buffer is rewritten only after its previous store has read it.
-struct EpiWarp {
-  const CUtensorMap* map;
-  uint8_t* buf;  // 2 * EPI_BUF bytes, 1024-aligned
-  int sel;
-  int lane;
-
-  __device__ __forceinline__ void store(const uint32_t (&w)[32], int W, int32_t x, int32_t y, bool do_store) {
-    if (lane == 0) bulk_wait_read<1>();
-    __syncwarp();
-    uint8_t* b = buf + sel * EPI_BUF + lane * W;
-    const int sw = W == 128 ? (lane & 7) : (W == 64 ? ((lane >> 1) & 3) : ((lane >> 2) & 1));
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-      if (i < W / 16)
-        *reinterpret_cast<uint4*>(b + ((i ^ sw) << 4)) = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0 && do_store) {
-      tma_store_2d(map, buf + sel * EPI_BUF, x, y);
-      bulk_commit();
-    }
-    sel ^= 1;
-  }
-};
 
 // Epilogue of one accumulator tile for the 32 output rows of this warp (TMEM lanes 32q..32q+31 of `tacc`).
 // `row` is this lane's output row, `row0` the warp's first row, `nb` the tile column.
@@ -436,32 +364,6 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 // ---------------------------------------------------------------------------------------------- host side
 
-static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
-  }
-  return fn;
-}
-
-// int8 [rows, cols] row-major, box = 128 bytes of K x box_rows rows, 128-byte swizzle, zero fill outside.
-static bool make_tmap_i8(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
-  auto fn = encode_fn();
-  if (!fn) return false;
-  cuuint64_t dims[2] = {cols, rows};
-  cuuint64_t strides[1] = {cols};
-  cuuint32_t box[2] = {BK, box_rows};
-  cuuint32_t es[2] = {1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, es,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
-}
-
 int sm_count(int device) {
   static int cache[64] = {0};
   if (device < 0 || device >= 64) return 148;
@@ -471,23 +373,6 @@ int sm_count(int device) {
     cache[device] = v > 0 ? v : 148;
   }
   return cache[device];
-}
-
-// Output tensor map for the epilogue's TMA stores: [M, nout] row-major, box = (W / es) columns x 32 rows,
-// swizzle matching the box's row width W.
-static bool make_tmap_out(CUtensorMap* m, void* base, uint64_t rows, uint64_t cols, int es, int W) {
-  auto fn = encode_fn();
-  if (!fn) return false;
-  cuuint64_t dims[2] = {cols, rows};
-  cuuint64_t strides[1] = {cols * (uint64_t)es};
-  cuuint32_t box[2] = {(cuuint32_t)(W / es), 32};
-  cuuint32_t estr[2] = {1, 1};
-  const CUtensorMapDataType dt =
-      es == 4 ? CU_TENSOR_MAP_DATA_TYPE_UINT32 : CU_TENSOR_MAP_DATA_TYPE_UINT16;
-  const CUtensorMapSwizzle sw =
-      W == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : (W == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
-  return fn(m, dt, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
-            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 template <int EPI, bool PAIR>
@@ -549,14 +434,15 @@ template <bool PAIR>
 static cudaError_t launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
                                   const GemmArgs& a, int num_n, int nk, cudaStream_t st) {
   const int num_m = (int)((a.M + GemmCfg<PAIR>::kTileM - 1) / GemmCfg<PAIR>::kTileM);
-  // L2 reuse: when the whole weight fits comfortably in L2 (126 MB), sweep tile-columns fastest so the weight
-  // stays resident and every operand is read from DRAM about once; otherwise take groups of tile-rows whose
-  // activation block stays near 40 MB while the weight streams past it.
+  // L2 reuse (measured with ncu DRAM counters at the DiT shapes): a weight of up to ~32 MB stays resident while
+  // tile-columns sweep fastest (group_m = 1), so both operands are read from DRAM about once.  A larger weight
+  // does not stay resident; instead groups of tile-rows whose activation block is ~24 MB stay in L2 while the
+  // weight streams past them (weight re-read num_m / group_m times, activations once).
   const double weight_bytes = (double)a.N * (double)a.K;
   int group_m = 1;
-  if (weight_bytes > 96e6) {
+  if (weight_bytes > 32e6) {
     const double rows_bytes = (double)GemmCfg<PAIR>::kTileM * (double)(a.K > 0 ? a.K : 1);
-    group_m = (int)(40e6 / rows_bytes);
+    group_m = (int)(24e6 / rows_bytes);
     if (group_m < 1) group_m = 1;
     if (group_m > num_m) group_m = num_m;
   }
