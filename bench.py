@@ -168,6 +168,41 @@ def config_block(n_gpus: int) -> dict:
 
 # --------------------------------------------------------------------------------------------- our arm
 
+def nvfp4_c3(dev, peaks: dict, reps: int = 10) -> dict:
+    """the text encoder's NVFP4+AWQ linears at 512 prompt tokens (5120 -> 25600 and
+    25600 -> 5120), fused fp4-decode + bf16 tcgen05 GEMM; CUDA-event time per layer and TFLOP/s against the measured
+    bf16 peak (the tensor cores run bf16 here: the activations stay bf16)."""
+    import torch
+    import h3q
+    g = torch.Generator(device=dev).manual_seed(99)
+    pool = torch.tensor([(e << 3) | m for e in (6, 7, 8) for m in range(8)] + [9 << 3], dtype=torch.uint8, device=dev)
+    res = []
+    for K, N in ((5120, 25600), (25600, 5120)):
+        M = 512
+        x = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
+        q = torch.randint(0, 256, (N, K // 2), generator=g, device=dev, dtype=torch.uint8)
+        nbytes = ((N + 127) // 128) * ((K // 16 + 3) // 4) * 512
+        bs = pool[torch.randint(0, pool.numel(), (nbytes,), generator=g, device=dev)]
+        gs = torch.tensor([1.0 / 448.0], device=dev)
+        pqs = (torch.rand(K, generator=g, device=dev) * 1.5 + 0.5).to(torch.bfloat16)
+        for _ in range(3):
+            h3q.nvfp4_linear(x, q, bs, gs, pqs)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            h3q.nvfp4_linear(x, q, bs, gs, pqs)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+        wbytes = N * K // 2 + nbytes
+        res.append({"linear": f"{K}->{N}", "M": M, "ms": round(ms, 4), "tflops": round(tf, 1),
+                    "frac_of_bf16_peak": round(tf / peaks["bf16_tflops"], 3),
+                    "weight_gbs": round(wbytes / (ms * 1e-3) / 1e9, 1)})
+    return {"workload": "BASELINE c3: NVFP4+AWQ text-encoder linears, M=512", "layers": res,
+            "note": "time per call includes the AWQ pre-pass and, for 25600->5120, the split-K reduction"}
+
+
 def run_profile_case(args) -> None:
     """One fc1-shaped linear at 4096 tokens (A 21 MB, W 71 MB, out 113 MB: more than L2 in total, a few hundred
     MB on the device): warmup + steps launches of the quantizer and the GEMM, for ncu --set full captures."""
@@ -340,6 +375,8 @@ def main() -> None:
                "d2h_bytes_per_step": int(sum(h.numel() * 2 for h in host_o)), "ms_per_step": e_ms,
                "path": "h3q_gemm_s8 (C ABI) with pinned host input/output, copies inside the timed region"}
 
+    nv = nvfp4_c3(dev, load_peaks()) if rank == 0 else None
+
     cb = None
     if rank == 0 and ws_n == 1 and not args.no_cpu_baseline:
         cb = cpu_baseline()
@@ -366,6 +403,7 @@ def main() -> None:
                            "frac": q_achieved / peaks["hbm_gbs"], "avg_launch_ms": quant_avg_ms,
                            "bytes_per_launch": quant_bytes_launch},
         "per_linear": per_linear,
+        "nvfp4_c3": nv,
         "cpu_baseline": cb, "e2e": e2e, "clocks": clk.summary(),
         "gpu_launches": 2 * launches,
     }

@@ -112,6 +112,7 @@ h3q_status gemm_core(const int8_t* a, const float* xs, const int8_t* w, const fl
 namespace h3q {
 // Lets other translation units of the library report an error through h3q_last_error().
 void set_last_error(const char* msg) { g_last_error = msg; }
+int* error_word_current() { return error_word(); }
 }  // namespace h3q
 
 extern "C" {

@@ -40,5 +40,7 @@ cudaError_t launch_rotate_bf16(const uint16_t* x, uint16_t* y, int64_t M, int64_
 cudaError_t launch_swiglu(const void* y, void* out, int kind, int64_t rows, int64_t F, int interleaved, cudaStream_t st);
 cudaError_t launch_gemm_i8(const int8_t* A, const int8_t* B, const GemmArgs& a, cudaStream_t st);
 int sm_count(int device);
+// the per-device error word kernels latch bounded-wait time-outs into (allocated once per device)
+int* error_word_current();
 
 }  // namespace h3q

@@ -1,0 +1,522 @@
+// nvfp4_gemm.cu -- the NVFP4 (+AWQ) linear of h3-rs's text encoder, fused: fp4 weights are decoded to bf16
+// inside the GEMM and multiplied on the 5th-generation tensor cores (tcgen05 kind::f16, f32 accumulators).
+//
+// Reference (weights.rs:612-635 with dequant_nvfp4, kernels.rs:65-81):
+//   x2 = bf16(x * bf16(pre_quant_scale))                    (AWQ, weights.rs:617-620)
+//   W  = bf16(E2M1[nibble] * e4m3(block scale) * global)    (even column = high nibble, 128x4 swizzled scales)
+//   y  = bf16(x2 @ W^T)  (+ bf16(bias), added in bf16)      (weights.rs:632-635)
+// The reference materialises W in HBM (2 bytes per weight) for every call and runs a bf16 cuBLAS GEMM.  Here the
+// packed weight (0.56 bytes per weight with its scales) is read once per tile and decoded in shared memory.
+//
+// One 2-CTA cluster computes a 256 x 256 output tile (tcgen05.mma.cta_group::2, M=256, N=256, K=16).  Per CTA:
+//   warp 0      TMA: bf16 activation tile (128 rows x 64, 128-byte swizzle), packed weight tile (128 rows x
+//               32 bytes) and the 512-byte block-scale atom of those 128 rows x 4 blocks, into a 5-stage ring;
+//   warp 1      TMEM allocation; in the leader CTA, one thread issues the pair MMAs;
+//   warps 2-5   epilogue (TMEM -> bf16 or f32 split-K partials -> TMA store);
+//   warps 6-9   decoders: thread r turns weight row r's 64 codes of the stage into bf16, written straight into
+//               the 128-byte-swizzled K-major layout the MMA reads.  Decode per pair of codes: cvt e2m1x2 ->
+//               f16x2, f16x2 multiply by the e4m3 scale (exact: at most 5 significant bits), widen to f32,
+//               multiply by the global scale, round to bf16 -- the same rounding as the reference's dequant.
+// Split-K (units = tiles x splits) keeps all SMs busy for narrow outputs; partials are summed in a fixed order.
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include "../../include/h3q.h"
+#include "ptx.cuh"
+#include "h3q_internal.h"
+#include "gemm_common.cuh"
+
+namespace h3q {
+void set_last_error(const char* msg);
+
+namespace {
+constexpr int NF_STAGES = 5;
+constexpr int NF_THREADS = 320;
+constexpr int NF_A = 128 * 128;   // bf16 activation tile: 128 rows x 64 elements
+constexpr int NF_BD = 128 * 128;  // decoded bf16 weight tile
+constexpr int NF_BR = 128 * 32;   // packed fp4 weight tile: 128 rows x 64 codes
+constexpr int NF_SC = 512;        // one 128-row x 4-block scale atom
+constexpr uint32_t NF_TX = NF_A + NF_BR + NF_SC;
+constexpr size_t NF_SMEM = 1024 + (size_t)NF_STAGES * (NF_A + NF_BD + NF_BR + NF_SC) + EPI_SMEM + 512;
+constexpr uint32_t NF_IDESC = idesc_bf16(256, 256);
+}  // namespace
+
+struct Nvfp4Args {
+  int64_t M, N, K;
+  int64_t Mp;             // rows per split-K partial: M rounded up to a tile, so a tile's rows past M stay inside
+  const uint8_t* bscale;  // swizzled e4m3 block scales
+  const float* gscale;    // device scalar
+  const float* bias;      // f32 [N] or null (only when splits == 1)
+  int splits;
+  int* err;
+};
+
+// four bytes of packed e2m1 pairs -> four f16x2 (per byte: low nibble -> low half, high nibble -> high half)
+__device__ __forceinline__ void cvt_e2m1x8_f16x2(uint32_t w, uint32_t (&d)[4]) {
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\tmov.b32 {b0, b1, b2, b3}, %4;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\tcvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
+      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\tcvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(w));
+}
+__device__ __forceinline__ uint32_t cvt_e4m3x2_f16x2(uint16_t two_bytes) {
+  uint32_t d;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(d) : "h"(two_bytes));
+  return d;
+}
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+// bf16x2 word with `lo` in the low half (RNE, like f2bf for finite values)
+__device__ __forceinline__ uint32_t cvt_bf16x2(float lo, float hi) {
+  uint32_t d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
+// Decode 8 packed bytes (16 codes of one 16-element block, even code in each byte's high nibble) with scale
+// `sc2` (f16x2 of the block's e4m3 scale) and global scale g into 8 bf16x2 words in column order.
+__device__ __forceinline__ void decode_block(uint32_t w0, uint32_t w1, uint32_t sc2, float g, uint32_t (&o)[8]) {
+  const uint32_t w[2] = {w0, w1};
+#pragma unroll
+  for (int wi = 0; wi < 2; ++wi) {
+    uint32_t d[4];
+    cvt_e2m1x8_f16x2(w[wi], d);
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const uint32_t h = hmul2(d[b], sc2);  // exact: at most 5 significant bits, inside the f16 range
+      const float odd = __half2float(__ushort_as_half((unsigned short)(h & 0xffffu)));   // low nibble
+      const float even = __half2float(__ushort_as_half((unsigned short)(h >> 16)));     // high nibble
+      o[4 * wi + b] = cvt_bf16x2(__fmul_rn(even, g), __fmul_rn(odd, g));
+    }
+  }
+}
+
+__global__ void __launch_bounds__(NF_THREADS, 1)
+    nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ CUtensorMap tmO, const Nvfp4Args p, int num_m, int num_n, int nk) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sBD = sA + NF_STAGES * NF_A;
+  uint8_t* sBR = sBD + NF_STAGES * NF_BD;
+  uint8_t* sSC = sBR + NF_STAGES * NF_BR;
+  uint8_t* sE = sSC + NF_STAGES * NF_SC;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sE + EPI_SMEM);
+  uint64_t* decd = full + NF_STAGES;
+  uint64_t* empty = decd + NF_STAGES;
+  uint64_t* accf = empty + NF_STAGES;
+  uint64_t* acce = accf + 2;
+  uint64_t* mma_done = acce + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NF_STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&decd[s], 8);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&accf[a], 1);
+      mbar_init(&acce[a], 8);
+    }
+    mbar_init(mma_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmO);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, 512);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int splits = p.splits;
+  const int num_units = num_m * num_n * splits;
+  const int unit0 = (int)(blockIdx.x >> 1), units = (int)(gridDim.x >> 1);
+  const int64_t ncb = (p.K / 16 + 3) / 4;  // scale atoms per 128-row group
+
+  auto unit_coords = [&](int u, int& mb, int& nb, int& kb0, int& kb1) {
+    const int tile = u / splits, ks = u % splits;
+    tile_coords(tile, num_m, num_n, num_m, mb, nb);  // both tile-rows of an output column together
+    kb0 = (int)((int64_t)ks * nk / splits);
+    kb1 = (int)((int64_t)(ks + 1) * nk / splits);
+  };
+
+  if (warp == 0) {
+    if (elect_one()) {
+      // ---------------------------------------------------------------- TMA producer (each CTA, own stages)
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_par = 0;
+      for (int u = unit0; u < num_units; u += units) {
+        int mb, nb, kb0, kb1;
+        unit_coords(u, mb, nb, kb0, kb1);
+        const int32_t arow = mb * 256 + (int32_t)rank * 128;
+        const int32_t brow = nb * 256 + (int32_t)rank * 128;
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag, p.err, kDevTimeoutEmpty)) { ok = false; break; }
+          // weight rows past N (the second half of a last 256-wide tile): the codes arrive as zeros from the TMA's
+          // out-of-bounds fill and no scale atom exists to copy; those accumulator columns are never stored
+          const bool brows = brow < p.N;
+          mbar_arrive_expect_tx(&full[stage], brows ? NF_TX : NF_TX - NF_SC);
+          tma_load_2d(sA + stage * NF_A, &tmA, &full[stage], kb * 64, arow);
+          tma_load_2d(sBR + stage * NF_BR, &tmB, &full[stage], kb * 32, brow);
+          if (brows)
+            bulk_load_1d(sSC + stage * NF_SC, p.bscale + ((int64_t)(brow / 128) * ncb + kb) * 512, NF_SC, &full[stage]);
+          issued_mask |= 1u << stage;
+          issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
+          if (++stage == NF_STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+      }
+      for (int s = 0; s < NF_STAGES; ++s)
+        if (issued_mask & (1u << s)) mbar_drain(&full[s], (issued_par >> s) & 1u, p.err, kDevTimeoutDrain);
+    }
+  } else if (warp == 1) {
+    if (leader && elect_one()) {
+      // ---------------------------------------------------------------- MMA issuer (pair leader)
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      for (int u = unit0; u < num_units; u += units, ++it) {
+        int mb, nb, kb0, kb1;
+        unit_coords(u, mb, nb, kb0, kb1);
+        const int acc = it & 1;
+        const uint32_t accph = (it >> 1) & 1;
+        if (!mbar_wait_bounded(&acce[acc], accph ^ 1, abort_flag, p.err, kDevTimeoutAccEmpty)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + acc * 256;
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          // both CTAs' decoders have finished this stage: their activation and weight tiles are in place
+          if (!mbar_wait_bounded(&decd[stage], phase, abort_flag, p.err, kDevTimeoutFull)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t da = smem_desc_k128(smem_u32(sA + stage * NF_A));
+          const uint64_t db = smem_desc_k128(smem_u32(sBD + stage * NF_BD));
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            mma_bf16_pair(d, da + (uint64_t)(k * 2), db + (uint64_t)(k * 2), NF_IDESC, (kb > kb0) || (k > 0));
+          mma_commit_pair(mapa_shared(&empty[stage], 0));
+          mma_commit_pair(mapa_shared(&empty[stage], 1));
+          if (++stage == NF_STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        mma_commit_pair(mapa_shared(&accf[acc], 0));
+        mma_commit_pair(mapa_shared(&accf[acc], 1));
+      }
+      mma_commit_pair(mapa_shared(mma_done, 0));
+      mbar_drain(mma_done, 0, p.err, kDevTimeoutDrain);
+    }
+  } else if (warp >= 6) {
+    // ------------------------------------------------------------------ decoders (both CTAs)
+    const int r = threadIdx.x - 192;  // weight row of the CTA's 128-row half
+    const float g = __ldg(p.gscale);
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int u = unit0; u < num_units; u += units) {
+      int mb, nb, kb0, kb1;
+      unit_coords(u, mb, nb, kb0, kb1);
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait_bounded(&full[stage], phase, abort_flag, p.err, kDevTimeoutFull)) { ok = false; break; }
+        const uint8_t* br = sBR + stage * NF_BR + r * 32;
+        const uint4 q0 = *reinterpret_cast<const uint4*>(br);
+        const uint4 q1 = *reinterpret_cast<const uint4*>(br + 16);
+        const uint32_t sc4 = *reinterpret_cast<const uint32_t*>(sSC + stage * NF_SC + (r % 32) * 16 + (r / 32) * 4);
+        const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+        uint8_t* bd = sBD + stage * NF_BD + r * 128;
+#pragma unroll
+        for (int blk = 0; blk < 4; ++blk) {
+          const uint32_t sb = (sc4 >> (8 * blk)) & 0xffu;
+          const uint32_t sc2 = cvt_e4m3x2_f16x2((uint16_t)(sb | (sb << 8)));
+          uint32_t o[8];
+          decode_block(qw[2 * blk], qw[2 * blk + 1], sc2, g, o);
+          // 16 bf16 = chunks 2*blk and 2*blk+1 of the 128-byte row, 128-byte swizzle
+          *reinterpret_cast<uint4*>(bd + (((2 * blk) ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+          *reinterpret_cast<uint4*>(bd + (((2 * blk + 1) ^ (r & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(&decd[stage], 0));
+        if (++stage == NF_STAGES) { stage = 0; phase ^= 1; }
+      }
+      if (!ok) break;
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue warps 2..5 (both CTAs)
+    const int q = warp & 3;
+    EpiWarp ew{&tmO, sE + (warp - 2) * 2 * EPI_BUF, 0, lane};
+    const bool partial = splits > 1;
+    int it = 0;
+    for (int u = unit0; u < num_units; u += units, ++it) {
+      int mb, nb, kb0, kb1;
+      unit_coords(u, mb, nb, kb0, kb1);
+      const int ks = u % splits;
+      const int acc = it & 1;
+      const uint32_t accph = (it >> 1) & 1;
+      if (!mbar_wait_bounded(&accf[acc], accph, abort_flag, p.err, kDevTimeoutAccFull)) break;
+      tc_fence_after();
+      const int64_t row0 = (int64_t)mb * 256 + (int64_t)rank * 128 + 32 * q;
+      const uint32_t tacc = tmem_base + ((uint32_t)(32 * q) << 16) + acc * 256;
+#pragma unroll 1
+      for (int c = 0; c < 8; ++c) {
+        uint32_t r32[32];
+        __syncwarp();
+        tmem_ld_32x32b_x32(tacc + 32 * c, r32);
+        tmem_wait_ld();
+        const int64_t col0 = (int64_t)nb * 256 + 32 * c;
+        const bool st = row0 < p.M && col0 < p.N;
+        uint32_t o[32];
+        if (partial) {
+          ew.store(r32, 128, (int32_t)col0, (int32_t)(ks * p.Mp + row0), st);
+        } else {
+          float v[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = bf16r(__uint_as_float(r32[i]));  // the bf16 GEMM output
+          if (p.bias) {
+            const int valid = clamp32(p.N - col0);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = __fadd_rn(v[i], i < valid ? bf16r(__ldg(p.bias + col0 + i)) : 0.f);
+          }
+          ew.store(o, pack_out(v, 2, o), (int32_t)col0, (int32_t)row0, st);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(&acce[acc], 0));
+    }
+    if (lane == 0) bulk_wait_all();
+  }
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, 512);
+  }
+}
+
+// x2 = bf16(x * bf16 pre_quant_scale), 8 elements per thread-iteration (weights.rs:617-620)
+__global__ void awq_scale_kernel(const uint16_t* __restrict__ x, const uint16_t* __restrict__ pqs,
+                                 uint16_t* __restrict__ x2, int64_t M, int64_t K) {
+  const int64_t nv = M * K / 8;
+  for (int64_t v = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; v < nv; v += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t k = (v * 8) % K;
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(x) + v);
+    const uint4 s = __ldg(reinterpret_cast<const uint4*>(pqs + k));
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, sw[4] = {s.x, s.y, s.z, s.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      o[i] = pack_bf2(__fmul_rn(__uint_as_float(aw[i] << 16), __uint_as_float(sw[i] << 16)),
+                      __fmul_rn(__uint_as_float(aw[i] & 0xffff0000u), __uint_as_float(sw[i] & 0xffff0000u)));
+    reinterpret_cast<uint4*>(x2)[v] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// out = bf16(bf16(sum_s partial[s]) + bf16(bias)) with the splits summed in order; partial s starts at row s * Mp
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, const float* __restrict__ bias,
+                                     uint16_t* __restrict__ out, int64_t M, int64_t Mp, int64_t N, int splits) {
+  const int64_t n = M * N, stride_s = Mp * N;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    float acc = part[i];
+    for (int s = 1; s < splits; ++s) acc = __fadd_rn(acc, part[(int64_t)s * stride_s + i]);
+    float v = bf16r(acc);
+    if (bias) v = __fadd_rn(v, bf16r(__ldg(bias + i % N)));
+    out[i] = (uint16_t)f2bf(v);
+  }
+}
+
+// Split count that best fills the co-resident pairs (at most 4, at least 8 k-blocks per split).
+static int choose_splits(int tiles, int pairs, int nk) {
+  int best = 1;
+  double best_eff = 0.0;
+  for (int s = 1; s <= 4; ++s) {
+    if (s > 1 && nk / s < 8) break;
+    const int units = tiles * s;
+    const int waves = (units + pairs - 1) / pairs;
+    const double eff = (double)units / ((double)waves * pairs);
+    if (eff > best_eff + 0.02) {
+      best_eff = eff;
+      best = s;
+    }
+  }
+  return best;
+}
+
+static int nvfp4_pairs(int dev) {
+  static int cache[64] = {0};
+  if (dev < 0 || dev >= 64) return 1;
+  if (!cache[dev]) {
+    cudaFuncSetAttribute(nvfp4_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)NF_SMEM);
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cfg.blockDim = dim3(NF_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = NF_SMEM;
+    cfg.gridDim = dim3(2 * (sm_count(dev) / 2), 1, 1);
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, nvfp4_gemm_kernel, &cfg) != cudaSuccess || clusters < 1) clusters = 1;
+    cache[dev] = clusters;
+  }
+  return cache[dev];
+}
+
+static size_t align256(size_t v) { return (v + 255) / 256 * 256; }
+
+struct Nvfp4Plan {
+  int splits;
+  size_t x2_bytes, part_bytes;
+};
+
+static Nvfp4Plan nvfp4_plan(int64_t m, int64_t n, int64_t k, bool awq) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int tiles = (int)(((m + 255) / 256) * ((n + 255) / 256));
+  Nvfp4Plan pl;
+  pl.splits = choose_splits(tiles, nvfp4_pairs(dev), (int)(k / 64));
+  pl.x2_bytes = awq ? align256((size_t)m * k * 2) : 0;
+  pl.part_bytes = pl.splits > 1 ? align256((size_t)pl.splits * ((m + 255) / 256 * 256) * n * 4) : 0;
+  return pl;
+}
+
+}  // namespace h3q
+
+using namespace h3q;
+
+namespace {
+h3q_status nf_fail(h3q_status s, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof buf, fmt, ap);
+  va_end(ap);
+  h3q::set_last_error(buf);
+  return s;
+}
+int* nf_err_word() {
+  // time-outs of this kernel are latched into the same per-device word as the int8 path's
+  return h3q::error_word_current();
+}
+}  // namespace
+
+extern "C" size_t h3q_nvfp4_linear_workspace_size(int64_t m, int64_t n, int64_t k, int has_pre_quant_scale) {
+  if (m <= 0 || n <= 0 || k <= 0) return 0;
+  const Nvfp4Plan pl = nvfp4_plan(m, n, k, has_pre_quant_scale != 0);
+  return pl.x2_bytes + pl.part_bytes;
+}
+
+extern "C" h3q_status h3q_nvfp4_linear(const uint16_t* x, const uint16_t* pre_quant_scale, const uint8_t* q,
+                                       const uint8_t* block_scale, const float* global_scale, const float* bias,
+                                       uint16_t* out, int64_t m, int64_t n, int64_t k, void* workspace,
+                                       size_t workspace_bytes, void* stream) {
+  const char* what = "h3q_nvfp4_linear";
+  if (m < 0 || n < 0 || k < 0) return nf_fail(H3Q_ERR_ARG, "%s: negative shape", what);
+  if (m == 0 || n == 0) return H3Q_OK;
+  if (k % 64 != 0 || n % 128 != 0)
+    return nf_fail(H3Q_ERR_UNSUPPORTED, "%s: this build needs k %% 64 == 0 and n %% 128 == 0 (k %lld, n %lld)", what,
+                   (long long)k, (long long)n);
+  if (!x || !q || !block_scale || !global_scale || !out) return nf_fail(H3Q_ERR_ARG, "%s: null pointer", what);
+  const auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (!al16(x) || !al16(q) || !al16(block_scale) || !al16(out) || (pre_quant_scale && !al16(pre_quant_scale)))
+    return nf_fail(H3Q_ERR_ARG, "%s: tensors must be 16-byte aligned", what);
+  const Nvfp4Plan pl = nvfp4_plan(m, n, k, pre_quant_scale != nullptr);
+  if (workspace_bytes < pl.x2_bytes + pl.part_bytes || (pl.x2_bytes + pl.part_bytes > 0 && !workspace))
+    return nf_fail(H3Q_ERR_WORKSPACE, "%s: workspace of %zu bytes, need %zu", what, workspace_bytes,
+                   pl.x2_bytes + pl.part_bytes);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* wsp = static_cast<uint8_t*>(workspace);
+  const uint16_t* xa = x;
+  if (pre_quant_scale) {
+    uint16_t* x2 = reinterpret_cast<uint16_t*>(wsp);
+    const int64_t nv = m * k / 8;
+    const int64_t blocks = (nv + 255) / 256;
+    awq_scale_kernel<<<(unsigned)(blocks < 148 * 16 ? blocks : 148 * 16), 256, 0, st>>>(x, pre_quant_scale, x2, m, k);
+    xa = x2;
+  }
+  float* part = reinterpret_cast<float*>(wsp + pl.x2_bytes);
+  CUtensorMap ta, tb, to;
+  auto fn = encode_fn();
+  if (!fn) return nf_fail(H3Q_ERR_CUDA, "%s: cuTensorMapEncodeTiled unavailable", what);
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)m};
+    cuuint64_t strides[1] = {(cuuint64_t)k * 2};
+    cuuint32_t box[2] = {64, 128};
+    cuuint32_t es[2] = {1, 1};
+    if (fn(&ta, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<uint16_t*>(xa), dims, strides, box, es,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return nf_fail(H3Q_ERR_CUDA, "%s: activation tensor map", what);
+  }
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)(k / 2), (cuuint64_t)n};
+    cuuint64_t strides[1] = {(cuuint64_t)(k / 2)};
+    cuuint32_t box[2] = {32, 128};
+    cuuint32_t es[2] = {1, 1};
+    if (fn(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(q), dims, strides, box, es,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return nf_fail(H3Q_ERR_CUDA, "%s: weight tensor map", what);
+  }
+  const bool partial = pl.splits > 1;
+  const int64_t mp = (m + 255) / 256 * 256;
+  if (!make_tmap_out(&to, partial ? (void*)part : (void*)out, (uint64_t)(partial ? pl.splits * mp : m), (uint64_t)n,
+                     partial ? 4 : 2, partial ? 128 : 64))
+    return nf_fail(H3Q_ERR_CUDA, "%s: output tensor map", what);
+  Nvfp4Args a{};
+  a.M = m; a.N = n; a.K = k; a.Mp = mp;
+  a.bscale = block_scale; a.gscale = global_scale;
+  a.bias = partial ? nullptr : bias;
+  a.splits = pl.splits;
+  a.err = nf_err_word();
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int num_m = (int)((m + 255) / 256), num_n = (int)((n + 255) / 256);
+  const int units_total = num_m * num_n * pl.splits;
+  const int pairs = nvfp4_pairs(dev);
+  const int u = units_total < pairs ? units_total : pairs;
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.blockDim = dim3(NF_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = NF_SMEM;
+  cfg.gridDim = dim3(2 * u, 1, 1);
+  cfg.stream = st;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, nvfp4_gemm_kernel, ta, tb, to, a, num_m, num_n, (int)(k / 64));
+  if (e == cudaSuccess && partial) {
+    const int64_t blocks = (m * n + 255) / 256;
+    splitk_reduce_kernel<<<(unsigned)(blocks < 148 * 16 ? blocks : 148 * 16), 256, 0, st>>>(part, bias, out, m, mp, n,
+                                                                                         pl.splits);
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) return nf_fail(H3Q_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  return H3Q_OK;
+}

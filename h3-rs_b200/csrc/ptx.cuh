@@ -143,6 +143,14 @@ __device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorM
       "l"(reinterpret_cast<uint64_t>(m)), "r"(bar_cluster), "r"(x), "r"(y)
       : "memory");
 }
+// 1-D bulk copy of `bytes` (multiple of 16, both addresses 16-byte aligned) into shared memory; completes on `bar`.
+__device__ __forceinline__ void bulk_load_1d(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
 // 2-D tiled store of a shared-memory box to global memory (bulk async group of the issuing thread).
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* m, const void* smem_src, int32_t x, int32_t y) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
@@ -216,6 +224,15 @@ __device__ __forceinline__ void mma_i8_pair(uint32_t d_tmem, uint64_t adesc, uin
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// Pair MMA of bf16 operands with f32 accumulation (kind::f16), same operand split as mma_i8_pair.
+__device__ __forceinline__ void mma_bf16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // Arrive once on the barrier at shared::cluster address `bar_cluster` when every pair MMA issued so far by this
 // thread has completed.
 __device__ __forceinline__ void mma_commit_pair(uint32_t bar_cluster) {
@@ -264,6 +281,14 @@ __device__ __forceinline__ uint64_t smem_desc_k128(uint32_t smem_addr) {
   d |= (uint64_t)1 << 46;                        // descriptor version (sm_100)
   d |= (uint64_t)2 << 61;                        // layout: 128-byte swizzle
   return d;
+}
+
+// Instruction descriptor for kind::f16 with bf16 A and B, f32 accumulator, both K-major, tile M x N.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
+  return (1u << 4)                     // D format: f32
+         | (1u << 7) | (1u << 10)      // A, B: bf16
+         | ((uint32_t)(N >> 3) << 17)  // N / 8
+         | ((uint32_t)(M >> 4) << 24); // M / 16
 }
 
 // Instruction descriptor for kind::i8: signed A and B, int32 accumulator, both K-major, tile M x N.

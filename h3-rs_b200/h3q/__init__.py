@@ -57,6 +57,8 @@ SIGNATURES = {
     "h3q_dequant_nvfp4": (_int, [_vp, _vp, _vp, _vp, _int, _i64, _i64, _vp]),
     "h3q_gate_add": (_int, [_vp, _vp, _int, _vp, _vp, _vp, _i64, _i64, _vp]),
     "h3q_gemm_s8_static": (_int, [_vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _int, _int, _vp]),
+    "h3q_nvfp4_linear_workspace_size": (_sz, [_i64, _i64, _i64, _int]),
+    "h3q_nvfp4_linear": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
     "h3q_default_switches": (Switches, []),
     "h3q_qlinear_plan": (_int, [ctypes.POINTER(QLinearDesc), _int, _i64, _int, ctypes.POINTER(Switches)]),
     "h3q_qlinear_workspace_size": (_sz, [ctypes.POINTER(QLinearDesc), _int, _i64, _int, ctypes.POINTER(Switches)]),
@@ -243,6 +245,23 @@ def dequant_nvfp4(q, block_scale, global_scale, out_dtype):
     out = torch.empty((rows, 2 * kp), dtype=out_dtype, device=q.device)
     check(lib().h3q_dequant_nvfp4(_p(q), _p(block_scale), _p(g), _p(out), _kind(out_dtype), rows, 2 * kp,
                                   _stream(q.device)))
+    return out
+
+
+def nvfp4_linear(x, q, block_scale, global_scale, pre_quant_scale=None, bias=None):
+    """QLinear::apply for an NVFP4 layer (weights.rs:612-635), fused: bf16 x [M,K] -> bf16 [M,N]."""
+    import torch
+    g = global_scale.to(torch.float32).reshape(1).contiguous()
+    pqs = None if pre_quant_scale is None else pre_quant_scale.to(torch.bfloat16).contiguous()
+    bias = None if bias is None else bias.to(torch.float32).contiguous()
+    _cuda(x, q, block_scale, g, pqs, bias)
+    M, K = x.shape
+    N = q.shape[0]
+    out = torch.empty((M, N), dtype=torch.bfloat16, device=x.device)
+    need = lib().h3q_nvfp4_linear_workspace_size(M, N, K, int(pqs is not None))
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device=x.device)
+    check(lib().h3q_nvfp4_linear(_p(x), _p(pqs), _p(q), _p(block_scale), _p(g), _p(bias), _p(out), M, N, K, _p(ws),
+                                 ws.numel(), _stream(x.device)))
     return out
 
 

@@ -123,6 +123,19 @@ h3q_status h3q_dequant_nvfp4(const uint8_t* q, const uint8_t* block_scale, const
 h3q_status h3q_gate_add(const void* x, const void* y, int kind, const float* gate, const uint32_t* idx, void* out,
                         int64_t s, int64_t c, void* stream);
 
+/* Workspace bytes h3q_nvfp4_linear needs (the AWQ-scaled activations and, for narrow outputs, split-K partials). */
+size_t h3q_nvfp4_linear_workspace_size(int64_t m, int64_t n, int64_t k, int has_pre_quant_scale);
+
+/* QLinear::apply for an NVFP4 layer (weights.rs:612-635; weight decode kernels.rs:65-81), fused:
+ *   x2 = bf16(x * pre_quant_scale)      (AWQ, bf16 [k] or NULL; weights.rs:617-620)
+ *   out = bf16(x2 @ W^T) (+ bias)       (bias f32 [n] added in bf16, weights.rs:633-635)
+ * with W decoded from q [n, k/2] (even column in the high nibble), e4m3 block scales in the 128x4 swizzled layout
+ * and the f32 global scale (device pointer) inside the GEMM.  x bf16 [m, k], out bf16 [m, n].  This build needs
+ * k % 64 == 0 and n % 128 == 0 (the text encoder's 5120 / 25600). */
+h3q_status h3q_nvfp4_linear(const uint16_t* x, const uint16_t* pre_quant_scale, const uint8_t* q,
+                            const uint8_t* block_scale, const float* global_scale, const float* bias, uint16_t* out,
+                            int64_t m, int64_t n, int64_t k, void* workspace, size_t workspace_bytes, void* stream);
+
 /* ---------------------------------------------------------------------------------------------------------
  * QLinear: the layer-level dispatch of weights.rs (QLinear::prepare / run / run_swiglu / try_gemm_s8 /
  * apply_int8, weights.rs:833-947) over the entry points above.  The reference reads its switches from the

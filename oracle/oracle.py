@@ -236,6 +236,39 @@ def dequant_nvfp4(q: np.ndarray, bs: np.ndarray, g: float, okind: int = 0) -> np
     return out
 
 
+def make_nvfp4_inputs(seed: int, M: int, K: int, N: int):
+    """Synthetic NVFP4+AWQ layer: e2m1 codes uniform over the 16 values (two per byte), e4m3
+    block scales drawn uniformly from the e4m3 values in [0.5, 4] and laid out in the 128x4 swizzle, global scale
+    1/448, AWQ pre-quant scale ~U(0.5, 2) rounded to bf16, x ~N(0, 1) in bf16, bias ~N(0, 0.02).  numpy PCG64
+    stream from `seed`.  Returns (x bits, q, bs, g, pqs bits, bias)."""
+    rng = np.random.default_rng(seed)
+    x = f32_to_bf16_bits(rng.standard_normal((M, K)).astype(np.float32))
+    q = rng.integers(0, 256, size=(N, K // 2), dtype=np.uint8)
+    e4m3_pool = np.array([(e << 3) | m for e in (6, 7, 8) for m in range(8)] + [9 << 3], dtype=np.uint8)
+    ncb = (K // 16 + 3) // 4
+    bs = np.zeros(((N + 127) // 128) * ncb * 512, dtype=np.uint8)
+    vals = rng.choice(e4m3_pool, size=(N, K // 16))
+    r_idx, b_idx = np.meshgrid(np.arange(N), np.arange(K // 16), indexing="ij")
+    off = (r_idx // 128 * ncb + b_idx // 4) * 512 + (r_idx % 32) * 16 + (r_idx % 128 // 32) * 4 + b_idx % 4
+    bs[off.ravel()] = vals.ravel()
+    pqs = f32_to_bf16_bits((rng.random(K) * 1.5 + 0.5).astype(np.float32))
+    bias = (rng.standard_normal(N) * 0.02).astype(np.float32)
+    return x, q, bs, np.float32(1.0 / 448.0), pqs, bias
+
+
+def nvfp4_linear(x_bf16, q, bs, g, pqs_bf16=None, bias=None, rows=None) -> np.ndarray:
+    """QLinear::apply for NVFP4 (weights.rs:612-635): x2 = bf16(x * pqs), W = dequant_nvfp4 -> bf16, y = bf16(x2 W^T)
+    (exact f64 products and sums here; cuBLAS accumulates in f32), + bias added in bf16.  bf16 bits out."""
+    x = bf16_bits_to_f32(x_bf16 if rows is None else x_bf16[rows])
+    if pqs_bf16 is not None:
+        x = bf16_round(x * bf16_bits_to_f32(pqs_bf16)[None, :])
+    w = bf16_bits_to_f32(dequant_nvfp4(q, bs, float(g), 2))
+    y = bf16_round((x.astype(np.float64) @ w.astype(np.float64).T).astype(np.float32))
+    if bias is not None:
+        y = bf16_round(y + bf16_round(np.asarray(bias, dtype=np.float32))[None, :])
+    return f32_to_bf16_bits(y)
+
+
 def gate_add(x, y, kind: int, gate, idx) -> np.ndarray:
     """kernels.rs:418-428."""
     x = np.ascontiguousarray(x)
