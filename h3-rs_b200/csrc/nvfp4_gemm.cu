@@ -41,7 +41,9 @@ constexpr int NF_BD = 128 * 128;  // decoded bf16 weight tile
 constexpr int NF_BR = 128 * 32;   // packed fp4 weight tile: 128 rows x 64 codes
 constexpr int NF_SC = 512;        // one 128-row x 4-block scale atom
 constexpr uint32_t NF_TX = NF_A + NF_BR + NF_SC;
-constexpr size_t NF_SMEM = 1024 + (size_t)NF_STAGES * (NF_A + NF_BD + NF_BR + NF_SC) + EPI_SMEM + 512;
+// the epilogue staging buffers must start on a 1024-byte boundary (the 128-byte swizzle atom of the f32 stores)
+constexpr size_t NF_SC_REGION = ((size_t)NF_STAGES * NF_SC + 1023) / 1024 * 1024;
+constexpr size_t NF_SMEM = 1024 + (size_t)NF_STAGES * (NF_A + NF_BD + NF_BR) + NF_SC_REGION + EPI_SMEM + 512;
 constexpr uint32_t NF_IDESC = idesc_bf16(256, 256);
 }  // namespace
 
@@ -107,7 +109,7 @@ __global__ void __launch_bounds__(NF_THREADS, 1)
   uint8_t* sBD = sA + NF_STAGES * NF_A;
   uint8_t* sBR = sBD + NF_STAGES * NF_BD;
   uint8_t* sSC = sBR + NF_STAGES * NF_BR;
-  uint8_t* sE = sSC + NF_STAGES * NF_SC;
+  uint8_t* sE = sSC + NF_SC_REGION;
   uint64_t* full = reinterpret_cast<uint64_t*>(sE + EPI_SMEM);
   uint64_t* decd = full + NF_STAGES;
   uint64_t* empty = decd + NF_STAGES;
