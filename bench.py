@@ -230,6 +230,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-nvfp4", action="store_true",
+                    help="small case for ncu captures: the two NVFP4 text-encoder linears only")
     ap.add_argument("--profile", action="store_true",
                     help="small case for ncu captures: one 4096-token fc1 linear (quant + GEMM), nothing else")
     args = ap.parse_args()
@@ -238,6 +240,10 @@ def main() -> None:
         return
     if args.profile:
         run_profile_case(args)
+        return
+    if args.profile_nvfp4:
+        import torch
+        print(json.dumps(nvfp4_c3(torch.device("cuda", 0), load_peaks(), reps=args.steps)))
         return
 
     import torch
