@@ -185,7 +185,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                    int group_m) {
   using C = GemmCfg<PAIR>;
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // align by offsetting the __shared__ array itself, so the compiler keeps shared-space (LDS/STS) accesses
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* sA = smem;
   uint8_t* sB = smem + C::kStages * C::kAStage;
   uint8_t* sE = sB + C::kStages * C::kBStage;
@@ -338,7 +339,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t accph = (it >> 1) & 1;
       int mb, nb;
       tile_coords(t, num_m, num_n, group_m, mb, nb);
-      if (!mbar_wait_bounded(&accf[acc], accph, abort_flag, p.err, kDevTimeoutAccFull)) break;
+      const bool ready = mbar_wait_bounded(&accf[acc], accph, abort_flag, p.err, kDevTimeoutAccFull);
+      if (!__all_sync(0xffffffffu, ready)) break;  // the warp's TMEM loads need all 32 lanes
       tc_fence_after();
       const int64_t row0 = (int64_t)mb * C::kTileM + (int64_t)rank * 128 + 32 * q;
       const uint32_t tacc = tmem_base + ((uint32_t)(32 * q) << 16) + acc * 256;

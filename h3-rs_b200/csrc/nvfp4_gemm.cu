@@ -13,8 +13,9 @@
 //               32 bytes) and the 512-byte block-scale atom of those 128 rows x 4 blocks, into a 5-stage ring;
 //   warp 1      TMEM allocation; in the leader CTA, one thread issues the pair MMAs;
 //   warps 2-5   epilogue (TMEM -> bf16 or f32 split-K partials -> TMA store);
-//   warps 6-9   decoders: thread r turns weight row r's 64 codes of the stage into bf16, written straight into
-//               the 128-byte-swizzled K-major layout the MMA reads.  Decode per pair of codes: cvt e2m1x2 ->
+//   warps 6-13  decoders: 256 threads, each turning half of one weight row (32 of the stage's 64 codes) into
+//               bf16, written straight into the 128-byte-swizzled K-major layout the MMA reads; after a named
+//               barrier one thread per CTA signals the leader (two arrivals per stage in all).  Decode per pair of codes: cvt e2m1x2 ->
 //               f16x2, f16x2 multiply by the e4m3 scale (exact: at most 5 significant bits), widen to f32,
 //               multiply by the global scale, round to bf16 -- the same rounding as the reference's dequant.
 // Split-K (units = tiles x splits) keeps all SMs busy for narrow outputs; partials are summed in a fixed order.
@@ -35,7 +36,7 @@ void set_last_error(const char* msg);
 
 namespace {
 constexpr int NF_STAGES = 5;
-constexpr int NF_THREADS = 320;
+constexpr int NF_THREADS = 448;  // 14 warps: TMA, MMA, 4 epilogue, 8 decoders
 constexpr int NF_A = 128 * 128;   // bf16 activation tile: 128 rows x 64 elements
 constexpr int NF_BD = 128 * 128;  // decoded bf16 weight tile
 constexpr int NF_BR = 128 * 32;   // packed fp4 weight tile: 128 rows x 64 codes
@@ -104,7 +105,8 @@ __global__ void __launch_bounds__(NF_THREADS, 1)
     nvfp4_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmO, const Nvfp4Args p, int num_m, int num_n, int nk) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // align by offsetting the __shared__ array itself, so the compiler keeps shared-space (LDS/STS) accesses
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t* sA = smem;
   uint8_t* sBD = sA + NF_STAGES * NF_A;
   uint8_t* sBR = sBD + NF_STAGES * NF_BD;
@@ -125,7 +127,7 @@ __global__ void __launch_bounds__(NF_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < NF_STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&decd[s], 8);
+      mbar_init(&decd[s], 2);
       mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -229,8 +231,10 @@ __global__ void __launch_bounds__(NF_THREADS, 1)
     }
   } else if (warp >= 6) {
     // ------------------------------------------------------------------ decoders (both CTAs)
-    const int r = threadIdx.x - 192;  // weight row of the CTA's 128-row half
+    const int d = threadIdx.x - 192;
+    const int r = d & 127, h = d >> 7;  // weight row of the CTA's 128-row half; which 32 of its 64 codes
     const float g = __ldg(p.gscale);
+    const uint32_t decd_leader0 = mapa_shared(&decd[0], 0);
     int stage = 0;
     uint32_t phase = 0;
     for (int u = unit0; u < num_units; u += units) {
@@ -238,26 +242,29 @@ __global__ void __launch_bounds__(NF_THREADS, 1)
       unit_coords(u, mb, nb, kb0, kb1);
       bool ok = true;
       for (int kb = kb0; kb < kb1; ++kb) {
-        if (!mbar_wait_bounded(&full[stage], phase, abort_flag, p.err, kDevTimeoutFull)) { ok = false; break; }
-        const uint8_t* br = sBR + stage * NF_BR + r * 32;
-        const uint4 q0 = *reinterpret_cast<const uint4*>(br);
-        const uint4 q1 = *reinterpret_cast<const uint4*>(br + 16);
-        const uint32_t sc4 = *reinterpret_cast<const uint32_t*>(sSC + stage * NF_SC + (r % 32) * 16 + (r / 32) * 4);
-        const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+        const bool landed = mbar_wait_bounded(&full[stage], phase, abort_flag, p.err, kDevTimeoutFull);
+        if (!bar_and(1, 256, landed)) { ok = false; break; }  // all decoder threads give up together
+        const uint4 qv = *reinterpret_cast<const uint4*>(sBR + stage * NF_BR + r * 32 + 16 * h);
+        const uint32_t sc2b =
+            *reinterpret_cast<const uint16_t*>(sSC + stage * NF_SC + (r % 32) * 16 + (r / 32) * 4 + 2 * h);
         uint8_t* bd = sBD + stage * NF_BD + r * 128;
 #pragma unroll
-        for (int blk = 0; blk < 4; ++blk) {
-          const uint32_t sb = (sc4 >> (8 * blk)) & 0xffu;
+        for (int j = 0; j < 2; ++j) {
+          const int blk = 2 * h + j;  // 16-code block of the row (4 per stage)
+          const uint32_t sb = (sc2b >> (8 * j)) & 0xffu;
           const uint32_t sc2 = cvt_e4m3x2_f16x2((uint16_t)(sb | (sb << 8)));
           uint32_t o[8];
-          decode_block(qw[2 * blk], qw[2 * blk + 1], sc2, g, o);
+          decode_block(j ? qv.z : qv.x, j ? qv.w : qv.y, sc2, g, o);
           // 16 bf16 = chunks 2*blk and 2*blk+1 of the 128-byte row, 128-byte swizzle
           *reinterpret_cast<uint4*>(bd + (((2 * blk) ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
           *reinterpret_cast<uint4*>(bd + (((2 * blk + 1) ^ (r & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
         }
         fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_cluster(mapa_shared(&decd[stage], 0));
+        asm volatile("bar.sync 1, 256;" ::: "memory");  // all 8 decoder warps of this CTA are done with the stage
+        if (d == 0) {
+          if (leader) mbar_arrive(&decd[stage]);
+          else mbar_arrive_cluster(decd_leader0 + (uint32_t)(stage * sizeof(uint64_t)));
+        }
         if (++stage == NF_STAGES) { stage = 0; phase ^= 1; }
       }
       if (!ok) break;
@@ -274,7 +281,8 @@ __global__ void __launch_bounds__(NF_THREADS, 1)
       const int ks = u % splits;
       const int acc = it & 1;
       const uint32_t accph = (it >> 1) & 1;
-      if (!mbar_wait_bounded(&accf[acc], accph, abort_flag, p.err, kDevTimeoutAccFull)) break;
+      const bool ready = mbar_wait_bounded(&accf[acc], accph, abort_flag, p.err, kDevTimeoutAccFull);
+      if (!__all_sync(0xffffffffu, ready)) break;  // the warp's TMEM loads need all 32 lanes
       tc_fence_after();
       const int64_t row0 = (int64_t)mb * 256 + (int64_t)rank * 128 + 32 * q;
       const uint32_t tacc = tmem_base + ((uint32_t)(32 * q) << 16) + acc * 256;

@@ -119,6 +119,19 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, int* 
   mbar_wait_bounded(bar, parity, &dummy, err, code);
 }
 
+// Named barrier `id` over `nthreads` threads that also ANDs `v` across them: every participant gets the same
+// answer, so a give-up decision after a bounded wait is taken by all of them together.
+__device__ __forceinline__ bool bar_and(uint32_t id, uint32_t nthreads, bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\tbar.red.and.pred p, %2, %3, q;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(r)
+      : "r"((uint32_t)v), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
+
 // ------------------------------------------------------------------------------------------------ TMA
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");

@@ -169,7 +169,8 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
                                                          int64_t M, int K, int box_rows, int boxes_per_row,
                                                          int* err, uint16_t* __restrict__ ybf) {
   extern __shared__ uint8_t qsm_raw[];
-  uint8_t* qsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(qsm_raw) + 1023) & ~uintptr_t(1023));
+  // align by offsetting the __shared__ array itself, so the compiler keeps shared-space (LDS/STS) accesses
+  uint8_t* qsm = qsm_raw + ((1024u - (smem_u32(qsm_raw) & 1023u)) & 1023u);
   __shared__ uint64_t full[kQStages];
   __shared__ unsigned s_max[3];
   __shared__ int s_abort;
@@ -204,7 +205,8 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
   int it = 0;
   for (int64_t row = blockIdx.x; row < M; row += gridDim.x, ++it) {
     const int stage = it % kQStages;
-    if (!mbar_wait_bounded(&full[stage], (uint32_t)(it / kQStages) & 1u, &s_abort, err, kDevTimeoutFull)) break;
+    const bool landed = mbar_wait_bounded(&full[stage], (uint32_t)(it / kQStages) & 1u, &s_abort, err, kDevTimeoutFull);
+    if (!__syncthreads_and(landed)) break;  // the whole CTA gives up together (barriers follow)
     float v[64];
     if (owner) {
       const uint8_t* base = qsm + (size_t)stage * stage_bytes;
