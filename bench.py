@@ -203,6 +203,51 @@ def nvfp4_c3(dev, peaks: dict, reps: int = 10) -> dict:
             "note": "time per call includes the AWQ pre-pass and, for 25600->5120, the split-K reduction"}
 
 
+def attention_c4(dev, peaks: dict, reps: int = 5, S: int = 32760, H: int = 40) -> dict:
+    """BASELINE config 4's attention: SageAttention-style int8 Q.K^T + f16 P.V at batch 1, 40 heads, head_dim 128,
+    32760 tokens.  CUDA-event time of the whole attn8::attention pipeline (K mean, Q/K quantisation, V relayout,
+    the tcgen05 attention kernel) and of the attention kernel alone; TOPS counted as the reference's attention bench
+    counts them (4 S^2 D H, examples/attn_bench.rs), plus each half against its own peak."""
+    import torch
+    import h3q
+    g = torch.Generator(device=dev).manual_seed(41)
+    q = torch.randn((S, H, 128), generator=g, device=dev).to(torch.bfloat16)
+    k = (torch.randn((S, H, 128), generator=g, device=dev) +
+         3.0 * torch.randn((1, H, 128), generator=g, device=dev)).to(torch.bfloat16)
+    v = torch.randn((S, H, 128), generator=g, device=dev).to(torch.bfloat16)
+    res = {}
+    for name, flags in (("per_token_f16", 0), ("block128_bf16", h3q.ATTN_SCALE_BLOCK128 | h3q.ATTN_PV_BF16)):
+        for _ in range(2):
+            h3q.attention(q, k, v, flags)
+        km = h3q.attn_kmean(k)
+        q8, qs = h3q.attn_quant_heads(q, None, flags)
+        k8, ks = h3q.attn_quant_heads(k, km, flags)
+        vt = h3q.attn_v_layout(v.reshape(S, H * 128), H * 128, 0, S, H, flags)
+        h3q.attention_core(q8, qs, k8, ks, vt, flags)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        ev[0].record()
+        for _ in range(reps):
+            h3q.attention(q, k, v, flags)
+        ev[1].record()
+        for _ in range(reps):
+            h3q.attention_core(q8, qs, k8, ks, vt, flags)
+        ev[2].record()
+        torch.cuda.synchronize()
+        ms_all = ev[0].elapsed_time(ev[1]) / reps
+        ms_core = ev[1].elapsed_time(ev[2]) / reps
+        half = 2.0 * S * S * 128 * H
+        res[name] = {"ms_pipeline": round(ms_all, 3), "ms_kernel": round(ms_core, 3),
+                     "tops_pipeline": round(2 * half / (ms_all * 1e-3) / 1e12, 1),
+                     "tops_kernel": round(2 * half / (ms_core * 1e-3) / 1e12, 1),
+                     "kernel_time_at_peaks_ms": round((half / (2 * peaks["bf16_tflops"] * 1e12) +
+                                                       half / (peaks["bf16_tflops"] * 1e12)) * 1e3, 3)}
+        res[name]["frac_of_tensor_roofline"] = round(res[name]["kernel_time_at_peaks_ms"] / ms_core, 3)
+    res["device_status"] = h3q.device_status(dev.index or 0)
+    return {"workload": f"BASELINE c4 attention: B1 H{H} D128 S{S}, non-causal", "modes": res,
+            "note": "tops = 4 S^2 D H / time (the reference's count); roofline = QK at 2x bf16 burst + PV at bf16 "
+                    "burst, serial"}
+
+
 def run_profile_case(args) -> None:
     """One fc1-shaped linear at 4096 tokens (A 21 MB, W 71 MB, out 113 MB: more than L2 in total, a few hundred
     MB on the device): warmup + steps launches of the quantizer and the GEMM, for ncu --set full captures."""
@@ -232,6 +277,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-nvfp4", action="store_true",
                     help="small case for ncu captures: the two NVFP4 text-encoder linears only")
+    ap.add_argument("--profile-attn", action="store_true",
+                    help="small case for ncu captures: the attention pipeline at S=8192, H=4")
     ap.add_argument("--profile", action="store_true",
                     help="small case for ncu captures: one 4096-token fc1 linear (quant + GEMM), nothing else")
     args = ap.parse_args()
@@ -244,6 +291,10 @@ def main() -> None:
     if args.profile_nvfp4:
         import torch
         print(json.dumps(nvfp4_c3(torch.device("cuda", 0), load_peaks(), reps=args.steps)))
+        return
+    if args.profile_attn:
+        import torch
+        print(json.dumps(attention_c4(torch.device("cuda", 0), load_peaks(), reps=args.steps, S=8192, H=4)))
         return
 
     import torch
@@ -382,6 +433,7 @@ def main() -> None:
                "path": "h3q_gemm_s8 (C ABI) with pinned host input/output, copies inside the timed region"}
 
     nv = nvfp4_c3(dev, load_peaks()) if rank == 0 else None
+    att = attention_c4(dev, load_peaks()) if rank == 0 else None
 
     cb = None
     if rank == 0 and ws_n == 1 and not args.no_cpu_baseline:
@@ -410,6 +462,7 @@ def main() -> None:
                            "bytes_per_launch": quant_bytes_launch},
         "per_linear": per_linear,
         "nvfp4_c3": nv,
+        "attention_c4": att,
         "cpu_baseline": cb, "e2e": e2e, "clocks": clk.summary(),
         "gpu_launches": 2 * launches,
     }

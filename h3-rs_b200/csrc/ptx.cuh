@@ -19,6 +19,10 @@ enum DeviceError : int {
   kDevTimeoutAccFull = 3,  // epilogue waited too long for an accumulator
   kDevTimeoutAccEmpty = 4, // MMA warp waited too long for the epilogue to drain an accumulator
   kDevTimeoutDrain = 5,    // TMA warp gave up waiting for its own loads at exit
+  kDevTimeoutScores = 6,   // attention: softmax warps waited too long for a score tile
+  kDevTimeoutProbs = 7,    // attention: MMA warp waited too long for a probability tile
+  kDevTimeoutScale = 8,    // attention: softmax warps waited too long for the key scales
+  kDevTimeoutPV = 9,       // attention: softmax warps waited too long for the P.V product
 };
 
 // ------------------------------------------------------------------------------------------------ numbers
@@ -143,6 +147,16 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
       "[%2];" ::"r"(smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// 3-D tiled load of the box at (x, y, z) into shared memory; completes on `bar`.
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m, uint64_t* bar, int32_t x,
+                                            int32_t y, int32_t z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], "
+      "[%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
 
@@ -284,6 +298,30 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
       : "memory");
 }
 
+// D[tmem] (+)= A[smem] * B[smem]^T for 16-bit operands (f16 or bf16, by the instruction descriptor), f32 D.
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns from registers into TMEM (the inverse of tmem_ld_32x32b_x32).
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, "
+      "%17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+      "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
+      "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 // Shared-memory matrix descriptor for a K-major operand stored with the 128-byte swizzle that TMA
 // writes: rows of 128 bytes, 8-row atoms 1024 bytes apart (SBO), leading offset unused, version 1.
 __device__ __forceinline__ uint64_t smem_desc_k128(uint32_t smem_addr) {
@@ -302,6 +340,12 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
          | (1u << 7) | (1u << 10)      // A, B: bf16
          | ((uint32_t)(N >> 3) << 17)  // N / 8
          | ((uint32_t)(M >> 4) << 24); // M / 16
+}
+
+// Instruction descriptor for kind::f16 with f16 (bf16 = false) or bf16 A and B, f32 accumulator, K-major.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool bf16) {
+  return (1u << 4) | (bf16 ? ((1u << 7) | (1u << 10)) : 0u) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
 }
 
 // Instruction descriptor for kind::i8: signed A and B, int32 accumulator, both K-major, tile M x N.

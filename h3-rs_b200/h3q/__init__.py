@@ -33,6 +33,7 @@ class Switches(ctypes.Structure):
 
 
 FMT_DENSE, FMT_INT8, FMT_NVFP4 = 0, 1, 2
+ATTN_SCALE_TOKEN, ATTN_SCALE_BLOCK128, ATTN_PV_F16, ATTN_PV_BF16 = 0, 1, 0, 2
 PATH_GEMM_S8, PATH_INT8_LINEAR, PATH_ROTATE_FUSED, PATH_ROTATE_SEPARATE, PATH_SWIGLU_FUSED, PATH_SWIGLU_AFTER = (
     1, 2, 4, 8, 16, 32)
 
@@ -64,6 +65,15 @@ SIGNATURES = {
     "h3q_qlinear_workspace_size": (_sz, [ctypes.POINTER(QLinearDesc), _int, _i64, _int, ctypes.POINTER(Switches)]),
     "h3q_qlinear_forward": (_int, [ctypes.POINTER(QLinearDesc), _vp, _int, _i64, _int, _vp, _vp, _sz,
                                    ctypes.POINTER(Switches), _vp]),
+    "h3q_attention_available": (_int, [_i64, _int, _int]),
+    "h3q_attention_workspace_size": (_sz, [_i64, _i64, _int]),
+    "h3q_attention": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _int, _vp, _sz, _vp]),
+    "h3q_attention_qkv": (_int, [_vp, _vp, _vp, _i64, _i64, _vp, _i64, _i64, _int, _vp, _sz, _vp]),
+    "h3q_attn_kmean_workspace_size": (_sz, [_i64, _i64]),
+    "h3q_attn_kmean": (_int, [_vp, _i64, _i64, _vp, _vp, _sz, _vp]),
+    "h3q_attn_quant_heads": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _int, _vp]),
+    "h3q_attn_v_layout": (_int, [_vp, _i64, _i64, _vp, _i64, _i64, _int, _vp]),
+    "h3q_attention_core": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _int, _vp, _vp]),
 }
 
 
@@ -274,6 +284,87 @@ def gate_add(x, y, gate, idx):
     out = torch.empty_like(x)
     check(lib().h3q_gate_add(_p(x), _p(y), _kind(x.dtype), _p(gate), _p(idx), _p(out), S, C, _stream(x.device)))
     return out
+
+
+def attention_available(q) -> bool:
+    """attn8::available (attn8.rs:592-602): head_dim 128, bf16, an sm_100 device."""
+    import torch
+    if not q.is_cuda:
+        return False
+    return bool(lib().h3q_attention_available(q.shape[-1], _kind(q.dtype) if q.dtype in (
+        torch.float32, torch.float16, torch.bfloat16) else -1, q.device.index or 0))
+
+
+def attention(q, k, v, flags: int = 0):
+    """attn8::attention (attn8.rs:611-615): q, k, v bf16 [S, H, 128] -> bf16 [S, H, 128]."""
+    import torch
+    _cuda(q, k, v)
+    S, H, _ = q.shape
+    out = torch.empty_like(q)
+    need = lib().h3q_attention_workspace_size(S, H, flags)
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)
+    check(lib().h3q_attention(_p(q), _p(k), _p(v), _p(out), S, H, flags, _p(ws), ws.numel(), _stream(q.device)))
+    return out
+
+
+def attention_qkv(q, k, qkv, v_col: int, flags: int = 0):
+    """attn8::attention_qkv (attn8.rs:604-609): V read from the fused qkv [S, W] at column v_col."""
+    import torch
+    _cuda(q, k, qkv)
+    S, H, _ = q.shape
+    out = torch.empty_like(q)
+    need = lib().h3q_attention_workspace_size(S, H, flags)
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)
+    check(lib().h3q_attention_qkv(_p(q), _p(k), _p(qkv), qkv.shape[1], v_col, _p(out), S, H, flags, _p(ws),
+                                  ws.numel(), _stream(q.device)))
+    return out
+
+
+def attn_kmean(k):
+    """ColMean / S (attn8.rs:429-455, :622) in a fixed summation order: f32 [H, 128]."""
+    import torch
+    _cuda(k)
+    S, H, _ = k.shape
+    out = torch.empty((H, 128), dtype=torch.float32, device=k.device)
+    need = lib().h3q_attn_kmean_workspace_size(S, H)
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device=k.device)
+    check(lib().h3q_attn_kmean(_p(k), S, H, _p(out), _p(ws), ws.numel(), _stream(k.device)))
+    return out
+
+
+def attn_quant_heads(x, mean=None, flags: int = 0):
+    """QuantHeads (attn8.rs:395-427): codes int8 [H, S, 128], scales f32 [H, roundup(S, 128)]."""
+    import torch
+    _cuda(x, mean)
+    S, H, _ = x.shape
+    Sp = (S + 127) // 128 * 128
+    codes = torch.empty((H, S, 128), dtype=torch.int8, device=x.device)
+    scales = torch.empty((H, Sp), dtype=torch.float32, device=x.device)
+    check(lib().h3q_attn_quant_heads(_p(x), _p(mean), _p(codes), _p(scales), S, H, flags, _stream(x.device)))
+    return codes, scales
+
+
+def attn_v_layout(src, row_stride: int, col_off: int, S: int, H: int, flags: int = 0):
+    """VToF16 (attn8.rs:457-486), transposed: V^T [H, 128, roundup(S, 128)] in f16 (or bf16)."""
+    import torch
+    _cuda(src)
+    Sp = (S + 127) // 128 * 128
+    dt = torch.bfloat16 if flags & ATTN_PV_BF16 else torch.float16
+    vt = torch.empty((H, 128, Sp), dtype=dt, device=src.device)
+    check(lib().h3q_attn_v_layout(_p(src), row_stride, col_off, _p(vt), S, H, flags, _stream(src.device)))
+    return vt
+
+
+def attention_core(q8, qs, k8, ks, vt, flags: int = 0, scores: bool = False):
+    """Attn (attn8.rs:488-520) on prepared stages -> bf16 [S, H, 128] (and the int32 Q.K^T [H, S, S] if scores)."""
+    import torch
+    _cuda(q8, qs, k8, ks, vt)
+    H, S, _ = q8.shape
+    out = torch.empty((S, H, 128), dtype=torch.bfloat16, device=q8.device)
+    sc = torch.empty((H, S, S), dtype=torch.int32, device=q8.device) if scores else None
+    check(lib().h3q_attention_core(_p(q8), _p(qs), _p(k8), _p(ks), _p(vt), _p(out), S, H, flags, _p(sc),
+                                   _stream(q8.device)))
+    return (out, sc) if scores else out
 
 
 def default_switches() -> Switches:

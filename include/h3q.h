@@ -190,6 +190,57 @@ h3q_status h3q_qlinear_forward(const h3q_qlinear* layer, const void* x, int x_ki
                                void* out, void* workspace, size_t workspace_bytes, const h3q_switches* sw,
                                void* stream);
 
+/* ---------------------------------------------------------------------------------------------------------
+ * int8 attention (attn8.rs): non-causal SageAttention-style attention over [S, H, 128] bf16 q / k / v, int8
+ * Q.K^T with K smoothed by its mean over the sequence, online softmax, 16-bit P.V with f32 accumulation.
+ * Layouts of the stage buffers: codes int8 [H, S, 128]; scales f32 [H, Sp] with Sp = roundup(S, 128) (entries
+ * S..Sp-1 zero); V^T 16-bit [H, 128, Sp].  Output bf16 [S, H, 128].
+ * ------------------------------------------------------------------------------------------------------- */
+enum {
+  H3Q_ATTN_SCALE_TOKEN = 0,    /* per-token Q / K scales (QuantHeads, attn8.rs:69-93)                        */
+  H3Q_ATTN_SCALE_BLOCK128 = 1, /* one scale per 128-token block of a head (every token of the block holds it) */
+  H3Q_ATTN_PV_F16 = 0,         /* P and V in f16 (attn8.rs:55-65, :100-104)                                  */
+  H3Q_ATTN_PV_BF16 = 2         /* P and V in bf16                                                            */
+};
+
+/* available(q) (attn8.rs:591-602): 1 if the int8 attention runs for head_dim on `device` with activations of
+ * x_kind (head_dim 128, bf16, an sm_100 device), else 0. */
+int h3q_attention_available(int64_t head_dim, int x_kind, int device);
+
+/* Workspace bytes of h3q_attention / h3q_attention_qkv for S tokens and H heads (flags: H3Q_ATTN_*). */
+size_t h3q_attention_workspace_size(int64_t S, int64_t H, int flags);
+
+/* attention(q, k, v) (attn8.rs:611-615): q, k, v bf16 [S, H, 128] contiguous -> out bf16 [S, H, 128]. */
+h3q_status h3q_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int64_t S,
+                         int64_t H, int flags, void* workspace, size_t workspace_bytes, void* stream);
+
+/* attention_qkv(q, k, qkv, v_col) (attn8.rs:604-609): V read from the fused qkv activation [S, qkv_width] at
+ * column v_col (head h at v_col + 128 h). */
+h3q_status h3q_attention_qkv(const uint16_t* q, const uint16_t* k, const uint16_t* qkv, int64_t qkv_width,
+                             int64_t v_col, uint16_t* out, int64_t S, int64_t H, int flags, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
+/* The stages, for callers that keep the intermediates. */
+/* Workspace bytes of h3q_attn_kmean (the per-chunk column sums). */
+size_t h3q_attn_kmean_workspace_size(int64_t S, int64_t H);
+/* ColMean then `/ S` (attn8.rs:429-455, :622): kmean f32 [H, 128] = column sums of k [S, H*128] in a fixed order
+ * (chunks of ceil(S / min(128, S)) rows, chunk sums added in chunk order) times (float)(1 / S). */
+h3q_status h3q_attn_kmean(const uint16_t* k, int64_t S, int64_t H, float* kmean, void* workspace,
+                          size_t workspace_bytes, void* stream);
+/* QuantHeads (attn8.rs:395-427, kernel :69-93): x bf16 [S, H, 128] minus mean [H, 128] (NULL: none) -> codes
+ * [H, S, 128] (clamp +-127) and scales [H, Sp]; flags H3Q_ATTN_SCALE_*. */
+h3q_status h3q_attn_quant_heads(const uint16_t* x, const float* mean, int8_t* codes, float* scales, int64_t S,
+                                int64_t H, int flags, void* stream);
+/* VToF16 (attn8.rs:457-486, kernel :55-65), transposed: rows of [S, row_stride] bf16 at column col_off ->
+ * V^T [H, 128, Sp] in f16 (cvt.rn) or, with H3Q_ATTN_PV_BF16, bf16. */
+h3q_status h3q_attn_v_layout(const uint16_t* src, int64_t row_stride, int64_t col_off, uint16_t* vt, int64_t S,
+                             int64_t H, int flags, void* stream);
+/* Attn (attn8.rs:488-520, kernel :107-246) on prepared stages.  If `scores` is not NULL it also receives the
+ * int32 Q.K^T accumulators [H, S, S] (a diagnostic form for small S). */
+h3q_status h3q_attention_core(const int8_t* q8, const float* qs, const int8_t* k8, const float* ks,
+                              const uint16_t* vt, uint16_t* out, int64_t S, int64_t H, int flags, int32_t* scores,
+                              void* stream);
+
 /* h3q_gemm_s8 for callers that cannot allocate device memory (no counterpart in the reference).  Some callers
  * cannot call cudaMalloc: a plugin inside a host that has already reserved the GPU's whole memory for its own
  * pool, or code where cudaMalloc's implicit synchronisation or failure under memory pressure is not acceptable.

@@ -547,3 +547,160 @@ H3O_API void h3o_dequant_nvfp4(const uint8_t* q, const uint8_t* bs, float g, voi
             stf(out, okind, (size_t)(r * k + c), E2M1[nib] * s * g);
         }
 }
+
+/* ---------------------------------------------------------------- int8 attention (attn8.rs) */
+
+/*
+ * ColMean + `/ S` (attn8.rs:45-52 col_sum, launch :440-453, mean :622): column sums of k [S, C] (bf16, C = H*128)
+ * over row chunks of rows_per = ceil(S / min(128, S)) rows, each chunk summed in row order from 0.f, the chunk
+ * sums added in chunk order from 0.f (the reference adds them with atomicAdd in completion order), then
+ * multiplied by (float)(1 / S) (candle's affine with mul = 1/S).
+ */
+H3O_API void h3o_attn_kmean(const uint16_t* k, int64_t S, int64_t H, float* mean) {
+    const int64_t C = H * 128;
+    const int64_t parts = S < 128 ? S : 128;
+    const int64_t rows_per = (S + parts - 1) / parts;
+    const float inv_s = (float)(1.0 / (double)S);
+    for (int64_t c = 0; c < C; ++c) {
+        float a = 0.f;
+        for (int64_t r0 = 0; r0 < S; r0 += rows_per) {
+            float s = 0.f;
+            const int64_t r1 = r0 + rows_per < S ? r0 + rows_per : S;
+            for (int64_t r = r0; r < r1; ++r) s += bf2f(k[r * C + c]);
+            a += s;
+        }
+        mean[c] = a * inv_s;
+    }
+}
+
+/* quant_heads' per-element code (attn8.rs:85-90): clamp(__float2int_rn(v * inv), -127, 127) */
+static inline int8_t q127(float v, float inv) {
+    int q = f2i_rn(v * inv);
+    return (int8_t)(q < -127 ? -127 : (q > 127 ? 127 : q));
+}
+
+/*
+ * QuantHeads (attn8.rs:69-93): x bf16 [S, H, 128], v = x - mean[h, d] (or - 0), sc = fmaxf(max|v| / 127, 1e-20),
+ * inv = 1 / sc, codes [H, S, 128], scales [H, Sp] with Sp = roundup(S, 128), pads zero.
+ * block128: one scale per 128-token block of a head (the maximum over the block's valid tokens), stored at
+ * every token of the block.
+ */
+H3O_API void h3o_attn_quant_heads(const uint16_t* x, const float* mean, int8_t* codes, float* scales, int64_t S,
+                                  int64_t H, int block128) {
+    const int64_t Sp = (S + 127) / 128 * 128;
+    memset(scales, 0, (size_t)(H * Sp) * sizeof(float));
+    float v[128];
+    for (int64_t h = 0; h < H; ++h) {
+        if (!block128) {
+            for (int64_t s = 0; s < S; ++s) {
+                const uint16_t* xr = x + (s * H + h) * 128;
+                float m = 0.f;
+                for (int d = 0; d < 128; ++d) {
+                    v[d] = bf2f(xr[d]) - (mean ? mean[h * 128 + d] : 0.f);
+                    m = fmaxf(m, fabsf(v[d]));
+                }
+                const float sc = fmaxf(m / 127.f, 1e-20f);
+                const float inv = 1.f / sc;
+                for (int d = 0; d < 128; ++d) codes[(h * S + s) * 128 + d] = q127(v[d], inv);
+                scales[h * Sp + s] = sc;
+            }
+        } else {
+            for (int64_t b0 = 0; b0 < S; b0 += 128) {
+                const int64_t b1 = b0 + 128 < S ? b0 + 128 : S;
+                float m = 0.f;
+                for (int64_t s = b0; s < b1; ++s)
+                    for (int d = 0; d < 128; ++d)
+                        m = fmaxf(m, fabsf(bf2f(x[(s * H + h) * 128 + d]) - (mean ? mean[h * 128 + d] : 0.f)));
+                const float sc = fmaxf(m / 127.f, 1e-20f);
+                const float inv = 1.f / sc;
+                for (int64_t s = b0; s < b1; ++s) {
+                    for (int d = 0; d < 128; ++d) {
+                        const float vv = bf2f(x[(s * H + h) * 128 + d]) - (mean ? mean[h * 128 + d] : 0.f);
+                        codes[(h * S + s) * 128 + d] = q127(vv, inv);
+                    }
+                    scales[h * Sp + s] = sc;
+                }
+            }
+        }
+    }
+}
+
+/* int32 Q.K^T accumulators [H, S, S] of codes [H, S, 128] (attn8.rs:177-184 mma_s8 loop) */
+H3O_API void h3o_attn_scores(const int8_t* q8, const int8_t* k8, int64_t S, int64_t H, int32_t* out) {
+    for (int64_t h = 0; h < H; ++h)
+        for (int64_t i = 0; i < S; ++i) {
+            const int8_t* a = q8 + (h * S + i) * 128;
+            for (int64_t j = 0; j < S; ++j) {
+                const int8_t* b = k8 + (h * S + j) * 128;
+                int32_t s = 0;
+                for (int d = 0; d < 128; ++d) s += (int32_t)a[d] * (int32_t)b[d];
+                out[(h * S + i) * S + j] = s;
+            }
+        }
+}
+
+/* scale_log2 = (1 / sqrt(128)) * LOG2_E in f32 (attn8.rs:625) */
+H3O_API float h3o_attn_scale_log2(void) {
+    volatile float d = 128.0f;
+    const float r = 1.0f / sqrtf(d);
+    return r * 1.44269504088896340736f;
+}
+
+/*
+ * attn_qk8 (attn8.rs:107-246) for one head at a time, in its 64-key tiles:
+ *   p = (float)acc * (qs * scale_log2) * ks      (keys >= S excluded)
+ *   per tile: mn = max(m, tile max); a = 2^(m - mn); p = 2^(p - mn); l = l * a + sum p; o = o * a + sum f16(p) v
+ *   out = bf16(o * (1 / l))
+ * V is taken from rows of src (bf16, row stride v_rs elements, head h at column v_col + 128 h) and rounded to f16
+ * as v_to_f16 does (attn8.rs:55-65), or kept in bf16 with P rounded to bf16 (pv_bf16).  exp2f stands in for
+ * ex2.approx; sums run in a fixed order.  Output bf16 [S, H, 128].
+ */
+H3O_API void h3o_attn_forward(const int8_t* q8, const float* qs, const int8_t* k8, const float* ks,
+                              const uint16_t* vsrc, int64_t v_rs, int64_t v_col, uint16_t* out, int64_t S, int64_t H,
+                              int pv_bf16) {
+    const int64_t Sp = (S + 127) / 128 * 128;
+    const float sl2 = h3o_attn_scale_log2();
+    float* vv = (float*)malloc((size_t)S * 128 * sizeof(float));
+    float p[64], o[128];
+    for (int64_t h = 0; h < H; ++h) {
+        for (int64_t s = 0; s < S; ++s)
+            for (int d = 0; d < 128; ++d) {
+                const uint16_t b = vsrc[s * v_rs + v_col + h * 128 + d];
+                vv[s * 128 + d] = pv_bf16 ? bf2f(b) : h2f(f2h(bf2f(b)));
+            }
+        for (int64_t i = 0; i < S; ++i) {
+            const int8_t* a = q8 + (h * S + i) * 128;
+            const float qs0 = qs[h * Sp + i] * sl2;
+            float m = -INFINITY, l = 0.f;
+            for (int d = 0; d < 128; ++d) o[d] = 0.f;
+            for (int64_t j0 = 0; j0 < S; j0 += 64) {
+                const int64_t nj = S - j0 < 64 ? S - j0 : 64;
+                float mx = -INFINITY;
+                for (int64_t j = 0; j < nj; ++j) {
+                    const int8_t* b = k8 + (h * S + j0 + j) * 128;
+                    int32_t acc = 0;
+                    for (int d = 0; d < 128; ++d) acc += (int32_t)a[d] * (int32_t)b[d];
+                    p[j] = (float)acc * qs0 * ks[h * Sp + j0 + j];
+                    mx = fmaxf(mx, p[j]);
+                }
+                const float mn = fmaxf(m, mx);
+                const float al = mn == -INFINITY ? 1.f : exp2f(m - mn);
+                const float bb = mn == -INFINITY ? 0.f : mn;
+                float sum = 0.f;
+                for (int d = 0; d < 128; ++d) o[d] *= al;
+                for (int64_t j = 0; j < nj; ++j) {
+                    p[j] = exp2f(p[j] - bb);
+                    sum += p[j];
+                    const float pr = pv_bf16 ? bf16r(p[j]) : h2f(f2h(p[j]));
+                    const float* vr = vv + (j0 + j) * 128;
+                    for (int d = 0; d < 128; ++d) o[d] += pr * vr[d];
+                }
+                l = l * al + sum;
+                m = mn;
+            }
+            const float inv = l > 0.f ? 1.f / l : 0.f;
+            for (int d = 0; d < 128; ++d) out[(i * H + h) * 128 + d] = f2bf(o[d] * inv);
+        }
+    }
+    free(vv);
+}

@@ -319,3 +319,95 @@ def max_abs_rel(y: np.ndarray, r: np.ndarray) -> float:
     r = np.asarray(r, dtype=np.float64)
     den = np.max(np.abs(r))
     return float(np.max(np.abs(y - r)) / den) if den > 0 else float(np.max(np.abs(y - r)))
+
+
+# ----------------------------------------------------------------------------- int8 attention (attn8.rs)
+
+ATTN_SCALE_BLOCK128 = 1
+ATTN_PV_BF16 = 2
+
+
+def make_attn_inputs(seed: int, S: int, H: int, k_offset: float = 0.0):
+    """Seeded q, k, v bf16 bits [S, H, 128] ~ N(0, 1) drawn in that order from one TorchGen stream.  k_offset > 0
+    adds a per-(head, dim) offset ~ N(0, k_offset) to K, the outlier channels of real keys that the reference's
+    attention bench builds (examples/attn_bench.rs) and its mean smoothing removes."""
+    g = TorchGen(seed)
+    n = S * H * 128
+    q = f32_to_bf16_bits(g.randn(n).reshape(S, H, 128))
+    k = g.randn(n).reshape(S, H, 128)
+    v = f32_to_bf16_bits(g.randn(n).reshape(S, H, 128))
+    if k_offset:
+        k = k + (g.randn(H * 128) * np.float32(k_offset)).reshape(1, H, 128)
+    return q, f32_to_bf16_bits(k.astype(np.float32)), v
+
+
+def attn_kmean(k_bf16: np.ndarray) -> np.ndarray:
+    """ColMean / S (attn8.rs:45-52, :429-455, :622) in the fixed chunk order.  f32 [H, 128]."""
+    k = np.ascontiguousarray(k_bf16, dtype=np.uint16)
+    S, H = k.shape[0], k.shape[1]
+    out = np.empty((H, 128), dtype=np.float32)
+    lib().h3o_attn_kmean(_p(k), c_i64(S), c_i64(H), _p(out))
+    return out
+
+
+def attn_quant_heads(x_bf16: np.ndarray, mean=None, block128: bool = False):
+    """QuantHeads (attn8.rs:69-93): codes int8 [H, S, 128], scales f32 [H, roundup(S, 128)]."""
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
+    S, H = x.shape[0], x.shape[1]
+    Sp = (S + 127) // 128 * 128
+    codes = np.empty((H, S, 128), dtype=np.int8)
+    scales = np.empty((H, Sp), dtype=np.float32)
+    m = None if mean is None else np.ascontiguousarray(mean, dtype=np.float32)
+    lib().h3o_attn_quant_heads(_p(x), _p(m), _p(codes), _p(scales), c_i64(S), c_i64(H), c_int(1 if block128 else 0))
+    return codes, scales
+
+
+def attn_scores(q8: np.ndarray, k8: np.ndarray) -> np.ndarray:
+    """int32 Q.K^T [H, S, S] of codes [H, S, 128]."""
+    H, S = q8.shape[0], q8.shape[1]
+    out = np.empty((H, S, S), dtype=np.int32)
+    lib().h3o_attn_scores(_p(np.ascontiguousarray(q8)), _p(np.ascontiguousarray(k8)), c_i64(S), c_i64(H), _p(out))
+    return out
+
+
+def attn_scale_log2() -> float:
+    lib().h3o_attn_scale_log2.restype = c_f32
+    return float(lib().h3o_attn_scale_log2())
+
+
+def attn_forward(q8, qs, k8, ks, vsrc_bf16, v_rs: int, v_col: int, pv_bf16: bool = False) -> np.ndarray:
+    """attn_qk8 (attn8.rs:107-246) on prepared codes / scales, V from rows of vsrc (bf16 bits, row stride v_rs,
+    head h at column v_col + 128 h).  bf16 bits [S, H, 128]."""
+    H, S = q8.shape[0], q8.shape[1]
+    out = np.empty((S, H, 128), dtype=np.uint16)
+    v = np.ascontiguousarray(vsrc_bf16, dtype=np.uint16)
+    lib().h3o_attn_forward(_p(np.ascontiguousarray(q8)), _p(np.ascontiguousarray(qs, dtype=np.float32)),
+                           _p(np.ascontiguousarray(k8)), _p(np.ascontiguousarray(ks, dtype=np.float32)), _p(v),
+                           c_i64(v_rs), c_i64(v_col), _p(out), c_i64(S), c_i64(H), c_int(1 if pv_bf16 else 0))
+    return out
+
+
+def attention(q_bf16, k_bf16, v_bf16, flags: int = 0) -> np.ndarray:
+    """attention(q, k, v) (attn8.rs:611-627): K mean, Q / K quantisation, int8 attention.  bf16 bits [S, H, 128]."""
+    S, H = q_bf16.shape[0], q_bf16.shape[1]
+    block = bool(flags & ATTN_SCALE_BLOCK128)
+    km = attn_kmean(k_bf16)
+    q8, qs = attn_quant_heads(q_bf16, None, block)
+    k8, ks = attn_quant_heads(k_bf16, km, block)
+    return attn_forward(q8, qs, k8, ks, np.ascontiguousarray(v_bf16).reshape(S, H * 128), H * 128, 0,
+                        bool(flags & ATTN_PV_BF16))
+
+
+def attention_exact(q_bf16, k_bf16, v_bf16) -> np.ndarray:
+    """Softmax attention in f64 on the bf16 inputs (no quantisation): the float semantics the int8 attention
+    approximates (ops.rs:72-109 attention_fallback, non-causal).  f64 [S, H, 128]."""
+    q = bf16_bits_to_f32(q_bf16).astype(np.float64)
+    k = bf16_bits_to_f32(k_bf16).astype(np.float64)
+    v = bf16_bits_to_f32(v_bf16).astype(np.float64)
+    out = np.empty_like(q)
+    for h in range(q.shape[1]):
+        s = q[:, h, :] @ k[:, h, :].T / np.sqrt(128.0)
+        s -= s.max(axis=1, keepdims=True)
+        p = np.exp(s)
+        out[:, h, :] = (p / p.sum(axis=1, keepdims=True)) @ v[:, h, :]
+    return out

@@ -89,3 +89,41 @@ def dequant_nvfp4(q, bs, g, out_dtype):
     _check(lib().h3ref_dequant_nvfp4(_ptr(q), _ptr(bs), _ptr(g), _ptr(out), ctypes.c_ulonglong(rows),
                                      ctypes.c_ulonglong(2 * kp), okind, _stream()), "ref dequant_nvfp4")
     return out
+
+
+def col_mean(k):
+    """ColMean then / S (attn8.rs:429-455, :622), with the reference's atomicAdd chunk sums: f32 [H, 128]."""
+    import torch
+    S, H, _ = k.shape
+    acc = torch.zeros(H * 128, dtype=torch.float32, device=k.device)
+    _check(lib().h3ref_col_sum(_ptr(k), _ptr(acc), S, H * 128, _stream()), "ref col_sum")
+    return (acc * torch.tensor(1.0 / S, dtype=torch.float64).to(torch.float32).item()).reshape(H, 128)
+
+
+def quant_heads(x, mean=None):
+    """QuantHeads (attn8.rs:395-427): codes int8 [H, S, 128] and scales f32 [H, S]."""
+    import torch
+    S, H, _ = x.shape
+    codes = torch.empty((H, S, 128), dtype=torch.int8, device=x.device)
+    scales = torch.empty((H, S), dtype=torch.float32, device=x.device)
+    _check(lib().h3ref_quant_heads(_ptr(x), _ptr(mean), _ptr(codes), _ptr(scales), S, H, _stream()), "ref quant_heads")
+    return codes, scales
+
+
+def v_to_f16(src, row_stride: int, col_off: int, S: int, H: int):
+    """VToF16 (attn8.rs:457-486): [H, S, 128] f16."""
+    import torch
+    out = torch.empty((H, S, 128), dtype=torch.float16, device=src.device)
+    _check(lib().h3ref_v_to_f16(_ptr(src), ctypes.c_ulonglong(row_stride), ctypes.c_ulonglong(col_off), _ptr(out), S,
+                                H, _stream()), "ref v_to_f16")
+    return out
+
+
+def attn_qk8(q8, qs, k8, ks, v16, scale_log2: float):
+    """attn_qk8 (attn8.rs:107-246): codes [H, S, 128], scales [H, S], V f16 [H, S, 128] -> bf16 [S, H, 128]."""
+    import torch
+    H, S, _ = q8.shape
+    out = torch.empty((S, H, 128), dtype=torch.bfloat16, device=q8.device)
+    _check(lib().h3ref_attn_qk8(_ptr(q8), _ptr(qs), _ptr(k8), _ptr(ks), _ptr(v16), _ptr(out), S, H,
+                                ctypes.c_float(scale_log2), _stream()), "ref attn_qk8")
+    return out
