@@ -5,12 +5,13 @@
 //   out = bf16( sum_j f16(2^(p_j - m)) v_j / sum_j 2^(p_j - m) )
 // with keys >= S masked out; non-causal, no mask otherwise.
 //
-// One CTA per (head, 256 query rows) = two 128-row Q tiles; 320 threads:
+// One CTA per (head, 256 query rows) = two 128-row Q tiles; 384 threads:
 //   warp 0     one elected lane: TMA loads of the two Q tiles, then per 128-key tile the K codes (3-stage ring),
 //              the 128 key scales (1-D bulk copy, 4-stage ring) and the V^T tile (2-stage ring);
 //   warp 1     allocates 512 TMEM columns (S0, S1: int32 scores; O0, O1: f32 outputs) and issues the MMAs:
 //              S_t = Q_t K_j^T for the next key tile as soon as softmax t has read S_t, then O_t += P_t V_j;
-//   warps 2-5  softmax for Q tile 0, warps 6-9 for Q tile 1: thread = query row = TMEM lane.  Each reads its
+//   (warps 2-3 idle; warpgroup 0 runs with 88 registers per thread, the softmax warpgroups with 208)
+//   warps 4-7  softmax for Q tile 0, warps 8-11 for Q tile 1: thread = query row = TMEM lane.  Each reads its
 //              row's 128 scores, scales them by the key scales, takes the row maximum, writes
 //              P = 2^(s * qs' - m) as 16-bit values into shared memory (the K-major 128-byte-swizzle layout the
 //              MMA reads), and accumulates the row sum.  The running maximum m is only moved when a tile raises
@@ -36,7 +37,12 @@ constexpr int BN = 128;                 // keys per key tile
 constexpr int HD = 128;                 // head dim
 constexpr int NQ = 2;                   // Q tiles per CTA
 constexpr int KST = 3, VST = 2, SST = 4;
-constexpr int THREADS = 64 + NQ * 128;
+constexpr int THREADS = 128 + NQ * 128;  // warpgroup 0: loads + MMA; one softmax warpgroup per Q tile
+// Register split (setmaxnreg): launched at 168 per thread (384 x 168 = 64,512 of the 65,536), warpgroup 0 gives
+// back to 88 and the softmax warpgroups grow to 208: 128 x 88 + 256 x 208 = 64,512, and per SM sub-partition
+// (one warp of each warpgroup) 88 + 208 + 208 = 504 <= 512 registers per lane.  Neither side spills.
+constexpr int REGS_LOW = 88, REGS_HIGH = 208;
+static_assert(128 * REGS_LOW + NQ * 128 * REGS_HIGH <= THREADS * 168, "setmaxnreg split exceeds the launch");
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int Q_TILE = BM * HD;         // 16 KiB of int8 codes
 constexpr int K_TILE = BN * HD;         // 16 KiB
@@ -129,8 +135,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (warp == 0) {
-    if (elect_one()) {
+  if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(REGS_LOW));
+    if (warp == 0 && elect_one()) {
       // ------------------------------------------------------------------ TMA producer
       tma_prefetch_desc(&tmQ);
       tma_prefetch_desc(&tmK);
@@ -170,8 +177,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int j = last - VST + 1; j <= last; ++j)
         if (j >= 0) mbar_drain(&v_full[j % VST], (j / VST) & 1, p.err, kDevTimeoutDrain);
     }
-  } else if (warp == 1) {
-    if (elect_one()) {
+    if (warp == 1 && elect_one()) {
       // ------------------------------------------------------------------ MMA issuer
       constexpr uint32_t idq = idesc_i8(BM, BN);
       constexpr uint32_t idp = idesc_f16(BM, HD, BF16PV);
@@ -192,17 +198,20 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       for (int j = 0; ok && j < nkv; ++j) {
         const int jn = j + 1;
-        if (jn < nkv && !mbar_wait_bounded(&k_full[jn % KST], (jn / KST) & 1, abort_flag, p.err, kDevTimeoutFull)) break;
-        for (int t = 0; t < NQ && ok; ++t) {
-          if (jn < nkv) {
+        // next key tile's scores for both Q tiles first (each as soon as its softmax has read the current S),
+        // so neither softmax group waits behind the other group's P.V
+        if (jn < nkv) {
+          if (!mbar_wait_bounded(&k_full[jn % KST], (jn / KST) & 1, abort_flag, p.err, kDevTimeoutFull)) break;
+          for (int t = 0; t < NQ; ++t) {
             if (!mbar_wait_bounded(&s_free[t], j & 1, abort_flag, p.err, kDevTimeoutAccEmpty)) { ok = false; break; }
             tc_fence_after();
             issue_qk(t, jn);
           }
-          if (t == 0 && !mbar_wait_bounded(&v_full[j % VST], (j / VST) & 1, abort_flag, p.err, kDevTimeoutFull)) {
-            ok = false;
-            break;
-          }
+          if (!ok) break;
+          mma_commit(&k_empty[jn % KST]);
+        }
+        if (!mbar_wait_bounded(&v_full[j % VST], (j / VST) & 1, abort_flag, p.err, kDevTimeoutFull)) break;
+        for (int t = 0; t < NQ; ++t) {
           if (!mbar_wait_bounded(&p_full[t], j & 1, abort_flag, p.err, kDevTimeoutProbs)) { ok = false; break; }
           tc_fence_after();
           const uint8_t* pt = smem + OFF_P + t * P_TILE;
@@ -216,7 +225,6 @@ __global__ void __launch_bounds__(THREADS, 1)
           mma_commit(&pv_done[t]);
         }
         if (!ok) break;
-        if (jn < nkv) mma_commit(&k_empty[jn % KST]);
         mma_commit(&v_empty[j % VST]);
       }
       // every MMA this thread issued completes before TMEM is released
@@ -224,8 +232,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       mbar_drain(mma_done, 0, p.err, kDevTimeoutDrain);
     }
   } else {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(REGS_HIGH));
     // -------------------------------------------------------------------- softmax warps
-    const int g = (warp - 2) >> 2;        // Q tile of this warp
+    const int g = (warp - 4) >> 2;        // Q tile of this warp
     const int quarter = warp & 3;         // TMEM lane quarter the warp may access
     const int rloc = quarter * 32 + lane; // row within the Q tile
     const int row = (qb * NQ + g) * BM + rloc;
@@ -263,20 +272,38 @@ __global__ void __launch_bounds__(THREADS, 1)
         break;
       }
       const float4* ksm = reinterpret_cast<const float4*>(smem + OFF_SC + ss * BN * 4);
-      float s[BN];
-      float mx = -INFINITY;
+      // s = (float)acc * ks.  |acc| <= 128 * 127 * 127 < 2^22, so the bits of acc + 1.5 * 2^23 read as a float
+      // minus 1.5 * 2^23 is (float)acc exactly: an integer add and a paired subtract in place of the
+      // quarter-rate int-to-float conversion.
+      f2 s2[BN / 2];
+      const f2 magic = pk(12582912.f, 12582912.f);
 #pragma unroll
       for (int i4 = 0; i4 < BN / 4; ++i4) {
         const float4 kv = ksm[i4];
-        const float kk[4] = {kv.x, kv.y, kv.z, kv.w};
+        const int i = 4 * i4;
+        const f2 a = pk(__int_as_float((int)r[i >> 5][i & 31] + 0x4B400000),
+                        __int_as_float((int)r[(i + 1) >> 5][(i + 1) & 31] + 0x4B400000));
+        const f2 b = pk(__int_as_float((int)r[(i + 2) >> 5][(i + 2) & 31] + 0x4B400000),
+                        __int_as_float((int)r[(i + 3) >> 5][(i + 3) & 31] + 0x4B400000));
+        s2[2 * i4] = mul2(sub2(a, magic), pk(kv.x, kv.y));
+        s2[2 * i4 + 1] = mul2(sub2(b, magic), pk(kv.z, kv.w));
+      }
+      if (nvalid < BN) {  // the last key tile: keys >= S take no part
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int i = 4 * i4 + e;
-          const float v = i < nvalid ? __fmul_rn((float)(int)r[i >> 5][i & 31], kk[e]) : -INFINITY;
-          s[i] = v;
-          mx = fmaxf(mx, v);
+        for (int i2 = 0; i2 < BN / 2; ++i2) {
+          float lo, hi;
+          upk(s2[i2], lo, hi);
+          s2[i2] = pk(2 * i2 < nvalid ? lo : -INFINITY, 2 * i2 + 1 < nvalid ? hi : -INFINITY);
         }
       }
+      float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int i2 = 0; i2 < BN / 2; ++i2) {
+        float lo, hi;
+        upk(s2[i2], lo, hi);
+        mq[i2 & 3] = max3f(mq[i2 & 3], lo, hi);
+      }
+      const float mx = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3]));
       __syncwarp();
       if (lane == 0) mbar_arrive(&sc_empty[ss]);
       const float m_new = __fmul_rn(mx, qsl);
@@ -287,18 +314,24 @@ __global__ void __launch_bounds__(THREADS, 1)
         m_used = m_new;
       }
       l = __fmul_rn(l, alpha);
-      const float negm = -m_used;
-      uint32_t pk[BN / 2];
-      float l0 = 0.f, l1 = 0.f;
+      const f2 q2 = pk(qsl, qsl), nm2 = pk(-m_used, -m_used);
+      uint32_t pk16[BN / 2];
+      f2 la = pk(0.f, 0.f), lb = pk(0.f, 0.f);
 #pragma unroll
-      for (int i = 0; i < BN / 2; ++i) {
-        const float p0 = ex2(__fmaf_rn(s[2 * i], qsl, negm));
-        const float p1 = ex2(__fmaf_rn(s[2 * i + 1], qsl, negm));
-        l0 = __fadd_rn(l0, p0);
-        l1 = __fadd_rn(l1, p1);
-        pk[i] = pack_pv(p0, p1, BF16PV);
+      for (int i2 = 0; i2 < BN / 2; ++i2) {
+        float t0, t1;
+        upk(fma2(s2[i2], q2, nm2), t0, t1);
+        const float p0 = ex2(t0), p1 = ex2(t1);
+        if (i2 & 1) lb = add2(lb, pk(p0, p1));
+        else la = add2(la, pk(p0, p1));
+        pk16[i2] = pack_pv(p0, p1, BF16PV);
       }
-      l = __fadd_rn(l, __fadd_rn(l0, l1));
+      {
+        float a0, a1, b0, b1;
+        upk(la, a0, a1);
+        upk(lb, b0, b1);
+        l = __fadd_rn(l, __fadd_rn(__fadd_rn(a0, a1), __fadd_rn(b0, b1)));
+      }
       // P_g and O_g are free once the previous tile's P.V product has completed
       if (j > 0) {
         if (!__all_sync(0xffffffffu,
@@ -324,7 +357,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int sl = 0; sl < 2; ++sl)
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
-          const uint32_t* q4 = &pk[sl * 32 + c * 4];
+          const uint32_t* q4 = &pk16[sl * 32 + c * 4];
           sts128(prow + sl * P_SLAB + ((c ^ swz) << 4), q4[0], q4[1], q4[2], q4[3]);
         }
       fence_proxy_async_smem();

@@ -77,40 +77,6 @@ __device__ __forceinline__ void h4_inreg(float& a0, float& a1, float& a2, float&
   }
 }
 
-// Paired f32 arithmetic (sm_100 add/sub/mul/fma.f32x2): two independent IEEE-rounded operations per
-// instruction, each lane rounded exactly like the scalar instruction.
-struct f2 {
-  uint64_t v;
-};
-__device__ __forceinline__ f2 pk(float lo, float hi) {
-  f2 r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r.v) : "f"(lo), "f"(hi));
-  return r;
-}
-__device__ __forceinline__ void upk(f2 a, float& lo, float& hi) {
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(a.v));
-}
-__device__ __forceinline__ f2 add2(f2 a, f2 b) {
-  f2 r;
-  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
-  return r;
-}
-__device__ __forceinline__ f2 sub2(f2 a, f2 b) {
-  f2 r;
-  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
-  return r;
-}
-__device__ __forceinline__ f2 mul2(f2 a, f2 b) {
-  f2 r;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r.v) : "l"(a.v), "l"(b.v));
-  return r;
-}
-__device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) {
-  f2 r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r.v) : "l"(a.v), "l"(b.v), "l"(c.v));
-  return r;
-}
-
 // Digit-3 butterfly of two columns at once: a_p holds (column c, column c+1) for digit-3 value p.
 template <int ORDER>
 __device__ __forceinline__ void h4_pair(f2& a0, f2& a1, f2& a2, f2& a3) {
