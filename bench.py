@@ -307,7 +307,17 @@ def main() -> None:
     if ws_n > 1:
         import datetime
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+        # NCCL announces its version on stdout while the communicator is created; keep stdout for the JSON line
+        saved = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+            dist.barrier()
+            torch.cuda.synchronize()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved, 1)
+            os.close(saved)
     if not h3q.available_arch(local):
         raise SystemExit("bench.py: this library needs an sm_100 (B200) GPU")
 

@@ -10,7 +10,7 @@
 //              the 128 key scales (1-D bulk copy, 4-stage ring) and the V^T tile (2-stage ring);
 //   warp 1     allocates 512 TMEM columns (S0, S1: int32 scores; O0, O1: f32 outputs) and issues the MMAs:
 //              S_t = Q_t K_j^T for the next key tile as soon as softmax t has read S_t, then O_t += P_t V_j;
-//   (warps 2-3 idle; warpgroup 0 runs with 88 registers per thread, the softmax warpgroups with 208)
+//   (warps 2-3 idle; warpgroup 0 runs with 96 registers per thread, the softmax warpgroups with 200)
 //   warps 4-7  softmax for Q tile 0, warps 8-11 for Q tile 1: thread = query row = TMEM lane.  Each reads its
 //              row's 128 scores, scales them by the key scales, takes the row maximum, writes
 //              P = 2^(s * qs' - m) as 16-bit values into shared memory (the K-major 128-byte-swizzle layout the
@@ -39,9 +39,9 @@ constexpr int NQ = 2;                   // Q tiles per CTA
 constexpr int KST = 3, VST = 2, SST = 4;
 constexpr int THREADS = 128 + NQ * 128;  // warpgroup 0: loads + MMA; one softmax warpgroup per Q tile
 // Register split (setmaxnreg): launched at 168 per thread (384 x 168 = 64,512 of the 65,536), warpgroup 0 gives
-// back to 88 and the softmax warpgroups grow to 208: 128 x 88 + 256 x 208 = 64,512, and per SM sub-partition
-// (one warp of each warpgroup) 88 + 208 + 208 = 504 <= 512 registers per lane.  Neither side spills.
-constexpr int REGS_LOW = 88, REGS_HIGH = 208;
+// back to 96 and the softmax warpgroups grow to 200: 128 x 96 + 256 x 200 = 63,488 <= 64,512, and per SM
+// sub-partition (one warp of each warpgroup) 96 + 200 + 200 = 496 <= 512 registers per lane.  Neither side spills.
+constexpr int REGS_LOW = 96, REGS_HIGH = 200;
 static_assert(128 * REGS_LOW + NQ * 128 * REGS_HIGH <= THREADS * 168, "setmaxnreg split exceeds the launch");
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int Q_TILE = BM * HD;         // 16 KiB of int8 codes
