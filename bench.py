@@ -248,6 +248,72 @@ def attention_c4(dev, peaks: dict, reps: int = 5, S: int = 32760, H: int = 40) -
                     "burst, serial"}
 
 
+def _max_over_ranks(ms: float, dist, dev) -> float:
+    import torch
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def multi_gpu_extras(layers, M: int, dist, dev, reps: int = 3) -> dict:
+    """BASELINE config 4's other partitionings at N > 1 GPUs (all ranks take part; times are CUDA events, max over
+    ranks):
+      nsplit: the four c1 linears with the weight rows split over the ranks and the activations replicated
+              (M = 32760 in total, strong scaling); "fused" is one GEMM per rank writing its column block into
+              every rank's output over NVLink (h3q_gemm_s8_allgather), "nccl" a local GEMM + NCCL all-gather +
+              relayout;
+      attention: query-sharded c4 attention (S = 32760, H = 40 in total): K/V rows all-gathered, each rank attends
+              its 32760 / N queries (h3q_attention_rows)."""
+    import torch
+    import h3q
+    from h3q import parallel as P
+    world = dist.get_world_size()
+    rank = dist.get_rank()
+    res = {}
+    for fused in (True, False):
+        lins = [P.NSplitLinear(ly["w"], ly["ws"], ly["b"], fused=fused) for ly in layers]
+
+        def step():
+            for lin, ly in zip(lins, layers):
+                lin.forward(ly["x"])
+        step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = _max_over_ranks(e0.elapsed_time(e1) / reps, dist, dev)
+        res["fused" if fused else "nccl"] = {"ms_per_step": round(ms, 3),
+                                             "tops": round(ops_per_step(M) / (ms * 1e-3) / 1e12, 1)}
+        for lin in lins:
+            lin.close()
+        torch.cuda.synchronize()
+        dist.barrier()
+    S, H = 32760, 40
+    lo, hi = P.row_range(S, world, rank)
+    g = torch.Generator(device=dev).manual_seed(77 + rank)
+    q = torch.randn((hi - lo, H, 128), generator=g, device=dev).to(torch.bfloat16)
+    k = torch.randn((hi - lo, H, 128), generator=g, device=dev).to(torch.bfloat16)
+    v = torch.randn((hi - lo, H, 128), generator=g, device=dev).to(torch.bfloat16)
+    P.sharded_attention(q, k, v, S)
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        P.sharded_attention(q, k, v, S)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = _max_over_ranks(e0.elapsed_time(e1) / reps, dist, dev)
+    att = {"ms": round(ms, 3), "tops": round(4.0 * S * S * 128 * H / (ms * 1e-3) / 1e12, 1),
+           "note": "K/V all-gather + kmean/quant of the full K + attention of this rank's query rows"}
+    return {"nsplit_c1_linears": dict(res, workload="c1 linears, N split, M=32760 in total (strong scaling)"),
+            "attention_c4_query_sharded": att, "device_status": h3q.device_status(dev.index or 0)}
+
+
 def run_profile_case(args) -> None:
     """One fc1-shaped linear at 4096 tokens (A 21 MB, W 71 MB, out 113 MB: more than L2 in total, a few hundred
     MB on the device): warmup + steps launches of the quantizer and the GEMM, for ncu --set full captures."""
@@ -442,6 +508,7 @@ def main() -> None:
                "d2h_bytes_per_step": int(sum(h.numel() * 2 for h in host_o)), "ms_per_step": e_ms,
                "path": "h3q_gemm_s8 (C ABI) with pinned host input/output, copies inside the timed region"}
 
+    extras = multi_gpu_extras(layers, M, dist, dev) if dist is not None else None
     nv = nvfp4_c3(dev, load_peaks()) if rank == 0 else None
     att = attention_c4(dev, load_peaks()) if rank == 0 else None
 
@@ -473,6 +540,7 @@ def main() -> None:
         "per_linear": per_linear,
         "nvfp4_c3": nv,
         "attention_c4": att,
+        "multi_gpu": extras,
         "cpu_baseline": cb, "e2e": e2e, "clocks": clk.summary(),
         "gpu_launches": 2 * launches,
     }

@@ -78,11 +78,12 @@ __device__ __forceinline__ void sts128(uint32_t addr, uint32_t a, uint32_t b, ui
 }  // namespace
 
 struct AttnArgs {
-  const float* qs;     // [H, Sp] query scales
+  const float* qs;     // [H, Sqp] query scales
   const float* ks;     // [H, Sp] key scales
-  uint16_t* out;       // [S, H, 128] bf16
-  int32_t* scores;     // optional [H, S, S] int32 accumulators (diagnostic instantiation only)
-  int S, H, Sp, nqb;
+  uint16_t* out;       // [Sq, H, 128] bf16
+  int32_t* scores;     // optional [H, Sq, S] int32 accumulators (diagnostic instantiation only)
+  int S, H, Sp, nqb;   // keys, heads, padded keys, 256-row query blocks per head
+  int Sq, Sqp;         // query rows and their padded count (Sq == S unless the queries are a shard)
   float scale_log2;
   int* err;
 };
@@ -238,8 +239,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int quarter = warp & 3;         // TMEM lane quarter the warp may access
     const int rloc = quarter * 32 + lane; // row within the Q tile
     const int row = (qb * NQ + g) * BM + rloc;
-    const bool rv = row < p.S;
-    const float qsl = rv ? __fmul_rn(__ldg(p.qs + (int64_t)h * p.Sp + row), p.scale_log2) : p.scale_log2;
+    const bool rv = row < p.Sq;
+    const float qsl = rv ? __fmul_rn(__ldg(p.qs + (int64_t)h * p.Sqp + row), p.scale_log2) : p.scale_log2;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const uint32_t tS = tmem_base + lane_off + g * BN;
     const uint32_t tO = tmem_base + lane_off + NQ * BN + g * HD;
@@ -262,7 +263,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (lane == 0) mbar_arrive(&s_free[g]);
       const int nvalid = p.S - j * BN < BN ? p.S - j * BN : BN;
       if (DUMP && rv) {
-        int32_t* dst = p.scores + ((int64_t)h * p.S + row) * p.S + (int64_t)j * BN;
+        int32_t* dst = p.scores + ((int64_t)h * p.Sq + row) * p.S + (int64_t)j * BN;
         for (int i = 0; i < nvalid; ++i) dst[i] = (int32_t)r[i >> 5][i & 31];
       }
       const int ss = j % SST;
@@ -449,13 +450,13 @@ static cudaError_t launch_attn_variant(const CUtensorMap& tq, const CUtensorMap&
   return cudaGetLastError();
 }
 
-cudaError_t launch_attention(const int8_t* q8, const float* qs, const int8_t* k8, const float* ks,
+cudaError_t launch_attention(const int8_t* q8, const float* qs, int64_t Sq, const int8_t* k8, const float* ks,
                              const uint16_t* vt, uint16_t* out, int64_t S, int64_t H, bool bf16pv,
                              int32_t* scores, int* err, cudaStream_t st) {
-  if (S <= 0 || H <= 0) return cudaSuccess;
+  if (S <= 0 || Sq <= 0 || H <= 0) return cudaSuccess;
   const int64_t Sp = (S + 127) / 128 * 128;
   CUtensorMap tq, tk, tv;
-  if (!make_tmap_codes(&tq, q8, S, H) || !make_tmap_codes(&tk, k8, S, H) || !make_tmap_vt(&tv, vt, S, Sp, H))
+  if (!make_tmap_codes(&tq, q8, Sq, H) || !make_tmap_codes(&tk, k8, S, H) || !make_tmap_vt(&tv, vt, S, Sp, H))
     return cudaErrorInvalidValue;
   AttnArgs a{};
   a.qs = qs;
@@ -465,7 +466,9 @@ cudaError_t launch_attention(const int8_t* q8, const float* qs, const int8_t* k8
   a.S = (int)S;
   a.H = (int)H;
   a.Sp = (int)Sp;
-  a.nqb = (int)((S + NQ * BM - 1) / (NQ * BM));
+  a.Sq = (int)Sq;
+  a.Sqp = (int)((Sq + 127) / 128 * 128);
+  a.nqb = (int)((Sq + NQ * BM - 1) / (NQ * BM));
   a.scale_log2 = attn_scale_log2();
   a.err = err;
   if (scores) {

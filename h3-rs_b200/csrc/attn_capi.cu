@@ -15,7 +15,7 @@ cudaError_t launch_quant_heads(const uint16_t* x, const float* mean, int8_t* cod
                                int64_t H, bool block128, cudaStream_t st);
 cudaError_t launch_v_layout(const uint16_t* x, int64_t rs, int64_t col, uint16_t* vt, int64_t S, int64_t H,
                             bool keep_bf16, cudaStream_t st);
-cudaError_t launch_attention(const int8_t* q8, const float* qs, const int8_t* k8, const float* ks,
+cudaError_t launch_attention(const int8_t* q8, const float* qs, int64_t Sq, const int8_t* k8, const float* ks,
                              const uint16_t* vt, uint16_t* out, int64_t S, int64_t H, bool bf16pv,
                              int32_t* scores, int* err, cudaStream_t st);
 }  // namespace h3q
@@ -70,9 +70,9 @@ struct AttnWs {
   size_t bytes;
 };
 
-AttnWs carve(uint8_t* base, int64_t S, int64_t H) {
+AttnWs carve(uint8_t* base, int64_t Sq, int64_t S, int64_t H) {
   AttnWs w{};
-  const int64_t Sp = padded(S);
+  const int64_t Sp = padded(S), Sqp = padded(Sq);
   size_t off = 0;
   auto take = [&](size_t n) {
     uint8_t* p = base ? base + off : nullptr;
@@ -81,8 +81,8 @@ AttnWs carve(uint8_t* base, int64_t S, int64_t H) {
   };
   w.kmean = reinterpret_cast<float*>(take((size_t)H * HD * 4));
   w.part = reinterpret_cast<float*>(take(h3q::kmean_workspace_bytes(S, H)));
-  w.q8 = reinterpret_cast<int8_t*>(take((size_t)S * H * HD));
-  w.qs = reinterpret_cast<float*>(take((size_t)H * Sp * 4));
+  w.q8 = reinterpret_cast<int8_t*>(take((size_t)Sq * H * HD));
+  w.qs = reinterpret_cast<float*>(take((size_t)H * Sqp * 4));
   w.k8 = reinterpret_cast<int8_t*>(take((size_t)S * H * HD));
   w.ks = reinterpret_cast<float*>(take((size_t)H * Sp * 4));
   w.vt = reinterpret_cast<uint16_t*>(take((size_t)H * HD * Sp * 2));
@@ -90,21 +90,22 @@ AttnWs carve(uint8_t* base, int64_t S, int64_t H) {
   return w;
 }
 
-// attention_f16v (attn8.rs:617-627) with V given as rows of [S, rs] at column `col`.
-h3q_status run_attention(const uint16_t* q, const uint16_t* k, const uint16_t* vsrc, int64_t rs, int64_t col,
-                         uint16_t* out, int64_t S, int64_t H, int flags, void* workspace, size_t workspace_bytes,
-                         void* stream, const char* what) {
+// attention_f16v (attn8.rs:617-627) for Sq query rows against S keys, V given as rows of [S, rs] at column `col`.
+h3q_status run_attention(const uint16_t* q, int64_t Sq, const uint16_t* k, const uint16_t* vsrc, int64_t rs,
+                         int64_t col, uint16_t* out, int64_t S, int64_t H, int flags, void* workspace,
+                         size_t workspace_bytes, void* stream, const char* what) {
   if (h3q_status s = check_shape(S, H, what)) return s;
+  if (h3q_status s = check_shape(Sq, H, what)) return s;
   if (h3q_status s = check_flags(flags, what)) return s;
-  if (S == 0) return H3Q_OK;
+  if (S == 0 || Sq == 0) return H3Q_OK;
   if (!q || !k || !vsrc || !out) return fail(H3Q_ERR_ARG, "%s: null pointer", what);
   if (!aligned16(q) || !aligned16(k) || !aligned16(out))
     return fail(H3Q_ERR_ARG, "%s: q, k and out must be 16-byte aligned", what);
-  const AttnWs need = carve(nullptr, S, H);
+  const AttnWs need = carve(nullptr, Sq, S, H);
   if (!workspace || workspace_bytes < need.bytes)
     return fail(H3Q_ERR_WORKSPACE, "%s: workspace of %zu bytes, need %zu", what, workspace_bytes, need.bytes);
   if (!aligned16(workspace)) return fail(H3Q_ERR_ARG, "%s: workspace must be 16-byte aligned", what);
-  const AttnWs w = carve(static_cast<uint8_t*>(workspace), S, H);
+  const AttnWs w = carve(static_cast<uint8_t*>(workspace), Sq, S, H);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int* err = h3q::error_word_current();
   if (!err) return fail(H3Q_ERR_CUDA, "%s: could not set up the device error word", what);
@@ -112,10 +113,11 @@ h3q_status run_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v
   const bool bf16pv = (flags & H3Q_ATTN_PV_BF16) != 0;
   // smoothing K by its mean over tokens shifts every score of a query by the same amount (attn8.rs:620-621)
   if (h3q_status s = cuda_status(h3q::launch_kmean(k, S, H, w.kmean, w.part, st), what)) return s;
-  if (h3q_status s = cuda_status(h3q::launch_quant_heads(q, nullptr, w.q8, w.qs, S, H, block, st), what)) return s;
+  if (h3q_status s = cuda_status(h3q::launch_quant_heads(q, nullptr, w.q8, w.qs, Sq, H, block, st), what)) return s;
   if (h3q_status s = cuda_status(h3q::launch_quant_heads(k, w.kmean, w.k8, w.ks, S, H, block, st), what)) return s;
   if (h3q_status s = cuda_status(h3q::launch_v_layout(vsrc, rs, col, w.vt, S, H, bf16pv, st), what)) return s;
-  return cuda_status(h3q::launch_attention(w.q8, w.qs, w.k8, w.ks, w.vt, out, S, H, bf16pv, nullptr, err, st), what);
+  return cuda_status(h3q::launch_attention(w.q8, w.qs, Sq, w.k8, w.ks, w.vt, out, S, H, bf16pv, nullptr, err, st),
+                     what);
 }
 
 }  // namespace
@@ -129,12 +131,29 @@ int h3q_attention_available(int64_t head_dim, int x_kind, int device) {
 size_t h3q_attention_workspace_size(int64_t S, int64_t H, int flags) {
   (void)flags;
   if (S <= 0 || H <= 0) return 0;
-  return carve(nullptr, S, H).bytes;
+  return carve(nullptr, S, S, H).bytes;
+}
+
+size_t h3q_attention_rows_workspace_size(int64_t Sq, int64_t S, int64_t H, int flags) {
+  (void)flags;
+  if (S <= 0 || Sq <= 0 || H <= 0) return 0;
+  return carve(nullptr, Sq, S, H).bytes;
+}
+
+h3q_status h3q_attention_rows(const uint16_t* q, int64_t Sq, const uint16_t* k, const uint16_t* v_src,
+                              int64_t v_row_stride, int64_t v_col, uint16_t* out, int64_t S, int64_t H, int flags,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+  const char* what = "h3q_attention_rows";
+  if (v_col < 0 || v_row_stride < v_col + H * HD)
+    return fail(H3Q_ERR_ARG, "%s: V columns [%lld, %lld) outside a row of %lld elements", what, (long long)v_col,
+                (long long)(v_col + H * HD), (long long)v_row_stride);
+  return run_attention(q, Sq, k, v_src, v_row_stride, v_col, out, S, H, flags, workspace, workspace_bytes, stream,
+                       what);
 }
 
 h3q_status h3q_attention(const uint16_t* q, const uint16_t* k, const uint16_t* v, uint16_t* out, int64_t S,
                          int64_t H, int flags, void* workspace, size_t workspace_bytes, void* stream) {
-  return run_attention(q, k, v, H * HD, 0, out, S, H, flags, workspace, workspace_bytes, stream, "h3q_attention");
+  return run_attention(q, S, k, v, H * HD, 0, out, S, H, flags, workspace, workspace_bytes, stream, "h3q_attention");
 }
 
 h3q_status h3q_attention_qkv(const uint16_t* q, const uint16_t* k, const uint16_t* qkv, int64_t qkv_width,
@@ -144,7 +163,7 @@ h3q_status h3q_attention_qkv(const uint16_t* q, const uint16_t* k, const uint16_
   if (v_col < 0 || qkv_width < v_col + H * HD)
     return fail(H3Q_ERR_ARG, "%s: V columns [%lld, %lld) outside a qkv row of width %lld", what, (long long)v_col,
                 (long long)(v_col + H * HD), (long long)qkv_width);
-  return run_attention(q, k, qkv, qkv_width, v_col, out, S, H, flags, workspace, workspace_bytes, stream, what);
+  return run_attention(q, S, k, qkv, qkv_width, v_col, out, S, H, flags, workspace, workspace_bytes, stream, what);
 }
 
 size_t h3q_attn_kmean_workspace_size(int64_t S, int64_t H) { return h3q::kmean_workspace_bytes(S, H); }
@@ -207,7 +226,7 @@ h3q_status h3q_attention_core(const int8_t* q8, const float* qs, const int8_t* k
   if (scores && S > 8192) return fail(H3Q_ERR_ARG, "%s: the score dump is for S <= 8192", what);
   int* err = h3q::error_word_current();
   if (!err) return fail(H3Q_ERR_CUDA, "%s: could not set up the device error word", what);
-  return cuda_status(h3q::launch_attention(q8, qs, k8, ks, vt, out, S, H, (flags & H3Q_ATTN_PV_BF16) != 0, scores,
+  return cuda_status(h3q::launch_attention(q8, qs, S, k8, ks, vt, out, S, H, (flags & H3Q_ATTN_PV_BF16) != 0, scores,
                                            err, (cudaStream_t)stream),
                      what);
 }

@@ -58,8 +58,17 @@ __device__ __forceinline__ int pack_out(const float (&v)[32], int kind, uint32_t
 // One warp's TMA-store epilogue: each lane stages its row of a 32-row box into a swizzled shared-memory buffer
 // (the TMA swizzle of the box's row width W, which also makes the 16-byte writes bank-conflict free), then lane
 // 0 stores the box.  Two buffers alternate; a buffer is rewritten only after its previous store has read it.
+// Output tensor maps of a GEMM launch: one per destination buffer.  The all-gather GEMM stores every output box to
+// each rank's copy of the output (peer memory over NVLink); every other launch has one destination.
+template <int NDST>
+struct OutMaps {
+  CUtensorMap m[NDST];
+  int n;  // destinations in use (1..NDST)
+};
+
 struct EpiWarp {
-  const CUtensorMap* map;
+  const CUtensorMap* map;  // `nmaps` consecutive maps
+  int nmaps;
   uint8_t* buf;  // 2 * EPI_BUF bytes, 1024-aligned
   int sel;
   int lane;
@@ -76,7 +85,7 @@ struct EpiWarp {
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0 && do_store) {
-      tma_store_2d(map, buf + sel * EPI_BUF, x, y);
+      for (int d = 0; d < nmaps; ++d) tma_store_2d(map + d, buf + sel * EPI_BUF, x, y);
       bulk_commit();
     }
     sel ^= 1;
@@ -111,13 +120,14 @@ inline bool make_tmap_i8(CUtensorMap* m, const void* base, uint64_t rows, uint64
   return r == CUDA_SUCCESS;
 }
 
-// Output tensor map for the epilogue's TMA stores: [M, nout] row-major, box = (W / es) columns x 32 rows,
-// swizzle matching the box's row width W.
-inline bool make_tmap_out(CUtensorMap* m, void* base, uint64_t rows, uint64_t cols, int es, int W) {
+// Output tensor map for the epilogue's TMA stores: [M, nout] row-major (row pitch `pitch` elements, default nout),
+// box = (W / es) columns x 32 rows, swizzle matching the box's row width W.
+inline bool make_tmap_out(CUtensorMap* m, void* base, uint64_t rows, uint64_t cols, int es, int W,
+                          uint64_t pitch = 0) {
   auto fn = encode_fn();
   if (!fn) return false;
   cuuint64_t dims[2] = {cols, rows};
-  cuuint64_t strides[1] = {cols * (uint64_t)es};
+  cuuint64_t strides[1] = {(pitch ? pitch : cols) * (uint64_t)es};
   cuuint32_t box[2] = {(cuuint32_t)(W / es), 32};
   cuuint32_t estr[2] = {1, 1};
   const CUtensorMapDataType dt =

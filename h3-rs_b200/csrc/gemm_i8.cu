@@ -178,10 +178,10 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& p, EpiWarp& ew, ui
   }
 }
 
-template <int EPI, bool PAIR>
+template <int EPI, bool PAIR, int NDST>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_i8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmO, const GemmArgs p, int num_m, int num_n, int nk,
+                   const __grid_constant__ OutMaps<NDST> tmO, const GemmArgs p, int num_m, int num_n, int nk,
                    int group_m) {
   using C = GemmCfg<PAIR>;
   extern __shared__ uint8_t smem_raw[];
@@ -217,7 +217,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 0 && lane == 0 && nk > 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
-    tma_prefetch_desc(&tmO);
+    for (int d = 0; d < (NDST == 1 ? 1 : tmO.n); ++d) tma_prefetch_desc(&tmO.m[d]);
   }
   if (warp == 1) {
     if (PAIR) {
@@ -332,7 +332,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const bool ws_al = (reinterpret_cast<uintptr_t>(p.ws) & 15) == 0;
     const bool b_al = p.bias && (reinterpret_cast<uintptr_t>(p.bias) & 15) == 0;
-    EpiWarp ew{&tmO, sE + (warp - 2) * 2 * EPI_BUF, 0, lane};
+    EpiWarp ew{tmO.m, NDST == 1 ? 1 : tmO.n, sE + (warp - 2) * 2 * EPI_BUF, 0, lane};
     int it = 0;
     for (int t = unit; t < num_tiles; t += units, ++it) {
       const int acc = it & 1;
@@ -377,11 +377,11 @@ int sm_count(int device) {
   return cache[device];
 }
 
-template <int EPI, bool PAIR>
-static cudaError_t launch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+template <int EPI, bool PAIR, int NDST = 1>
+static cudaError_t launch_epi(const CUtensorMap& ta, const CUtensorMap& tb, const OutMaps<NDST>& to,
                               const GemmArgs& a, int num_m, int num_n, int nk, int group_m, cudaStream_t st) {
   using C = GemmCfg<PAIR>;
-  auto kern = gemm_i8_kernel<EPI, PAIR>;
+  auto kern = gemm_i8_kernel<EPI, PAIR, NDST>;
   static int grid_cache[64] = {0};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -433,7 +433,7 @@ static void out_geometry(const GemmArgs& a, int& es, int& W, int64_t& nout) {
 }
 
 template <bool PAIR>
-static cudaError_t launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+static cudaError_t launch_variant(const CUtensorMap& ta, const CUtensorMap& tb, const OutMaps<1>& to,
                                   const GemmArgs& a, int num_n, int nk, cudaStream_t st) {
   const int num_m = (int)((a.M + GemmCfg<PAIR>::kTileM - 1) / GemmCfg<PAIR>::kTileM);
   // L2 reuse (measured with ncu DRAM counters at the DiT shapes): a weight of up to ~32 MB stays resident while
@@ -467,8 +467,10 @@ cudaError_t launch_gemm_i8(const int8_t* A, const int8_t* B, const GemmArgs& a, 
   int es, W;
   int64_t nout;
   out_geometry(a, es, W, nout);
-  CUtensorMap ta, tb, to;
-  if (!make_tmap_out(&to, a.out, (uint64_t)a.M, (uint64_t)nout, es, W)) return cudaErrorInvalidValue;
+  CUtensorMap ta, tb;
+  OutMaps<1> to;
+  to.n = 1;
+  if (!make_tmap_out(&to.m[0], a.out, (uint64_t)a.M, (uint64_t)nout, es, W)) return cudaErrorInvalidValue;
   if (a.K > 0) {
     if (!make_tmap_i8(&ta, A, (uint64_t)a.M, (uint64_t)a.K, 128)) return cudaErrorInvalidValue;
     if (!make_tmap_i8(&tb, B, (uint64_t)a.N, (uint64_t)a.K, 128)) return cudaErrorInvalidValue;
@@ -481,6 +483,35 @@ cudaError_t launch_gemm_i8(const int8_t* A, const int8_t* B, const GemmArgs& a, 
   // 256-row pair tiles when there are at least two 128-row tiles of work, else one CTA per 128 x 256 tile
   if (a.M > 128) return launch_variant<true>(ta, tb, to, a, (int)ncols_tiles, nk, st);
   return launch_variant<false>(ta, tb, to, a, (int)ncols_tiles, nk, st);
+}
+
+
+// The local weight rows' output columns stored into every destination buffer (the N-split all-gather): outs[d] is
+// rank d's [M, n_total] bf16 output; this launch owns columns [n_offset, n_offset + a.N).  Each destination map
+// starts at that column block and is a.N columns wide, so the TMA stores clip at the block's edge.
+cudaError_t launch_gemm_i8_allgather(const int8_t* A, const int8_t* B, const GemmArgs& a, void* const* outs, int n_out,
+                                     int64_t n_total, int64_t n_offset, cudaStream_t st) {
+  if (a.M == 0 || a.N == 0) return cudaSuccess;
+  if (a.epi != kEpiLinear || a.out_kind != 2 || n_out < 1 || n_out > kMaxGatherRanks || a.K <= 0)
+    return cudaErrorInvalidValue;
+  OutMaps<kMaxGatherRanks> to;
+  to.n = n_out;
+  for (int d = 0; d < n_out; ++d) {
+    uint16_t* base = static_cast<uint16_t*>(outs[d]) + n_offset;
+    if (!make_tmap_out(&to.m[d], base, (uint64_t)a.M, (uint64_t)a.N, 2, 64, (uint64_t)n_total))
+      return cudaErrorInvalidValue;
+  }
+  CUtensorMap ta, tb;
+  if (!make_tmap_i8(&ta, A, (uint64_t)a.M, (uint64_t)a.K, 128)) return cudaErrorInvalidValue;
+  if (!make_tmap_i8(&tb, B, (uint64_t)a.N, (uint64_t)a.K, 128)) return cudaErrorInvalidValue;
+  const int nk = (int)((a.K + BK - 1) / BK);
+  const int num_n = (int)((a.N + 255) / 256);
+  if (a.M > 128) {
+    const int num_m = (int)((a.M + 255) / 256);
+    return launch_epi<kEpiLinear, true, kMaxGatherRanks>(ta, tb, to, a, num_m, num_n, nk, 1, st);
+  }
+  const int num_m = (int)((a.M + 127) / 128);
+  return launch_epi<kEpiLinear, false, kMaxGatherRanks>(ta, tb, to, a, num_m, num_n, nk, 1, st);
 }
 
 }  // namespace h3q

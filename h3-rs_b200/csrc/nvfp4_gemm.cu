@@ -272,7 +272,7 @@ __global__ void __launch_bounds__(NF_THREADS, 1)
   } else {
     // ------------------------------------------------------------------ epilogue warps 2..5 (both CTAs)
     const int q = warp & 3;
-    EpiWarp ew{&tmO, sE + (warp - 2) * 2 * EPI_BUF, 0, lane};
+    EpiWarp ew{&tmO, 1, sE + (warp - 2) * 2 * EPI_BUF, 0, lane};
     const bool partial = splits > 1;
     int it = 0;
     for (int u = unit0; u < num_units; u += units, ++it) {

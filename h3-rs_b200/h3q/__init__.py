@@ -69,7 +69,15 @@ SIGNATURES = {
     "h3q_attention_workspace_size": (_sz, [_i64, _i64, _int]),
     "h3q_attention": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _int, _vp, _sz, _vp]),
     "h3q_attention_qkv": (_int, [_vp, _vp, _vp, _i64, _i64, _vp, _i64, _i64, _int, _vp, _sz, _vp]),
+    "h3q_attention_rows_workspace_size": (_sz, [_i64, _i64, _i64, _int]),
+    "h3q_attention_rows": (_int, [_vp, _i64, _vp, _vp, _i64, _i64, _vp, _i64, _i64, _int, _vp, _sz, _vp]),
     "h3q_attn_kmean_workspace_size": (_sz, [_i64, _i64]),
+    "h3q_peer_buffer_alloc": (_int, [_sz, ctypes.POINTER(_vp), _vp]),
+    "h3q_peer_buffer_open": (_int, [_vp, ctypes.POINTER(_vp)]),
+    "h3q_peer_buffer_close": (_int, [_vp]),
+    "h3q_peer_buffer_free": (_int, [_vp]),
+    "h3q_gemm_s8_allgather": (_int, [_vp, _vp, _vp, _vp, _i64, _vp, ctypes.POINTER(_vp), _int, _i64, _i64, _i64,
+                                     _i64, _i64, _vp]),
     "h3q_attn_kmean": (_int, [_vp, _i64, _i64, _vp, _vp, _sz, _vp]),
     "h3q_attn_quant_heads": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _int, _vp]),
     "h3q_attn_v_layout": (_int, [_vp, _i64, _i64, _vp, _i64, _i64, _int, _vp]),
@@ -317,6 +325,21 @@ def attention_qkv(q, k, qkv, v_col: int, flags: int = 0):
     ws = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)
     check(lib().h3q_attention_qkv(_p(q), _p(k), _p(qkv), qkv.shape[1], v_col, _p(out), S, H, flags, _p(ws),
                                   ws.numel(), _stream(q.device)))
+    return out
+
+
+def attention_rows(q, k, v_src, v_row_stride: int, v_col: int, flags: int = 0):
+    """Attention of the query rows q [Sq, H, 128] against all keys k [S, H, 128] (V from rows of v_src [S, W] at
+    column v_col): the rows of attention() on the whole sequence that q covers."""
+    import torch
+    _cuda(q, k, v_src)
+    Sq, H, _ = q.shape
+    S = k.shape[0]
+    out = torch.empty_like(q)
+    need = lib().h3q_attention_rows_workspace_size(Sq, S, H, flags)
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)
+    check(lib().h3q_attention_rows(_p(q), Sq, _p(k), _p(v_src), v_row_stride, v_col, _p(out), S, H, flags, _p(ws),
+                                   ws.numel(), _stream(q.device)))
     return out
 
 

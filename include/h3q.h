@@ -220,6 +220,18 @@ h3q_status h3q_attention_qkv(const uint16_t* q, const uint16_t* k, const uint16_
                              int64_t v_col, uint16_t* out, int64_t S, int64_t H, int flags, void* workspace,
                              size_t workspace_bytes, void* stream);
 
+/* Workspace bytes of h3q_attention_rows. */
+size_t h3q_attention_rows_workspace_size(int64_t Sq, int64_t S, int64_t H, int flags);
+
+/* attention_qkv / attention for a block of Sq query rows against all S keys (no counterpart in the reference,
+ * which attends all rows at once): q bf16 [Sq, H, 128]; k bf16 [S, H, 128]; V from rows of v_src [S,
+ * v_row_stride] at column v_col (head h at v_col + 128 h) -> out bf16 [Sq, H, 128].  The rows of the result equal
+ * the matching rows of h3q_attention on the whole sequence (per-token scales; with H3Q_ATTN_SCALE_BLOCK128 the
+ * query blocks start at the first row of q).  It is the per-GPU step of query-sharded multi-GPU attention. */
+h3q_status h3q_attention_rows(const uint16_t* q, int64_t Sq, const uint16_t* k, const uint16_t* v_src,
+                              int64_t v_row_stride, int64_t v_col, uint16_t* out, int64_t S, int64_t H, int flags,
+                              void* workspace, size_t workspace_bytes, void* stream);
+
 /* The stages, for callers that keep the intermediates. */
 /* Workspace bytes of h3q_attn_kmean (the per-chunk column sums). */
 size_t h3q_attn_kmean_workspace_size(int64_t S, int64_t H);
@@ -240,6 +252,34 @@ h3q_status h3q_attn_v_layout(const uint16_t* src, int64_t row_stride, int64_t co
 h3q_status h3q_attention_core(const int8_t* q8, const float* qs, const int8_t* k8, const float* ks,
                               const uint16_t* vt, uint16_t* out, int64_t S, int64_t H, int flags, int32_t* scores,
                               void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------
+ * Multi-GPU on one node (one process per GPU).  The reference runs on one GPU; these serve the N-split form of
+ * the linear: every rank holds a block of weight rows (output columns) and the full activation, and each rank's
+ * GEMM writes its column block into every rank's copy of the [m, n_total] output over NVLink, so the all-gather
+ * happens inside the GEMM.  Buffers that peers write are shared through CUDA IPC handles, exchanged by the caller.
+ * ------------------------------------------------------------------------------------------------------- */
+#define H3Q_PEER_HANDLE_BYTES 64
+
+/* Allocates `bytes` of device memory on the current device (set-up, not the hot path) and writes its IPC handle
+ * (H3Q_PEER_HANDLE_BYTES bytes) to `handle`. */
+h3q_status h3q_peer_buffer_alloc(size_t bytes, void** ptr, void* handle);
+/* Maps another process's buffer from its handle into this process (a peer pointer this GPU can write). */
+h3q_status h3q_peer_buffer_open(const void* handle, void** ptr);
+/* Unmaps a buffer mapped by h3q_peer_buffer_open. */
+h3q_status h3q_peer_buffer_close(void* ptr);
+/* Frees a buffer from h3q_peer_buffer_alloc. */
+h3q_status h3q_peer_buffer_free(void* ptr);
+
+/* N-split linear step: quantized activations a [m, k] (scales xs [m]) times this rank's weight rows w_local
+ * [n_local, k] (scales ws_local, per row when ws_numel == n_local > 1; bias_local [n_local] or NULL), written as
+ * bf16 into columns [n_offset, n_offset + n_local) of every outs[r] ([m, n_total], r < n_ranks <= 8; outs[r] is
+ * rank r's buffer, this rank's own included).  Each output tile is computed once and stored to all ranks.  Ranks
+ * own disjoint column blocks; a cross-rank barrier after the call (stream-ordered) makes the full output
+ * readable.  n_offset and n_total must be multiples of 8; k % 16 == 0. */
+h3q_status h3q_gemm_s8_allgather(const int8_t* a, const float* xs, const int8_t* w_local, const float* ws_local,
+                                 int64_t ws_numel, const float* bias_local, void* const* outs, int n_ranks, int64_t m,
+                                 int64_t n_total, int64_t n_offset, int64_t n_local, int64_t k, void* stream);
 
 /* h3q_gemm_s8 for callers that cannot allocate device memory (no counterpart in the reference).  Some callers
  * cannot call cudaMalloc: a plugin inside a host that has already reserved the GPU's whole memory for its own

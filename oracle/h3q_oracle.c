@@ -653,12 +653,13 @@ H3O_API float h3o_attn_scale_log2(void) {
  *   out = bf16(o * (1 / l))
  * V is taken from rows of src (bf16, row stride v_rs elements, head h at column v_col + 128 h) and rounded to f16
  * as v_to_f16 does (attn8.rs:55-65), or kept in bf16 with P rounded to bf16 (pv_bf16).  exp2f stands in for
- * ex2.approx; sums run in a fixed order.  Output bf16 [S, H, 128].
+ * ex2.approx; sums run in a fixed order.  Queries: Sq rows (codes [H, Sq, 128], scales [H, roundup(Sq, 128)]);
+ * keys and values: S rows.  Output bf16 [Sq, H, 128].
  */
-H3O_API void h3o_attn_forward(const int8_t* q8, const float* qs, const int8_t* k8, const float* ks,
-                              const uint16_t* vsrc, int64_t v_rs, int64_t v_col, uint16_t* out, int64_t S, int64_t H,
-                              int pv_bf16) {
-    const int64_t Sp = (S + 127) / 128 * 128;
+H3O_API void h3o_attn_forward_rows(const int8_t* q8, const float* qs, int64_t Sq, const int8_t* k8, const float* ks,
+                                   const uint16_t* vsrc, int64_t v_rs, int64_t v_col, uint16_t* out, int64_t S,
+                                   int64_t H, int pv_bf16) {
+    const int64_t Sp = (S + 127) / 128 * 128, Sqp = (Sq + 127) / 128 * 128;
     const float sl2 = h3o_attn_scale_log2();
     float* vv = (float*)malloc((size_t)S * 128 * sizeof(float));
     float p[64], o[128];
@@ -668,9 +669,9 @@ H3O_API void h3o_attn_forward(const int8_t* q8, const float* qs, const int8_t* k
                 const uint16_t b = vsrc[s * v_rs + v_col + h * 128 + d];
                 vv[s * 128 + d] = pv_bf16 ? bf2f(b) : h2f(f2h(bf2f(b)));
             }
-        for (int64_t i = 0; i < S; ++i) {
-            const int8_t* a = q8 + (h * S + i) * 128;
-            const float qs0 = qs[h * Sp + i] * sl2;
+        for (int64_t i = 0; i < Sq; ++i) {
+            const int8_t* a = q8 + (h * Sq + i) * 128;
+            const float qs0 = qs[h * Sqp + i] * sl2;
             float m = -INFINITY, l = 0.f;
             for (int d = 0; d < 128; ++d) o[d] = 0.f;
             for (int64_t j0 = 0; j0 < S; j0 += 64) {
@@ -703,4 +704,11 @@ H3O_API void h3o_attn_forward(const int8_t* q8, const float* qs, const int8_t* k
         }
     }
     free(vv);
+}
+
+/* the whole sequence: Sq == S */
+H3O_API void h3o_attn_forward(const int8_t* q8, const float* qs, const int8_t* k8, const float* ks,
+                              const uint16_t* vsrc, int64_t v_rs, int64_t v_col, uint16_t* out, int64_t S, int64_t H,
+                              int pv_bf16) {
+    h3o_attn_forward_rows(q8, qs, S, k8, ks, vsrc, v_rs, v_col, out, S, H, pv_bf16);
 }

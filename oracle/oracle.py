@@ -387,6 +387,31 @@ def attn_forward(q8, qs, k8, ks, vsrc_bf16, v_rs: int, v_col: int, pv_bf16: bool
     return out
 
 
+def attn_forward_rows(q8, qs, k8, ks, vsrc_bf16, v_rs: int, v_col: int, pv_bf16: bool = False) -> np.ndarray:
+    """attn_forward for Sq query rows (codes [H, Sq, 128], scales [H, roundup(Sq, 128)]) against S keys.
+    bf16 bits [Sq, H, 128]."""
+    H, Sq = q8.shape[0], q8.shape[1]
+    S = k8.shape[1]
+    out = np.empty((Sq, H, 128), dtype=np.uint16)
+    v = np.ascontiguousarray(vsrc_bf16, dtype=np.uint16)
+    lib().h3o_attn_forward_rows(_p(np.ascontiguousarray(q8)), _p(np.ascontiguousarray(qs, dtype=np.float32)),
+                                c_i64(Sq), _p(np.ascontiguousarray(k8)),
+                                _p(np.ascontiguousarray(ks, dtype=np.float32)), _p(v), c_i64(v_rs), c_i64(v_col),
+                                _p(out), c_i64(S), c_i64(H), c_int(1 if pv_bf16 else 0))
+    return out
+
+
+def attention_rows(q_bf16, k_bf16, v_bf16, flags: int = 0) -> np.ndarray:
+    """h3q_attention_rows: query rows q [Sq, H, 128] against keys / values [S, H, 128]; bf16 bits [Sq, H, 128]."""
+    S, H = k_bf16.shape[0], k_bf16.shape[1]
+    block = bool(flags & ATTN_SCALE_BLOCK128)
+    km = attn_kmean(k_bf16)
+    q8, qs = attn_quant_heads(q_bf16, None, block)
+    k8, ks = attn_quant_heads(k_bf16, km, block)
+    return attn_forward_rows(q8, qs, k8, ks, np.ascontiguousarray(v_bf16).reshape(S, H * 128), H * 128, 0,
+                             bool(flags & ATTN_PV_BF16))
+
+
 def attention(q_bf16, k_bf16, v_bf16, flags: int = 0) -> np.ndarray:
     """attention(q, k, v) (attn8.rs:611-627): K mean, Q / K quantisation, int8 attention.  bf16 bits [S, H, 128]."""
     S, H = q_bf16.shape[0], q_bf16.shape[1]

@@ -188,3 +188,16 @@ def test_attention_rejects_bad_arguments(cuda):
     qkv = torch.zeros((S, 3 * 128), dtype=torch.bfloat16, device=cuda)
     with pytest.raises(h3q.H3QError):
         h3q.attention_qkv(x, x, qkv, 3 * 128 - 64)
+
+
+@pytest.mark.parametrize("lo,hi", [(0, 300), (100, 357), (513, 1000), (999, 1000)])
+def test_attention_rows_equal_whole_sequence_rows(cuda, lo, hi):
+    """A block of query rows against all keys gives exactly those rows of the whole-sequence attention, and the
+    oracle's restatement of it."""
+    S, H = 1000, 2
+    (q, k, v), (tq, tk, tv) = _inputs(25, S, H, cuda)
+    full = h3q.attention(tq, tk, tv)
+    part = h3q.attention_rows(tq[lo:hi].contiguous(), tk, tv.reshape(S, H * 128), H * 128, 0)
+    assert torch.equal(part.view(torch.int16), full[lo:hi].view(torch.int16))
+    ref = O.attention_rows(q[lo:hi], k, v)
+    assert O.max_abs_rel(O.bf16_bits_to_f32(bf16_bits(part)), O.bf16_bits_to_f32(ref)) <= TOL
