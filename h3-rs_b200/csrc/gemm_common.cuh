@@ -84,8 +84,11 @@ struct EpiWarp {
         *reinterpret_cast<uint4*>(b + ((i ^ sw) << 4)) = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
     fence_proxy_async_smem();
     __syncwarp();
-    if (lane == 0 && do_store) {
-      for (int d = 0; d < nmaps; ++d) tma_store_2d(map + d, buf + sel * EPI_BUF, x, y);
+    // one bulk group per call, empty when the box lies outside the output: the wait at the top of the next call
+    // that reuses this buffer then always covers the store that last read it
+    if (lane == 0) {
+      if (do_store)
+        for (int d = 0; d < nmaps; ++d) tma_store_2d(map + d, buf + sel * EPI_BUF, x, y);
       bulk_commit();
     }
     sel ^= 1;

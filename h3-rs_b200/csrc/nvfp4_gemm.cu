@@ -14,10 +14,11 @@
 //   warp 1      TMEM allocation; in the leader CTA, one thread issues the pair MMAs;
 //   warps 2-5   epilogue (TMEM -> bf16 or f32 split-K partials -> TMA store);
 //   warps 6-13  decoders: 256 threads, each turning half of one weight row (32 of the stage's 64 codes) into
-//               bf16, written straight into the 128-byte-swizzled K-major layout the MMA reads; after a named
-//               barrier one thread per CTA signals the leader (two arrivals per stage in all).  Decode per pair of codes: cvt e2m1x2 ->
-//               f16x2, f16x2 multiply by the e4m3 scale (exact: at most 5 significant bits), widen to f32,
-//               multiply by the global scale, round to bf16 -- the same rounding as the reference's dequant.
+//               bf16, written straight into the 128-byte-swizzled K-major layout the MMA reads; each decoder
+//               warp then signals the leader's stage barrier itself (16 arrivals per stage), with no barrier
+//               among the decoders.  Decode per pair of codes: cvt e2m1x2 -> f16x2, f16x2 multiply by the e4m3
+//               scale (exact: at most 5 significant bits), widen to f32, multiply by the global scale, round to
+//               bf16 -- the same rounding as the reference's dequant.
 // Split-K (units = tiles x splits) keeps all SMs busy for narrow outputs; partials are summed in a fixed order.
 #include <cstdarg>
 #include <cstdint>
@@ -127,7 +128,7 @@ __global__ void __launch_bounds__(NF_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < NF_STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&decd[s], 2);
+      mbar_init(&decd[s], 16);  // every decoder warp of both CTAs
       mbar_init(&empty[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -243,7 +244,7 @@ __global__ void __launch_bounds__(NF_THREADS, 1)
       bool ok = true;
       for (int kb = kb0; kb < kb1; ++kb) {
         const bool landed = mbar_wait_bounded(&full[stage], phase, abort_flag, p.err, kDevTimeoutFull);
-        if (!bar_and(1, 256, landed)) { ok = false; break; }  // all decoder threads give up together
+        if (!__all_sync(0xffffffffu, landed)) { ok = false; break; }
         const uint4 qv = *reinterpret_cast<const uint4*>(sBR + stage * NF_BR + r * 32 + 16 * h);
         const uint32_t sc2b =
             *reinterpret_cast<const uint16_t*>(sSC + stage * NF_SC + (r % 32) * 16 + (r / 32) * 4 + 2 * h);
@@ -260,8 +261,8 @@ __global__ void __launch_bounds__(NF_THREADS, 1)
           *reinterpret_cast<uint4*>(bd + (((2 * blk + 1) ^ (r & 7)) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
         }
         fence_proxy_async_smem();
-        asm volatile("bar.sync 1, 256;" ::: "memory");  // all 8 decoder warps of this CTA are done with the stage
-        if (d == 0) {
+        __syncwarp();
+        if (lane == 0) {  // this warp's rows are in place: one arrival per decoder warp on the leader's barrier
           if (leader) mbar_arrive(&decd[stage]);
           else mbar_arrive_cluster(decd_leader0 + (uint32_t)(stage * sizeof(uint64_t)));
         }
@@ -355,8 +356,11 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, const float
   }
 }
 
-// Split count that best fills the co-resident pairs (at most 4, at least 8 k-blocks per split).
+// Split count that best fills the co-resident pairs (at most 4, at least 8 k-blocks per split).  Splitting costs
+// an f32 partial per split and output element (written, then read back by the reduction), so it is used only
+// when the tiles do not fill one wave of pairs.
 static int choose_splits(int tiles, int pairs, int nk) {
+  if (tiles >= pairs) return 1;
   int best = 1;
   double best_eff = 0.0;
   for (int s = 1; s <= 4; ++s) {

@@ -39,7 +39,8 @@ def test_acc_extreme_codes(cuda):
     assert np.all(acc[:, 0::2] == 128 * 128 * K) and np.all(acc[:, 1::2] == -128 * 127 * K)
 
 
-@pytest.mark.parametrize("M,K,N", [(256, 1024, 1024), (77, 5120, 512), (129, 13824, 256), (1, 256, 16)])
+@pytest.mark.parametrize("M,K,N", [(256, 1024, 1024), (77, 5120, 512), (129, 13824, 256), (1, 256, 16),
+                                   (300, 2048, 384), (512, 1024, 640)])
 @pytest.mark.parametrize("rotate", [True, False])
 def test_gemm_s8_bit_exact_vs_oracle(cuda, M, K, N, rotate):
     (x, w, ws, bias), (xd, wd, wsd, bd) = linear_inputs(M + N, M, K, N, cuda)

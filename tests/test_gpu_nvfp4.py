@@ -45,7 +45,8 @@ def test_kat_weights_through_the_linear(cuda):
 
 
 @pytest.mark.parametrize("M,K,N,awq,bias", [(300, 1024, 1024, True, True), (77, 512, 384, False, True),
-                                            (512, 4096, 512, True, False), (1, 256, 256, True, True)])
+                                            (512, 4096, 512, True, False), (1, 256, 256, True, True),
+                                            (300, 2048, 384, True, True), (512, 2048, 384, True, False)])
 def test_linear_matches_reference_composition(cuda, M, K, N, awq, bias):
     x, q, bs, g, pqs, b = O.make_nvfp4_inputs(M + N, M, K, N)
     y = O.bf16_bits_to_f32(bf16_bits(_run(x, q, bs, g, pqs if awq else None, b if bias else None, cuda)))
