@@ -264,7 +264,7 @@ __global__ void __launch_bounds__(NF_THREADS, 1)
         __syncwarp();
         if (lane == 0) {  // this warp's rows are in place: one arrival per decoder warp on the leader's barrier
           if (leader) mbar_arrive(&decd[stage]);
-          else mbar_arrive_cluster(decd_leader0 + (uint32_t)(stage * sizeof(uint64_t)));
+          else mbar_arrive_remote_own_data(decd_leader0 + (uint32_t)(stage * sizeof(uint64_t)));
         }
         if (++stage == NF_STAGES) { stage = 0; phase ^= 1; }
       }

@@ -254,6 +254,15 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
 }
 
+// Arrive on a barrier of another CTA of the cluster with CTA-scope release (the default `mbarrier.arrive`
+// semantics), for a producer whose data stays in its own CTA's shared memory and is read by its own SM: the
+// operand halves of a cta_group::2 MMA.  The caller first orders its shared-memory stores for the tensor core with
+// fence.proxy.async; no cluster-wide fence is needed, and none is paid (a .release.cluster arrive per warp and
+// pipeline stage costs more than the MMA it feeds).
+__device__ __forceinline__ void mbar_arrive_remote_own_data(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
 // ------------------------------------------------------------------------------------------------ tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t* smem_dst, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_dst)),
