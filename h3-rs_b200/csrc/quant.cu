@@ -108,19 +108,6 @@ __device__ __forceinline__ uint32_t code_of(float t) {
   return (ORDER == 2 && t != t) ? 0u : b;
 }
 
-// Digits 0..2 of the thread's 64 values, in registers (element c has digits c&3, (c>>2)&3, (c>>4)&3).
-template <int ORDER>
-__device__ __forceinline__ void rotate_inreg(float (&v)[64]) {
-#pragma unroll
-  for (int d = 0, st = 1; d < 3; ++d, st *= 4) {
-#pragma unroll
-    for (int b = 0; b < 64; ++b) {
-      if ((b / st) % 4 != 0) continue;
-      h4_inreg<ORDER>(v[b], v[b + st], v[b + 2 * st], v[b + 3 * st], d == 0);
-    }
-  }
-}
-
 // Persistent row quantizer.  One CTA = one team of roundup(4G, 32) threads working through rows
 // blockIdx.x, blockIdx.x + gridDim.x, ...; thread t < 4G owns elements [64t, 64t + 64) of the row.  Rows arrive
 // by TMA (the row viewed as [K*es/128] x 128-byte lines, 128-byte swizzle) into a 3-stage ring, two rows ahead
@@ -138,7 +125,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
   // align by offsetting the __shared__ array itself, so the compiler keeps shared-space (LDS/STS) accesses
   uint8_t* qsm = qsm_raw + ((1024u - (smem_u32(qsm_raw) & 1023u)) & 1023u);
   __shared__ uint64_t full[kQStages];
-  __shared__ unsigned s_max[3];
+  __shared__ unsigned s_max[3], s_max2[3];
   __shared__ int s_abort;
   constexpr int ES = sizeof(Tin);
   constexpr int LINES = 64 * ES / 128;  // 128-byte lines per thread: 1 (16-bit) or 2 (f32)
@@ -151,6 +138,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
   if (t == 0) {
     for (int s = 0; s < kQStages; ++s) mbar_init(&full[s], 1);
     s_max[0] = s_max[1] = s_max[2] = 0u;
+    s_max2[0] = s_max2[1] = s_max2[2] = 0u;
     s_abort = 0;
     fence_barrier_init();
   }
@@ -173,7 +161,9 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
     const int stage = it % kQStages;
     const bool landed = mbar_wait_bounded(&full[stage], (uint32_t)(it / kQStages) & 1u, &s_abort, err, kDevTimeoutFull);
     if (!__syncthreads_and(landed)) break;  // the whole CTA gives up together (barriers follow)
-    float v[64];
+    // The thread's 64 values as 32 register pairs: v2[k] = elements (2k, 2k + 1).  Pairs of neighbouring elements
+    // follow the same butterfly through digits 1..3, so those stages run as paired f32x2 operations.
+    f2 v2[32];
     if (owner) {
       const uint8_t* base = qsm + (size_t)stage * stage_bytes;
 #pragma unroll
@@ -182,19 +172,40 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
 #pragma unroll
         for (int c = 0; c < 8; ++c) {
           const uint4 raw = *reinterpret_cast<const uint4*>(base + line * 128 + ((c ^ (line & 7)) << 4));
-          In<Tin>::cvt(raw, v + (l * 8 + c) * In<Tin>::kVec);
+          float tmp[In<Tin>::kVec];
+          In<Tin>::cvt(raw, tmp);
+#pragma unroll
+          for (int i = 0; i < In<Tin>::kVec / 2; ++i)
+            v2[((l * 8 + c) * In<Tin>::kVec) / 2 + i] = pk(tmp[2 * i], tmp[2 * i + 1]);
         }
       }
     } else {
 #pragma unroll
-      for (int c = 0; c < 64; ++c) v[c] = 0.f;
+      for (int k = 0; k < 32; ++k) v2[k] = pk(0.f, 0.f);
     }
     // Digit 3 crosses the quad.  Transpose through shared memory in two rounds of 32 columns, each thread
     // writing into its own (already consumed) 128-byte line of this stage: afterwards thread j holds, for all
     // four digit-3 values, columns 8j..8j+7 (round 0) and 32+8j..32+8j+7 (round 1) of its group.
-    float u[4][16];  // u[d3][i]
+    f2 u2[4][8];  // u2[d3][i] = columns (2i, 2i + 1) of the thread's two 8-column slices, in round order
     if (ORDER != 0) {
-      rotate_inreg<ORDER>(v);
+      // digit 0 (element offsets 1): within a pair, so scalar, with the reference's first-stage sum order
+#pragma unroll
+      for (int b4 = 0; b4 < 16; ++b4) {
+        float a0, a1, a2, a3;
+        upk(v2[2 * b4], a0, a1);
+        upk(v2[2 * b4 + 1], a2, a3);
+        h4_inreg<ORDER>(a0, a1, a2, a3, true);
+        v2[2 * b4] = pk(a0, a1);
+        v2[2 * b4 + 1] = pk(a2, a3);
+      }
+      // digit 1 (element offsets 4 = pair offsets 2) and digit 2 (offsets 16 = pair offsets 8), paired
+#pragma unroll
+      for (int blk = 0; blk < 4; ++blk)
+#pragma unroll
+        for (int k = 0; k < 2; ++k)
+          h4_pair<ORDER>(v2[8 * blk + k], v2[8 * blk + k + 2], v2[8 * blk + k + 4], v2[8 * blk + k + 6]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) h4_pair<ORDER>(v2[k], v2[k + 8], v2[k + 16], v2[k + 24]);
       uint8_t* xb = qsm + (size_t)stage * stage_bytes;
       uint8_t* own = xb + (size_t)t * LINES * 128;
       const int fo = xslot(t);
@@ -202,9 +213,12 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
       for (int r = 0; r < 2; ++r) {
         if (owner) {
 #pragma unroll
-          for (int c = 0; c < 8; ++c)
-            *reinterpret_cast<float4*>(own + ((c ^ fo) << 4)) =
-                make_float4(v[32 * r + 4 * c], v[32 * r + 4 * c + 1], v[32 * r + 4 * c + 2], v[32 * r + 4 * c + 3]);
+          for (int c = 0; c < 8; ++c) {
+            float x0, x1, x2, x3;
+            upk(v2[16 * r + 2 * c], x0, x1);
+            upk(v2[16 * r + 2 * c + 1], x2, x3);
+            *reinterpret_cast<float4*>(own + ((c ^ fo) << 4)) = make_float4(x0, x1, x2, x3);
+          }
         }
         __syncwarp();
         if (owner) {
@@ -216,39 +230,39 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
               const float4 f = *reinterpret_cast<const float4*>(line + (((2 * j + e) ^ fp) << 4));
-              u[d3][8 * r + 4 * e] = f.x; u[d3][8 * r + 4 * e + 1] = f.y;
-              u[d3][8 * r + 4 * e + 2] = f.z; u[d3][8 * r + 4 * e + 3] = f.w;
+              u2[d3][4 * r + 2 * e] = pk(f.x, f.y);
+              u2[d3][4 * r + 2 * e + 1] = pk(f.z, f.w);
             }
           }
         } else {
 #pragma unroll
           for (int d3 = 0; d3 < 4; ++d3)
 #pragma unroll
-            for (int i = 0; i < 8; ++i) u[d3][8 * r + i] = 0.f;
+            for (int i = 0; i < 4; ++i) u2[d3][4 * r + i] = pk(0.f, 0.f);
         }
         __syncwarp();
       }
       fence_proxy_async_smem();  // these generic writes precede a later TMA refill of the stage
 #pragma unroll
-      for (int i = 0; i < 16; i += 2) {
-        f2 a0 = pk(u[0][i], u[0][i + 1]), a1 = pk(u[1][i], u[1][i + 1]);
-        f2 a2 = pk(u[2][i], u[2][i + 1]), a3 = pk(u[3][i], u[3][i + 1]);
-        h4_pair<ORDER>(a0, a1, a2, a3);
-        upk(a0, u[0][i], u[0][i + 1]); upk(a1, u[1][i], u[1][i + 1]);
-        upk(a2, u[2][i], u[2][i + 1]); upk(a3, u[3][i], u[3][i + 1]);
-      }
+      for (int i = 0; i < 8; ++i) h4_pair<ORDER>(u2[0][i], u2[1][i], u2[2][i], u2[3][i]);
     } else {
 #pragma unroll
       for (int d3 = 0; d3 < 4; ++d3)
 #pragma unroll
-        for (int i = 0; i < 16; ++i) u[d3][i] = v[16 * d3 + i];
+        for (int i = 0; i < 8; ++i) u2[d3][i] = v2[8 * d3 + i];
     }
+    // Row maximum of |v|, NaN-propagating: rows holding an Inf or NaN (max bits >= the Inf pattern) take the exact
+    // slow path below; every other row needs neither the NaN-ignoring max nor per-element NaN / clamp selects.
     float m = 0.f;
     if (!ROT_ONLY) {
 #pragma unroll
       for (int d3 = 0; d3 < 4; ++d3)
 #pragma unroll
-        for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(u[d3][i]));
+        for (int i = 0; i < 8; ++i) {
+          float x0, x1;
+          upk(u2[d3][i], x0, x1);
+          asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(m), "f"(fabsf(x0)), "f"(fabsf(x1)));
+        }
     }
     const unsigned mw = __reduce_max_sync(0xffffffffu, __float_as_uint(m));
     const int slot = it % 3;
@@ -256,49 +270,80 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
     __syncthreads();  // the whole row is read out of `stage` and its max is complete
     if (t == 0) {
       s_max[(it + 1) % 3] = 0u;
+      s_max2[(it + 1) % 3] = 0u;
       const int64_t nr = row + (int64_t)kQStages * gridDim.x;
       if (nr < M) {
         fence_proxy_async_smem();
         issue(nr, stage);
       }
     }
+    unsigned mbits = s_max[slot];
+    const bool special = !ROT_ONLY && mbits >= 0x7f800000u;  // the same for every thread of the CTA
+    if (special) {
+      // the reference's max ignores NaN (fmaxf): reduce again without them
+      float mf = 0.f;
+#pragma unroll
+      for (int d3 = 0; d3 < 4; ++d3)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float x0, x1;
+          upk(u2[d3][i], x0, x1);
+          mf = fmaxf(mf, fmaxf(fabsf(x0), fabsf(x1)));
+        }
+      const unsigned mw2 = __reduce_max_sync(0xffffffffu, __float_as_uint(mf));
+      if ((t & 31) == 0) atomicMax(&s_max2[slot], mw2);
+      __syncthreads();
+      mbits = s_max2[slot];
+    }
     // scale from the true max (the 1/16 of the rotation is folded in exactly: powers of two)
-    const float mx = ORDER == 0 ? __uint_as_float(s_max[slot]) : __fmul_rn(__uint_as_float(s_max[slot]), 0.0625f);
+    const float mx = ORDER == 0 ? __uint_as_float(mbits) : __fmul_rn(__uint_as_float(mbits), 0.0625f);
     const float s = fmaxf(__fdiv_rn(mx, 127.f), 1e-30f);
     const float inv = ORDER == 0 ? __fdiv_rn(1.f, s) : __fmul_rn(__fdiv_rn(1.f, s), 0.0625f);
     if (ROT_ONLY) {
       if (owner) {
         uint16_t* dst = ybf + row * (int64_t)K + (t >> 2) * 256 + 8 * j;
+        const f2 q16 = pk(0.0625f, 0.0625f);
 #pragma unroll
         for (int h = 0; h < 8; ++h) {
-          const int d3 = h >> 1, i0 = 8 * (h & 1);
-          uint4 o;
-          o.x = pack_bf2(__fmul_rn(u[d3][i0], 0.0625f), __fmul_rn(u[d3][i0 + 1], 0.0625f));
-          o.y = pack_bf2(__fmul_rn(u[d3][i0 + 2], 0.0625f), __fmul_rn(u[d3][i0 + 3], 0.0625f));
-          o.z = pack_bf2(__fmul_rn(u[d3][i0 + 4], 0.0625f), __fmul_rn(u[d3][i0 + 5], 0.0625f));
-          o.w = pack_bf2(__fmul_rn(u[d3][i0 + 6], 0.0625f), __fmul_rn(u[d3][i0 + 7], 0.0625f));
-          *reinterpret_cast<uint4*>(dst + 64 * d3 + 32 * (h & 1)) = o;
+          const int d3 = h >> 1, i0 = 4 * (h & 1);
+          uint32_t o[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float y0, y1;
+            upk(mul2(u2[d3][i0 + e], q16), y0, y1);
+            o[e] = pack_bf2(y0, y1);
+          }
+          *reinterpret_cast<uint4*>(dst + 64 * d3 + 32 * (h & 1)) = make_uint4(o[0], o[1], o[2], o[3]);
         }
       }
       continue;
     }
     if (t == 0) scale[row] = s;
     if (owner) {
-      const f2 inv2 = pk(inv, inv), rnd2 = pk(12582912.0f, 12582912.0f);
-      uint32_t w[16];  // w[2*h + k]: bytes of u[d3 = h>>1][8*(h&1) + 4k .. +3]
+      const f2 inv2 = pk(inv, inv), rnd2 = pk(12582912.0f, 12582912.0f), zero2 = pk(0.f, 0.f);
+      uint32_t w[16];  // w[2*h + k]: bytes of slice h's columns 4k .. 4k+3 (h = 2 d3 + round)
 #pragma unroll
       for (int h = 0; h < 8; ++h) {
-        const int d3 = h >> 1, i0 = 8 * (h & 1);
+        const int d3 = h >> 1, i0 = 4 * (h & 1);
         uint32_t b[8];
 #pragma unroll
-        for (int e = 0; e < 8; e += 2) {
+        for (int e = 0; e < 4; ++e) {
           float t0, t1, r0, r1;
-          const f2 tt = mul2(pk(u[d3][i0 + e], u[d3][i0 + e + 1]), inv2);
-          upk(tt, t0, t1);
-          if (ORDER != 2) { t0 = fmaxf(t0, -128.f); t1 = fmaxf(t1, -128.f); }
-          upk(add2(pk(t0, t1), rnd2), r0, r1);
-          b[e] = (ORDER == 2 && t0 != t0) ? 0u : (__float_as_uint(r0) & 0xffu);
-          b[e + 1] = (ORDER == 2 && t1 != t1) ? 0u : (__float_as_uint(r1) & 0xffu);
+          // t = u * inv rounded to f32 first, as the reference's v * inv.  Written as fma(u, inv, +0): ptxas
+          // contracts a paired multiply feeding a paired add into one fused op (a single rounding of u * inv +
+          // 1.5 * 2^23, which breaks ties differently), and cannot fuse an fma with the add.  A zero product's
+          // sign does not matter here.
+          const f2 tt = fma2(u2[d3][i0 + e], inv2, zero2);
+          if (!special) {
+            // |t| <= 127 by construction of inv: the nearest-even integer is the code, no clamp or NaN case
+            upk(add2(tt, rnd2), r0, r1);
+            b[2 * e] = __float_as_uint(r0) & 0xffu;
+            b[2 * e + 1] = __float_as_uint(r1) & 0xffu;
+          } else {
+            upk(tt, t0, t1);
+            b[2 * e] = code_of<ORDER>(t0);
+            b[2 * e + 1] = code_of<ORDER>(t1);
+          }
         }
         w[2 * h] = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410);
         w[2 * h + 1] = __byte_perm(__byte_perm(b[4], b[5], 0x0040), __byte_perm(b[6], b[7], 0x0040), 0x5410);
