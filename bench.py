@@ -508,7 +508,14 @@ def main() -> None:
                "d2h_bytes_per_step": int(sum(h.numel() * 2 for h in host_o)), "ms_per_step": e_ms,
                "path": "h3q_gemm_s8 (C ABI) with pinned host input/output, copies inside the timed region"}
 
-    extras = multi_gpu_extras(layers, M, dist, dev) if dist is not None else None
+    extras = None
+    if dist is not None:
+        try:
+            extras = multi_gpu_extras(layers, M, dist, dev)
+        except Exception as e:  # the headline line must still print; the failure is reported in it
+            extras = {"error": f"{type(e).__name__}: {e}"}
+        torch.cuda.synchronize()
+        dist.barrier()
     nv = nvfp4_c3(dev, load_peaks()) if rank == 0 else None
     att = attention_c4(dev, load_peaks()) if rank == 0 else None
 

@@ -1,6 +1,6 @@
-"""Two-GPU parity of h3q.parallel (NCCL ranks in child processes; skipped with fewer than two GPUs): the fused
-N-split GEMM (every rank's column block written into every rank's output over NVLink), the NCCL all-gather form
-of it, and query-sharded attention, each bit-identical to the single-GPU result."""
+"""Multi-GPU parity of h3q.parallel (one NCCL rank per GPU in child processes, 2 to 8 GPUs; skipped with fewer than
+two): the fused N-split GEMM (every rank's column block written into every rank's output over NVLink), the NCCL
+all-gather form of it, and query-sharded attention, each bit-identical to the single-GPU result."""
 import datetime
 import os
 import socket
@@ -64,13 +64,14 @@ def _worker(rank: int, world: int, port: int, errors):
         dist.destroy_process_group()
 
 
-def test_two_gpu_nsplit_and_sharded_attention():
-    if torch.cuda.device_count() < 2:
+def test_multi_gpu_nsplit_and_sharded_attention():
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
         pytest.skip("needs two GPUs")
     ctx = mp.get_context("spawn")
     errors = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, errors)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, errors)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
