@@ -248,6 +248,38 @@ def attention_c4(dev, peaks: dict, reps: int = 5, S: int = 32760, H: int = 40) -
                     "burst, serial"}
 
 
+def modulate_fused(dev, peaks: dict, reps: int = 10, M: int = 32760, C: int = 5120) -> dict:
+    """The step in front of the qkv and fc1 linears: RMSNorm + adaLN modulate, then the rotated int8 quantizer.
+    "two_pass" runs h3q_rms_modulate (bf16 row to memory) then h3q_quant_rows_i8, as the reference's
+    rms_modulate + gemm_s8 do; "fused" is h3q_rms_modulate_quant.  HBM bytes counted as the fused pass's:
+    2C read + C + 4 written per row (the adaLN tables stay in L2)."""
+    import torch
+    import h3q
+    g = torch.Generator(device=dev).manual_seed(11)
+    x = torch.randn((M, C), generator=g, device=dev).to(torch.bfloat16)
+    w = (1.0 + 0.1 * torch.randn(C, generator=g, device=dev)).to(torch.bfloat16)
+    sc = 0.5 * torch.randn((6, C), generator=g, device=dev)
+    sh = 0.5 * torch.randn((6, C), generator=g, device=dev)
+    # table row of each token: its latent frame (21 frames of 1560 tokens at c1), as the DiT indexes its adaLN rows
+    idx = ((torch.arange(M, device=dev) // 1560) % 6).to(torch.int32)
+    res = {}
+    for name, fn in (("two_pass", lambda: h3q.quant_rows(h3q.rms_modulate(x, w, 1e-6, sc, sh, idx), True)),
+                     ("fused", lambda: h3q.rms_modulate_quant(x, w, 1e-6, sc, sh, idx))):
+        for _ in range(3):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / reps
+        res[name] = {"ms": round(ms, 4), "gbs_of_fused_bytes": round((3.0 * M * C + 4.0 * M) / (ms * 1e-3) / 1e9, 1)}
+    res["workload"] = f"rms_modulate + rotated int8 quantization of the qkv input, M={M} C={C}"
+    res["frac_of_hbm"] = round(res["fused"]["gbs_of_fused_bytes"] / peaks["hbm_gbs"], 3)
+    return res
+
+
 def _max_over_ranks(ms: float, dist, dev) -> float:
     import torch
     t = torch.tensor([ms], device=dev, dtype=torch.float64)
@@ -518,6 +550,7 @@ def main() -> None:
         dist.barrier()
     nv = nvfp4_c3(dev, load_peaks()) if rank == 0 else None
     att = attention_c4(dev, load_peaks()) if rank == 0 else None
+    modq = modulate_fused(dev, load_peaks()) if rank == 0 else None
 
     cb = None
     if rank == 0 and ws_n == 1 and not args.no_cpu_baseline:
@@ -547,6 +580,7 @@ def main() -> None:
         "per_linear": per_linear,
         "nvfp4_c3": nv,
         "attention_c4": att,
+        "modulate_quant": modq,
         "multi_gpu": extras,
         "cpu_baseline": cb, "e2e": e2e, "clocks": clk.summary(),
         "gpu_launches": 2 * launches,

@@ -272,4 +272,44 @@ h3q_status h3q_gate_add(const void* x, const void* y, int kind, const float* gat
   return cuda_status(launch_gate_add(x, y, kind, gate, idx, out, s, c, (cudaStream_t)stream), what);
 }
 
+
+static h3q_status rms_modulate_checks(const uint16_t* x, const uint16_t* w, const float* scale, const float* shift,
+                                      const uint32_t* idx, const void* out, int64_t S, int64_t C, const char* what) {
+  if (S < 0 || C < 0) return fail(H3Q_ERR_ARG, "%s: negative shape", what);
+  if (S == 0 || C == 0) return H3Q_OK;
+  if (!x || !w || !scale || !shift || !idx || !out) return fail(H3Q_ERR_ARG, "%s: null pointer", what);
+  if (C % 256 != 0 || C > 16384)
+    return fail(H3Q_ERR_UNSUPPORTED, "%s: this build needs C %% 256 == 0 and C <= 16384 (C = %lld)", what,
+                (long long)C);
+  if (!aligned16(x) || !aligned16(w) || !aligned16(scale) || !aligned16(shift) || !aligned16(out))
+    return fail(H3Q_ERR_ARG, "%s: tensors must be 16-byte aligned", what);
+  return H3Q_OK;
+}
+
+h3q_status h3q_rms_modulate(const uint16_t* x, const uint16_t* w, float eps, const float* scale, const float* shift,
+                            const uint32_t* idx, uint16_t* out, int64_t S, int64_t C, void* stream) {
+  const char* what = "h3q_rms_modulate";
+  if (h3q_status st = rms_modulate_checks(x, w, scale, shift, idx, out, S, C, what)) return st;
+  if (S == 0 || C == 0) return H3Q_OK;
+  int* err = error_word();
+  if (!err) return fail(H3Q_ERR_CUDA, "%s: could not set up the device error word", what);
+  return cuda_status(launch_rms_modulate(x, w, eps, scale, shift, idx, nullptr, nullptr, out, S, C, err,
+                                         (cudaStream_t)stream),
+                     what);
+}
+
+h3q_status h3q_rms_modulate_quant(const uint16_t* x, const uint16_t* w, float eps, const float* scale,
+                                  const float* shift, const uint32_t* idx, int8_t* codes, float* row_scale, int64_t S,
+                                  int64_t C, void* stream) {
+  const char* what = "h3q_rms_modulate_quant";
+  if (h3q_status st = rms_modulate_checks(x, w, scale, shift, idx, codes, S, C, what)) return st;
+  if (S == 0 || C == 0) return H3Q_OK;
+  if (!row_scale) return fail(H3Q_ERR_ARG, "%s: null pointer", what);
+  int* err = error_word();
+  if (!err) return fail(H3Q_ERR_CUDA, "%s: could not set up the device error word", what);
+  return cuda_status(launch_rms_modulate(x, w, eps, scale, shift, idx, codes, row_scale, nullptr, S, C, err,
+                                         (cudaStream_t)stream),
+                     what);
+}
+
 }  // extern "C"

@@ -39,6 +39,10 @@ cudaError_t launch_rotate_bf16(const uint16_t* x, uint16_t* y, int64_t M, int64_
 // `kind`, interleaved (g0,u0,g1,u1,...) or split halves (gates then ups); out [rows, F]
 cudaError_t launch_swiglu(const void* y, void* out, int kind, int64_t rows, int64_t F, int interleaved, cudaStream_t st);
 cudaError_t launch_gemm_i8(const int8_t* A, const int8_t* B, const GemmArgs& a, cudaStream_t st);
+// rms_modulate (kernels.rs:376-401) of bf16 rows, fused into the quantizer (codes != nullptr) or alone (y)
+cudaError_t launch_rms_modulate(const uint16_t* x, const uint16_t* w, float eps, const float* scale_tab,
+                                const float* shift_tab, const uint32_t* idx, int8_t* codes, float* row_scale,
+                                uint16_t* y, int64_t M, int64_t K, int* err, cudaStream_t st);
 // GEMM whose output columns [n_offset, n_offset + a.N) of an [M, n_total] bf16 result go to every buffer of outs
 constexpr int kMaxGatherRanks = 8;
 cudaError_t launch_gemm_i8_allgather(const int8_t* A, const int8_t* B, const GemmArgs& a, void* const* outs, int n_out,

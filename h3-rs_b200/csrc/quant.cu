@@ -94,6 +94,15 @@ __device__ __forceinline__ void h4_pair(f2& a0, f2& a1, f2& a2, f2& a3) {
   }
 }
 
+// Both halves rounded to bf16 (cvt.rn.bf16x2: nearest even, the reference's f2bf for finite values) and widened.
+__device__ __forceinline__ f2 bf16r2(f2 v) {
+  float lo, hi;
+  upk(v, lo, hi);
+  uint32_t p;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(p) : "f"(hi), "f"(lo));
+  return pk(__uint_as_float(p << 16), __uint_as_float(p & 0xffff0000u));
+}
+
 // Slot of a thread's 16-byte chunk c inside its exchange line: c ^ f(t).  With f(t) = (t & 7) ^ bit2(t), the
 // 8 lanes of a shared-memory phase hit 8 different bank groups both when each writes its own line and when the
 // lanes of two quads read chunks 2j, 2j+1 of one quad member's line.
@@ -116,16 +125,31 @@ constexpr int kQStages = 3;
 
 // ROT_ONLY: write bf16(rotated row) to `ybf` instead of codes and scales (rotate_activation, weights.rs:482-489,
 // for the paths that quantize a pre-rotated activation).
-template <int ORDER, typename Tin, bool ROT_ONLY = false>
+// MOD: apply RMSNorm + adaLN modulate to the row first (rms_modulate, kernels.rs:376-401; bf16 rows only):
+//   inv = rsqrtf(sum(x^2) / K + eps), summed in that kernel's order (512 thread partials, thread t taking
+//   elements t, t+512, ... with a fused multiply-add, then xor trees in 32-thread groups and over the 16 group sums);
+//   n = bf16((x * inv) * w[c]); y = bf16(fma(n, 1 + bf16(scale[idx[r], c]), bf16(shift[idx[r], c]))).
+// y is then rotated and quantized as the row would be after rms_modulate wrote it to memory: one pass instead of
+// a bf16 round trip through HBM.  With ORDER 0 and ROT_ONLY the kernel writes y itself (rms_modulate).
+struct ModArgs {
+  const uint16_t* w;       // bf16 [K] norm weight
+  const float* scale;      // f32 [R, K] adaLN scale table
+  const float* shift;      // f32 [R, K] adaLN shift table
+  const uint32_t* idx;     // [M] table row of each activation row
+  float eps;
+};
+
+template <int ORDER, typename Tin, bool ROT_ONLY = false, bool MOD = false>
 __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__ CUtensorMap tmx,
                                                          int8_t* __restrict__ q, float* __restrict__ scale,
                                                          int64_t M, int K, int box_rows, int boxes_per_row,
-                                                         int* err, uint16_t* __restrict__ ybf) {
+                                                         int* err, uint16_t* __restrict__ ybf, const ModArgs mod) {
   extern __shared__ uint8_t qsm_raw[];
   // align by offsetting the __shared__ array itself, so the compiler keeps shared-space (LDS/STS) accesses
   uint8_t* qsm = qsm_raw + ((1024u - (smem_u32(qsm_raw) & 1023u)) & 1023u);
   __shared__ uint64_t full[kQStages];
   __shared__ unsigned s_max[3], s_max2[3];
+  __shared__ float s_red[17];
   __shared__ int s_abort;
   constexpr int ES = sizeof(Tin);
   constexpr int LINES = 64 * ES / 128;  // 128-byte lines per thread: 1 (16-bit) or 2 (f32)
@@ -149,21 +173,154 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
       tma_load_2d(qsm + (size_t)stage * stage_bytes + (size_t)b * box_rows * 128, &tmx, &full[stage], 0,
                   (int32_t)(row * box_rows * boxes_per_row + b * box_rows));
   };
+  // Rows of this CTA: every gridDim.x-th row, or with MOD a contiguous block (neighbouring tokens share their
+  // adaLN table row, which then stays in L1).
+  const int64_t blk = (M + gridDim.x - 1) / gridDim.x;
+  const int64_t rb0 = MOD ? (int64_t)blockIdx.x * blk : (int64_t)blockIdx.x;
+  const int64_t rend = MOD ? (rb0 + blk < M ? rb0 + blk : M) : M;
+  auto row_of = [&](int64_t i) -> int64_t { return MOD ? rb0 + i : rb0 + i * (int64_t)gridDim.x; };
   if (t == 0) {
     tma_prefetch_desc(&tmx);
     for (int s = 0; s < kQStages; ++s) {
-      const int64_t r = blockIdx.x + (int64_t)s * gridDim.x;
-      if (r < M) issue(r, s);
+      const int64_t r = row_of(s);
+      if (r < rend) issue(r, s);
     }
   }
+  uint32_t tab_idx = 0xffffffffu;  // MOD: table row held in this thread's shared-memory slice
+  if (MOD && owner) {
+    // the norm weight of the thread's columns, once: 16-byte word c at wsm + (c * blockDim + t) * 16
+    uint8_t* wsm = qsm + (size_t)kQStages * stage_bytes + (size_t)blockDim.x * 256;
+    const uint4* wv = reinterpret_cast<const uint4*>(mod.w + 64 * t);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(wsm + ((size_t)c * blockDim.x + t) * 16) = __ldg(wv + c);
+  }
   int it = 0;
-  for (int64_t row = blockIdx.x; row < M; row += gridDim.x, ++it) {
+  for (int64_t row = row_of(0); row < rend; row = row_of(++it)) {
     const int stage = it % kQStages;
+    if (MOD && owner) {
+      // The thread's bf16 scale / shift values of the row's table row live in its slice of shared memory
+      // (16-byte word i at tab + (i * blockDim + t) * 16, columns 4i .. 4i+3 as scale pairs then shift pairs:
+      // conflict-free), reloaded, before the row has landed, only when the table index changes.
+      const uint32_t ridx = __ldg(mod.idx + row);
+      if (ridx != tab_idx) {
+        uint8_t* tab = qsm + (size_t)kQStages * stage_bytes;
+        const float4* scv = reinterpret_cast<const float4*>(mod.scale + (int64_t)ridx * K + 64 * t);
+        const float4* shv = reinterpret_cast<const float4*>(mod.shift + (int64_t)ridx * K + 64 * t);
+#pragma unroll 4
+        for (int q4 = 0; q4 < 16; ++q4) {
+          const float4 a = __ldg(scv + q4), b = __ldg(shv + q4);
+          uint32_t o[4];
+          asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(o[0]) : "f"(a.y), "f"(a.x));
+          asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(o[1]) : "f"(a.w), "f"(a.z));
+          asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(o[2]) : "f"(b.y), "f"(b.x));
+          asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(o[3]) : "f"(b.w), "f"(b.z));
+          *reinterpret_cast<uint4*>(tab + ((size_t)q4 * blockDim.x + t) * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+        tab_idx = ridx;
+      }
+    }
     const bool landed = mbar_wait_bounded(&full[stage], (uint32_t)(it / kQStages) & 1u, &s_abort, err, kDevTimeoutFull);
     if (!__syncthreads_and(landed)) break;  // the whole CTA gives up together (barriers follow)
+    float inv_rms = 0.f;
+    if (MOD) {
+      // the 512 partial sums of rms_modulate's row block, read from the landed row (128-byte-swizzled lines)
+      const uint8_t* base = qsm + (size_t)stage * stage_bytes;
+      const int nw = blockDim.x >> 5, wp = t >> 5, ln = t & 31;
+      if (blockDim.x >= 64) {
+        // thread m < 64 holds the partials of reference threads 8m .. 8m+7 (one 16-byte piece per 512-element
+        // stride, conflict-free); the reference's 32-thread xor trees are 4 neighbouring lanes here: levels 16 and
+        // 8 cross lanes (xor 2, xor 1), levels 4, 2, 1 stay inside the thread
+        float a[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) a[i] = 0.f;
+        if (t < 64) {
+          for (int c0 = 8 * t; c0 < K; c0 += 512) {
+            const int line = c0 >> 6, ch = (c0 >> 3) & 7;
+            const uint4 r8 = *reinterpret_cast<const uint4*>(base + line * 128 + ((ch ^ (line & 7)) << 4));
+            const uint32_t ww[4] = {r8.x, r8.y, r8.z, r8.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float x0 = __uint_as_float(ww[i] << 16), x1 = __uint_as_float(ww[i] & 0xffff0000u);
+              a[2 * i] = __fmaf_rn(x0, x0, a[2 * i]);
+              a[2 * i + 1] = __fmaf_rn(x1, x1, a[2 * i + 1]);
+            }
+          }
+        }
+#pragma unroll
+        for (int lo = 2; lo >= 1; lo >>= 1) {  // tree levels 16 (lanes xor 2) and 8 (lanes xor 1)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) a[i] = __fadd_rn(a[i], __shfl_xor_sync(0xffffffffu, a[i], lo));
+        }
+#pragma unroll
+        for (int o = 4; o >= 1; o >>= 1) {  // tree levels 4, 2, 1
+          float b[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) b[i] = __fadd_rn(a[i], a[i ^ o]);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) a[i] = b[i];
+        }
+        if (t < 64 && (t & 3) == 0) s_red[t >> 2] = a[0];
+      } else {
+        for (int rw = wp; rw < 16; rw += nw) {
+          float sq = 0.f;
+          for (int c = 32 * rw + ln; c < K; c += 512) {
+            const int line = c >> 6, ch = (c >> 3) & 7;
+            const float xv = bf2f(*reinterpret_cast<const uint16_t*>(base + line * 128 + ((ch ^ (line & 7)) << 4) +
+                                                                     (c & 7) * 2));
+            sq = __fmaf_rn(xv, xv, sq);
+          }
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) sq = __fadd_rn(sq, __shfl_xor_sync(0xffffffffu, sq, o));
+          if (ln == 0) s_red[rw] = sq;
+        }
+      }
+      __syncthreads();
+      if (wp == 0) {
+        float tt = ln < 16 ? s_red[ln] : 0.f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) tt = __fadd_rn(tt, __shfl_xor_sync(0xffffffffu, tt, o));
+        if (ln == 0) s_red[16] = tt;
+      }
+      __syncthreads();
+      inv_rms = rsqrtf(__fadd_rn(__fdiv_rn(s_red[16], (float)K), mod.eps));
+    }
     // The thread's 64 values as 32 register pairs: v2[k] = elements (2k, 2k + 1).  Pairs of neighbouring elements
     // follow the same butterfly through digits 1..3, so those stages run as paired f32x2 operations.
     f2 v2[32];
+    if (MOD && owner) {
+      // y = bf16(fma(bf16((x * inv) * w), 1 + bf16(scale), bf16(shift))) for the thread's columns 64t .. 64t+63
+      // (its own 128-byte line), two columns per instruction, written back in place as bf16 (y is a bf16 value);
+      // the roundings are cvt.rn (nearest even, as the reference's f2bf for every finite value; a NaN stays a
+      // NaN).  One 16-byte chunk at a time keeps the register footprint of the pass small.
+      uint8_t* own = qsm + (size_t)stage * stage_bytes + (size_t)t * 128;
+      const uint8_t* tab = qsm + (size_t)kQStages * stage_bytes;
+      const uint8_t* wsm = tab + (size_t)blockDim.x * 256;
+      const f2 inv2 = pk(inv_rms, inv_rms), one2 = pk(1.f, 1.f);
+#pragma unroll 1
+      for (int c = 0; c < 8; ++c) {
+        uint4* px = reinterpret_cast<uint4*>(own + ((c ^ (t & 7)) << 4));
+        const uint4 raw = *px;
+        const uint4 w8 = *reinterpret_cast<const uint4*>(wsm + ((size_t)c * blockDim.x + t) * 16);
+        const uint4 tb0 = *reinterpret_cast<const uint4*>(tab + ((size_t)(2 * c) * blockDim.x + t) * 16);
+        const uint4 tb1 = *reinterpret_cast<const uint4*>(tab + ((size_t)(2 * c + 1) * blockDim.x + t) * 16);
+        const uint32_t xx[4] = {raw.x, raw.y, raw.z, raw.w}, ww[4] = {w8.x, w8.y, w8.z, w8.w};
+        const uint32_t sp[4] = {tb0.x, tb0.y, tb1.x, tb1.y}, hp[4] = {tb0.z, tb0.w, tb1.z, tb1.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {  // columns 8c + 2i, +1
+          const f2 x2 = pk(__uint_as_float(xx[i] << 16), __uint_as_float(xx[i] & 0xffff0000u));
+          const f2 w2 = pk(__uint_as_float(ww[i] << 16), __uint_as_float(ww[i] & 0xffff0000u));
+          const f2 sc2 = pk(__uint_as_float(sp[i] << 16), __uint_as_float(sp[i] & 0xffff0000u));
+          const f2 sh2 = pk(__uint_as_float(hp[i] << 16), __uint_as_float(hp[i] & 0xffff0000u));
+          const f2 n = bf16r2(mul2(mul2(x2, inv2), w2));
+          float y0, y1;
+          upk(fma2(n, add2(one2, sc2), sh2), y0, y1);
+          asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(o[i]) : "f"(y1), "f"(y0));
+        }
+        *px = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+      fence_proxy_async_smem();  // these generic writes precede a later TMA refill of the stage
+    }
     if (owner) {
       const uint8_t* base = qsm + (size_t)stage * stage_bytes;
 #pragma unroll
@@ -271,8 +428,8 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
     if (t == 0) {
       s_max[(it + 1) % 3] = 0u;
       s_max2[(it + 1) % 3] = 0u;
-      const int64_t nr = row + (int64_t)kQStages * gridDim.x;
-      if (nr < M) {
+      const int64_t nr = row_of(it + kQStages);
+      if (nr < rend) {
         fence_proxy_async_smem();
         issue(nr, stage);
       }
@@ -299,6 +456,23 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
     const float mx = ORDER == 0 ? __uint_as_float(mbits) : __fmul_rn(__uint_as_float(mbits), 0.0625f);
     const float s = fmaxf(__fdiv_rn(mx, 127.f), 1e-30f);
     const float inv = ORDER == 0 ? __fdiv_rn(1.f, s) : __fmul_rn(__fdiv_rn(1.f, s), 0.0625f);
+    if (ROT_ONLY && ORDER == 0) {  // the (modulated) row itself, contiguous columns 64t .. 64t+63
+      if (owner) {
+        uint4* dst = reinterpret_cast<uint4*>(ybf + row * (int64_t)K + 64 * t);
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+          uint32_t o[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float y0, y1;
+            upk(u2[h >> 1][4 * (h & 1) + e], y0, y1);
+            o[e] = pack_bf2(y0, y1);
+          }
+          dst[h] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+      }
+      continue;
+    }
     if (ROT_ONLY) {
       if (owner) {
         uint16_t* dst = ybf + row * (int64_t)K + (t >> 2) * 256 + 8 * j;
@@ -366,8 +540,8 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
     int dummy = 0;
     for (int k = 0; k < kQStages; ++k) {
       const int i2 = it + k;  // loads issued for iterations it .. it+kQStages-1 may be pending
-      const int64_t r = blockIdx.x + (int64_t)i2 * gridDim.x;
-      if (r < M) mbar_wait_bounded(&full[i2 % kQStages], (uint32_t)(i2 / kQStages) & 1u, &dummy, err, kDevTimeoutDrain);
+      const int64_t r = row_of(i2);
+      if (r < rend) mbar_wait_bounded(&full[i2 % kQStages], (uint32_t)(i2 / kQStages) & 1u, &dummy, err, kDevTimeoutDrain);
     }
   }
   __syncthreads();
@@ -415,9 +589,9 @@ static PFN_cuTensorMapEncodeTiled_v12000 q_encode_fn() {
   return fn;
 }
 
-template <int ORDER, typename Tin, bool ROT_ONLY = false>
+template <int ORDER, typename Tin, bool ROT_ONLY = false, bool MOD = false>
 static cudaError_t launch_rows(const void* x, int8_t* q, float* scale, int64_t M, int K, int* err, cudaStream_t st,
-                               uint16_t* ybf = nullptr) {
+                               uint16_t* ybf = nullptr, const ModArgs* mod = nullptr) {
   constexpr int ES = sizeof(Tin);
   const int G = K / 256;
   const int threads = ((4 * G + 31) / 32) * 32;
@@ -433,8 +607,10 @@ static cudaError_t launch_rows(const void* x, int8_t* q, float* scale, int64_t M
   auto fn = q_encode_fn();
   if (!fn) return cudaErrorInvalidValue;
   const size_t stage_bytes = ((size_t)K * ES + 1023) / 1024 * 1024;
-  const size_t smem = 1024 + kQStages * stage_bytes;
-  auto kern = quant_rows_kernel<ORDER, Tin, ROT_ONLY>;
+  // MOD adds each thread's 64 columns of the current adaLN table row (bf16 scale / shift, 256 bytes) and of the
+  // norm weight (bf16, 128 bytes)
+  const size_t smem = 1024 + kQStages * stage_bytes + (MOD ? (size_t)threads * 384 : 0);
+  auto kern = quant_rows_kernel<ORDER, Tin, ROT_ONLY, MOD>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   int dev = 0, per_sm = 0;
@@ -460,8 +636,13 @@ static cudaError_t launch_rows(const void* x, int8_t* q, float* scale, int64_t M
            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
     const unsigned grid = (unsigned)(mc < want ? mc : want);
+    ModArgs ma{};
+    if (MOD) {
+      ma = *mod;
+      ma.idx = mod->idx + r0;
+    }
     kern<<<grid, threads, smem, st>>>(m, ROT_ONLY ? q : q + r0 * (int64_t)K, ROT_ONLY ? scale : scale + r0, mc, K,
-                                      box_rows, boxes, err, ROT_ONLY ? ybf + r0 * (int64_t)K : nullptr);
+                                      box_rows, boxes, err, ROT_ONLY ? ybf + r0 * (int64_t)K : nullptr, ma);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
@@ -495,6 +676,19 @@ cudaError_t launch_quant_rows(const void* x, int kind, int8_t* q, float* scale, 
 cudaError_t launch_rotate_bf16(const uint16_t* x, uint16_t* y, int64_t M, int64_t K, int* err, cudaStream_t st) {
   if (M == 0 || K == 0) return cudaSuccess;
   return launch_rows<2, __nv_bfloat16, true>(x, nullptr, nullptr, M, (int)K, err, st, y);
+}
+
+// rms_modulate followed by the quantizer quant_rows_raw would pick for the modulated bf16 row (rot2 order for
+// K / 256 <= 56, rot order beyond), or rms_modulate alone (codes == nullptr: the bf16 row goes to y).
+cudaError_t launch_rms_modulate(const uint16_t* x, const uint16_t* w, float eps, const float* scale_tab,
+                                const float* shift_tab, const uint32_t* idx, int8_t* codes, float* row_scale,
+                                uint16_t* y, int64_t M, int64_t K, int* err, cudaStream_t st) {
+  if (M == 0 || K == 0) return cudaSuccess;
+  ModArgs ma{w, scale_tab, shift_tab, idx, eps};
+  if (!codes) return launch_rows<0, __nv_bfloat16, true, true>(x, nullptr, nullptr, M, (int)K, err, st, y, &ma);
+  if (K / 256 <= 56)
+    return launch_rows<2, __nv_bfloat16, false, true>(x, codes, row_scale, M, (int)K, err, st, nullptr, &ma);
+  return launch_rows<1, __nv_bfloat16, false, true>(x, codes, row_scale, M, (int)K, err, st, nullptr, &ma);
 }
 
 __global__ void fill_f32_kernel(float* p, float v, int64_t n) {

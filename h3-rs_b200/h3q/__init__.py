@@ -65,6 +65,8 @@ SIGNATURES = {
     "h3q_qlinear_workspace_size": (_sz, [ctypes.POINTER(QLinearDesc), _int, _i64, _int, ctypes.POINTER(Switches)]),
     "h3q_qlinear_forward": (_int, [ctypes.POINTER(QLinearDesc), _vp, _int, _i64, _int, _vp, _vp, _sz,
                                    ctypes.POINTER(Switches), _vp]),
+    "h3q_rms_modulate": (_int, [_vp, _vp, ctypes.c_float, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
+    "h3q_rms_modulate_quant": (_int, [_vp, _vp, ctypes.c_float, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp]),
     "h3q_attention_available": (_int, [_i64, _int, _int]),
     "h3q_attention_workspace_size": (_sz, [_i64, _i64, _int]),
     "h3q_attention": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _int, _vp, _sz, _vp]),
@@ -292,6 +294,30 @@ def gate_add(x, y, gate, idx):
     out = torch.empty_like(x)
     check(lib().h3q_gate_add(_p(x), _p(y), _kind(x.dtype), _p(gate), _p(idx), _p(out), S, C, _stream(x.device)))
     return out
+
+
+def rms_modulate(x, w, eps: float, scale, shift, idx):
+    """kernels::rms_modulate (kernels.rs:1201-1204) for bf16 x [S, C]: bf16 [S, C]."""
+    import torch
+    w = w.to(torch.bfloat16).contiguous()
+    _cuda(x, w, scale, shift, idx)
+    S, C = x.shape
+    out = torch.empty_like(x)
+    check(lib().h3q_rms_modulate(_p(x), _p(w), eps, _p(scale), _p(shift), _p(idx), _p(out), S, C, _stream(x.device)))
+    return out
+
+
+def rms_modulate_quant(x, w, eps: float, scale, shift, idx):
+    """rms_modulate fused with the rotated per-row int8 quantizer: (codes int8 [S, C], row scales f32 [S])."""
+    import torch
+    w = w.to(torch.bfloat16).contiguous()
+    _cuda(x, w, scale, shift, idx)
+    S, C = x.shape
+    q = torch.empty((S, C), dtype=torch.int8, device=x.device)
+    xs = torch.empty(S, dtype=torch.float32, device=x.device)
+    check(lib().h3q_rms_modulate_quant(_p(x), _p(w), eps, _p(scale), _p(shift), _p(idx), _p(q), _p(xs), S, C,
+                                       _stream(x.device)))
+    return q, xs
 
 
 def attention_available(q) -> bool:

@@ -190,6 +190,21 @@ h3q_status h3q_qlinear_forward(const h3q_qlinear* layer, const void* x, int x_ki
                                void* out, void* workspace, size_t workspace_bytes, const h3q_switches* sw,
                                void* stream);
 
+/* kernels::rms_modulate (kernels.rs:1201-1204, kernel :376-401) for bf16 rows: out = bf16(fma(n, 1 + bf16(scale[
+ * idx[s], c]), bf16(shift[idx[s], c]))) with n = bf16((x * rsqrt(mean(x^2) + eps)) * w[c]), the mean summed in
+ * the reference kernel's order.  x, out bf16 [S, C]; w bf16 [C]; scale, shift f32 [R, C]; idx u32 [S].  This build
+ * needs C % 256 == 0 and C <= 16384. */
+h3q_status h3q_rms_modulate(const uint16_t* x, const uint16_t* w, float eps, const float* scale, const float* shift,
+                            const uint32_t* idx, uint16_t* out, int64_t S, int64_t C, void* stream);
+
+/* rms_modulate fused with the quantizer the next linear applies to its output (no counterpart in the reference,
+ * which writes the bf16 row to memory and reads it back): the modulated row is ConvRot-rotated and quantized per
+ * row exactly as h3q_quant_rows_i8(rotate = 1) would quantize h3q_rms_modulate's output (rot2 order for
+ * C / 256 <= 56), giving int8 codes [S, C] and f32 row scales [S] for h3q_gemm_s8_quantized.  Same limits. */
+h3q_status h3q_rms_modulate_quant(const uint16_t* x, const uint16_t* w, float eps, const float* scale,
+                                  const float* shift, const uint32_t* idx, int8_t* codes, float* row_scale, int64_t S,
+                                  int64_t C, void* stream);
+
 /* ---------------------------------------------------------------------------------------------------------
  * int8 attention (attn8.rs): non-causal SageAttention-style attention over [S, H, 128] bf16 q / k / v, int8
  * Q.K^T with K smoothed by its mean over the sequence, online softmax, 16-bit P.V with f32 accumulation.

@@ -712,3 +712,50 @@ H3O_API void h3o_attn_forward(const int8_t* q8, const float* qs, const int8_t* k
                               int pv_bf16) {
     h3o_attn_forward_rows(q8, qs, S, k8, ks, vsrc, v_rs, v_col, out, S, H, pv_bf16);
 }
+
+/* ---------------------------------------------------------------- RMSNorm + adaLN modulate (kernels.rs:376-401) */
+
+/*
+ * rms_modulate for bf16 rows x [S, C], weight w (bf16 [C]), f32 tables scale / shift [R, C] selected per row by
+ * idx: the sum of squares in the reference kernel's order (512 thread partials, thread t summing elements
+ * t, t+512, ... with a fused multiply-add; each 32-thread group then reduced by xor shuffles 16, 8, 4, 2, 1; the
+ * 16 group sums reduced the same way), inv = 1 / sqrt(sum / C + eps) (the reference calls rsqrtf, an approximate
+ * instruction; 1/sqrtf here can differ from it in the last bit), n = bf16((x * inv) * w), out =
+ * bf16(fma(n, 1 + bf16(scale), bf16(shift))).  Output bf16 bits [S, C].
+ */
+static float xor_tree32(const float* v) {
+    float a[32];
+    for (int i = 0; i < 32; ++i) a[i] = v[i];
+    for (int o = 16; o > 0; o >>= 1) {
+        float b[32];
+        for (int i = 0; i < 32; ++i) b[i] = a[i] + a[i ^ o];
+        for (int i = 0; i < 32; ++i) a[i] = b[i];
+    }
+    return a[0];
+}
+
+H3O_API void h3o_rms_modulate(const uint16_t* x, const uint16_t* w, float eps, const float* scale, const float* shift,
+                              const uint32_t* idx, uint16_t* out, int64_t S, int64_t C) {
+    for (int64_t r = 0; r < S; ++r) {
+        const uint16_t* xr = x + r * C;
+        float part[512], red[32];
+        for (int t = 0; t < 512; ++t) {
+            float sq = 0.f;
+            for (int64_t c = t; c < C; c += 512) {
+                const float v = bf2f(xr[c]);
+                sq = fmaf(v, v, sq);
+            }
+            part[t] = sq;
+        }
+        for (int wp = 0; wp < 16; ++wp) red[wp] = xor_tree32(part + 32 * wp);
+        for (int wp = 16; wp < 32; ++wp) red[wp] = 0.f;
+        const float total = xor_tree32(red);
+        const float inv = 1.0f / sqrtf(total / (float)C + eps);
+        const int64_t row = (int64_t)idx[r] * C;
+        for (int64_t c = 0; c < C; ++c) {
+            const float n = bf16r((bf2f(xr[c]) * inv) * bf2f(w[c]));
+            const float sc = bf16r(scale[row + c]), sh = bf16r(shift[row + c]);
+            out[r * C + c] = f2bf(fmaf(n, 1.f + sc, sh));
+        }
+    }
+}

@@ -436,3 +436,31 @@ def attention_exact(q_bf16, k_bf16, v_bf16) -> np.ndarray:
         p = np.exp(s)
         out[:, h, :] = (p / p.sum(axis=1, keepdims=True)) @ v[:, h, :]
     return out
+
+
+# ----------------------------------------------------------------------------- RMSNorm + adaLN modulate
+
+def rms_modulate(x_bf16, w_bf16, eps: float, scale, shift, idx) -> np.ndarray:
+    """rms_modulate (kernels.rs:376-401), the reduction in the reference kernel's order; bf16 bits [S, C].  The
+    reference's rsqrtf is an approximate instruction; 1 / sqrtf here can differ from it in the last bit."""
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
+    S, C = x.shape
+    out = np.empty_like(x)
+    lib().h3o_rms_modulate(_p(x), _p(np.ascontiguousarray(w_bf16, dtype=np.uint16)), c_f32(eps),
+                           _p(np.ascontiguousarray(scale, dtype=np.float32)),
+                           _p(np.ascontiguousarray(shift, dtype=np.float32)),
+                           _p(np.ascontiguousarray(idx, dtype=np.uint32)), _p(out), c_i64(S), c_i64(C))
+    return out
+
+
+def make_modulate_inputs(seed: int, S: int, C: int, R: int = 3):
+    """DiT-like inputs of rms_modulate: x bf16 ~N(0, 1) with 8 outlier channels x20, norm weight bf16 ~1 + N(0, 0.1),
+    adaLN scale / shift tables f32 ~N(0, 0.5) with R rows, idx u32 [S] in [0, R)."""
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((S, C)).astype(np.float32)
+    x[:, rng.choice(C, 8, replace=False)] *= 20.0
+    w = (1.0 + 0.1 * rng.standard_normal(C)).astype(np.float32)
+    scale = (0.5 * rng.standard_normal((R, C))).astype(np.float32)
+    shift = (0.5 * rng.standard_normal((R, C))).astype(np.float32)
+    idx = rng.integers(0, R, S).astype(np.uint32)
+    return f32_to_bf16_bits(x), f32_to_bf16_bits(w), scale, shift, idx

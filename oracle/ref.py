@@ -26,7 +26,7 @@ def lib() -> ctypes.CDLL:
         _LIB = ctypes.CDLL(path())
         for name in ("h3ref_quant_rows", "h3ref_quant_rows_linear", "h3ref_int8_epilogue", "h3ref_dequant_i8",
                      "h3ref_dequant_nvfp4", "h3ref_gate_add", "h3ref_gemm_s8", "h3ref_col_sum",
-                     "h3ref_quant_heads", "h3ref_v_to_f16", "h3ref_attn_qk8"):
+                     "h3ref_quant_heads", "h3ref_v_to_f16", "h3ref_attn_qk8", "h3ref_rms_modulate"):
             getattr(_LIB, name).restype = ctypes.c_int
     return _LIB
 
@@ -126,4 +126,14 @@ def attn_qk8(q8, qs, k8, ks, v16, scale_log2: float):
     out = torch.empty((S, H, 128), dtype=torch.bfloat16, device=q8.device)
     _check(lib().h3ref_attn_qk8(_ptr(q8), _ptr(qs), _ptr(k8), _ptr(ks), _ptr(v16), _ptr(out), S, H,
                                 ctypes.c_float(scale_log2), _stream()), "ref attn_qk8")
+    return out
+
+
+def rms_modulate(x, w, eps: float, scale, shift, idx):
+    """rms_modulate (kernels.rs:376-401), the reference's launch: bf16 [S, C]."""
+    import torch
+    S, C = x.shape
+    out = torch.empty_like(x)
+    _check(lib().h3ref_rms_modulate(_ptr(x), 2, _ptr(w), ctypes.c_float(eps), _ptr(scale), _ptr(shift), _ptr(idx),
+                                    _ptr(out), S, C, _stream()), "ref rms_modulate")
     return out

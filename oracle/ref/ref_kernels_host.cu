@@ -65,4 +65,12 @@ int h3ref_gate_add(const void* x, const void* y, int kind, const float* gate, co
   return (int)cudaGetLastError();
 }
 
+// RmsModulate::cuda_fwd launch (kernels.rs:1184-1196): one CTA of 512 threads per row
+int h3ref_rms_modulate(const void* x, int kind, const void* w, float eps, const float* scale, const float* shift,
+                       const unsigned* idx, void* out, int S, int C, void* stream) {
+  if (S == 0) return 0;
+  rms_modulate<<<S, 512, 0, (cudaStream_t)stream>>>(x, kind, w, eps, scale, shift, idx, out, C);
+  return (int)cudaGetLastError();
+}
+
 }  // extern "C"

@@ -106,3 +106,14 @@ def test_attention_cabi_argument_checks():
     assert L.h3q_attention_core(None, None, None, None, None, None, -1, 1, 0, None, None) == h3q.ERR_ARG
     assert L.h3q_attention_available(64, 2, 0) == 0
     assert L.h3q_attention_available(128, 1, 0) == 0
+
+
+def test_rms_modulate_oracle_formula():
+    """The oracle's rms_modulate against the formula in f64 (one bf16 unit of rounding slack)."""
+    x, w, sc, sh, idx = O.make_modulate_inputs(1, 40, 1024)
+    got = O.bf16_bits_to_f32(O.rms_modulate(x, w, 1e-6, sc, sh, idx)).astype(np.float64)
+    xf = O.bf16_bits_to_f32(x).astype(np.float64)
+    inv = 1.0 / np.sqrt((xf ** 2).mean(axis=1, keepdims=True) + 1e-6)
+    n = O.bf16_round((xf * inv * O.bf16_bits_to_f32(w)[None, :]).astype(np.float32)).astype(np.float64)
+    want = n * (1.0 + O.bf16_round(sc[idx]).astype(np.float64)) + O.bf16_round(sh[idx]).astype(np.float64)
+    assert np.max(np.abs(got - want) / (np.abs(want) + 1e-3)) < 2e-2
