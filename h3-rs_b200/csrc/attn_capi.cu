@@ -18,6 +18,15 @@ cudaError_t launch_v_layout(const uint16_t* x, int64_t rs, int64_t col, uint16_t
 cudaError_t launch_attention(const int8_t* q8, const float* qs, int64_t Sq, const int8_t* k8, const float* ks,
                              const uint16_t* vt, uint16_t* out, int64_t S, int64_t H, bool bf16pv,
                              int32_t* scores, int* err, cudaStream_t st);
+cudaError_t launch_qk_norm_rope(const uint16_t* x, int64_t rs, int64_t col, int64_t hs, const uint16_t* w,
+                                int do_norm, float eps, const float* cs, int rot, uint16_t* out, int64_t S, int64_t H,
+                                int64_t D, cudaStream_t st);
+cudaError_t launch_kmean_rope(const uint16_t* x, int64_t rs, int64_t col, const uint16_t* w, int do_norm, float eps,
+                              const float* cs, int rot, int64_t S, int64_t H, float* mean, float* part,
+                              cudaStream_t st);
+cudaError_t launch_qk_rope_quant(const uint16_t* x, int64_t rs, int64_t col, const uint16_t* w, int do_norm,
+                                 float eps, const float* cs, int rot, const float* mean, int8_t* codes, float* scales,
+                                 int64_t S, int64_t H, bool block128, cudaStream_t st);
 }  // namespace h3q
 
 namespace {
@@ -228,6 +237,78 @@ h3q_status h3q_attention_core(const int8_t* q8, const float* qs, const int8_t* k
   if (!err) return fail(H3Q_ERR_CUDA, "%s: could not set up the device error word", what);
   return cuda_status(h3q::launch_attention(q8, qs, S, k8, ks, vt, out, S, H, (flags & H3Q_ATTN_PV_BF16) != 0, scores,
                                            err, (cudaStream_t)stream),
+                     what);
+}
+
+h3q_status h3q_qk_norm_rope(const uint16_t* x, int64_t row_stride, int64_t col_off, int64_t head_stride,
+                            const uint16_t* w, int do_norm, float eps, const float* rope, int rot, uint16_t* out,
+                            int64_t S, int64_t H, int64_t D, void* stream) {
+  const char* what = "h3q_qk_norm_rope";
+  if (h3q_status s = check_shape(S, H, what)) return s;
+  if (D < 1 || D > 256) return fail(H3Q_ERR_UNSUPPORTED, "%s: head_dim %lld (1..256)", what, (long long)D);
+  if (S == 0) return H3Q_OK;
+  if (!x || !out) return fail(H3Q_ERR_ARG, "%s: null pointer", what);
+  if (col_off < 0 || head_stride < 0 || row_stride < col_off + (H - 1) * head_stride + D)
+    return fail(H3Q_ERR_ARG, "%s: heads at column %lld (stride %lld) outside a row of %lld elements", what,
+                (long long)col_off, (long long)head_stride, (long long)row_stride);
+  if (!rope) rot = 0;  // no table: no rotation (the reference's launch passes rot = 0)
+  if (rot < 0 || rot % 2 != 0 || rot > D)
+    return fail(H3Q_ERR_ARG, "%s: rot %d must be even and within head_dim %lld", what, rot, (long long)D);
+  return cuda_status(h3q::launch_qk_norm_rope(x, row_stride, col_off, head_stride, do_norm ? w : nullptr,
+                                              do_norm ? 1 : 0, eps, rope, rot, out, S, H, D, (cudaStream_t)stream),
+                     what);
+}
+
+h3q_status h3q_attend_qkv(const uint16_t* qkv, int64_t qkv_width, int64_t q_col, int64_t k_col, int64_t v_col,
+                          const uint16_t* q_norm, const uint16_t* k_norm, int do_norm, float eps, const float* rope,
+                          int rot, uint16_t* out, int64_t S, int64_t H, int flags, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  const char* what = "h3q_attend_qkv";
+  if (h3q_status s = check_shape(S, H, what)) return s;
+  if (h3q_status s = check_flags(flags, what)) return s;
+  if (S == 0) return H3Q_OK;
+  if (!qkv || !out) return fail(H3Q_ERR_ARG, "%s: null pointer", what);
+  const int64_t cols[3] = {q_col, k_col, v_col};
+  for (int i = 0; i < 3; ++i)
+    if (cols[i] < 0 || qkv_width < cols[i] + H * HD)
+      return fail(H3Q_ERR_ARG, "%s: columns [%lld, %lld) outside a qkv row of width %lld", what, (long long)cols[i],
+                  (long long)(cols[i] + H * HD), (long long)qkv_width);
+  if ((reinterpret_cast<uintptr_t>(qkv) & 7u) || qkv_width % 4 || q_col % 4 || k_col % 4)
+    return fail(H3Q_ERR_ARG, "%s: qkv must be 8-byte aligned with width and q / k columns multiples of 4", what);
+  if (do_norm && ((q_norm && (reinterpret_cast<uintptr_t>(q_norm) & 7u)) ||
+                  (k_norm && (reinterpret_cast<uintptr_t>(k_norm) & 7u))))
+    return fail(H3Q_ERR_ARG, "%s: norm weights must be 8-byte aligned", what);
+  if (!rope) rot = 0;
+  if (rot < 0 || rot % 8 != 0 || rot > HD)
+    return fail(H3Q_ERR_UNSUPPORTED, "%s: this build rotates rot %% 8 == 0 dims, rot <= 128 (rot = %d); use "
+                "h3q_qk_norm_rope + h3q_attention_qkv", what, rot);
+  if (rot && !aligned16(rope)) return fail(H3Q_ERR_ARG, "%s: the rope table must be 16-byte aligned", what);
+  if (!aligned16(out)) return fail(H3Q_ERR_ARG, "%s: out must be 16-byte aligned", what);
+  const AttnWs need = carve(nullptr, S, S, H);
+  if (!workspace || workspace_bytes < need.bytes)
+    return fail(H3Q_ERR_WORKSPACE, "%s: workspace of %zu bytes, need %zu", what, workspace_bytes, need.bytes);
+  if (!aligned16(workspace)) return fail(H3Q_ERR_ARG, "%s: workspace must be 16-byte aligned", what);
+  const AttnWs w = carve(static_cast<uint8_t*>(workspace), S, S, H);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int* err = h3q::error_word_current();
+  if (!err) return fail(H3Q_ERR_CUDA, "%s: could not set up the device error word", what);
+  const bool block = (flags & H3Q_ATTN_SCALE_BLOCK128) != 0;
+  const bool bf16pv = (flags & H3Q_ATTN_PV_BF16) != 0;
+  const int dn = do_norm ? 1 : 0;
+  const uint16_t* qw = dn ? q_norm : nullptr;
+  const uint16_t* kw = dn ? k_norm : nullptr;
+  // qk_norm_rope of q and k (dit.rs:748-749) fused into the K mean and the Q / K quantisation of attention_qkv
+  if (h3q_status s = cuda_status(h3q::launch_kmean_rope(qkv, qkv_width, k_col, kw, dn, eps, rope, rot, S, H, w.kmean,
+                                                        w.part, st), what))
+    return s;
+  if (h3q_status s = cuda_status(h3q::launch_qk_rope_quant(qkv, qkv_width, q_col, qw, dn, eps, rope, rot, nullptr,
+                                                           w.q8, w.qs, S, H, block, st), what))
+    return s;
+  if (h3q_status s = cuda_status(h3q::launch_qk_rope_quant(qkv, qkv_width, k_col, kw, dn, eps, rope, rot, w.kmean,
+                                                           w.k8, w.ks, S, H, block, st), what))
+    return s;
+  if (h3q_status s = cuda_status(h3q::launch_v_layout(qkv, qkv_width, v_col, w.vt, S, H, bf16pv, st), what)) return s;
+  return cuda_status(h3q::launch_attention(w.q8, w.qs, S, w.k8, w.ks, w.vt, out, S, H, bf16pv, nullptr, err, st),
                      what);
 }
 

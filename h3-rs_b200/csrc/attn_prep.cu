@@ -10,6 +10,10 @@
 //   v_layout    VToF16 (attn8.rs:55-65) with a transposed output: [S, H, 128] (row stride, column offset) ->
 //               [H, 128, Sp] f16 (or bf16), so V is a K-major operand of the P.V MMA.
 //
+//   qk_norm_rope  (kernels.rs:86-126) per-head RMSNorm + split-half RoPE, standalone, and fused into the K mean and
+//               the Q / K quantisation for the DiT's attention step (dit.rs:741-757), so the normalised q and k
+//               never reach memory.
+//
 // Layouts: codes [H, S, 128] int8; scales [H, Sp] f32 with Sp = roundup(S, 128) (block mode: every token of a
 // block holds the block's scale; entries S..Sp-1 are zero).
 #include <cstdint>
@@ -245,6 +249,269 @@ __global__ void __launch_bounds__(256) v_layout_kernel(const uint16_t* __restric
   }
 }
 
+// ------------------------------------------------------------------------------- q/k RMSNorm + split-half RoPE
+//
+// qk_norm_rope (kernels.rs:86-126) per (token, head) row of D <= 256 dims, bf16 in and out:
+//   ss   = sum of v_d^2 in the reference's order: 32-lane xor trees (levels 16 .. 1) inside each 32-dim slice,
+//          then an xor tree over the slice sums (lane 0's view: ((t0 + t4) + (t2 + t6)) + ((t1 + t5) + (t3 + t7)),
+//          absent slices zero); squares of bf16 values are exact in f32, so no contraction question arises.
+//   v    = (v * rsqrtf(ss / D + eps)) * w_d                                   (when normalising)
+//   o    = fma(v_d, cos, -(v_{d+half} * sin))  for d < half,
+//          fma(v_d, cos,   v_{d-half} * sin)   for half <= d < rot,           (cos, sin = table[s, d mod half])
+//          v_d otherwise;  the reference's compiled kernel rounds the second product and fuses the first (measured
+//          against it: every other association differs in about 1e-5 of the outputs).
+//   out  = bf16(o), nearest even, NaN -> 0x7fc0 (the reference's f2bf).
+namespace {
+
+__device__ __forceinline__ uint16_t f2bf_ref(float f) {
+  const uint32_t u = __float_as_uint(f);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return 0x7fc0;
+  return (uint16_t)((u + 0x7fffu + ((u >> 16) & 1u)) >> 16);
+}
+
+__device__ __forceinline__ float rope_lo(float v, float c, float partner, float sn) {
+  return __fmaf_rn(v, c, -__fmul_rn(partner, sn));
+}
+__device__ __forceinline__ float rope_hi(float v, float c, float partner, float sn) {
+  return __fmaf_rn(v, c, __fmul_rn(partner, sn));
+}
+
+// The general form: one warp per row, lane l holding dims 32 i + l (the reference's thread d sits in slice d / 32 at
+// lane d % 32); partners of the rotation through a per-warp row buffer.
+__global__ void __launch_bounds__(256) qk_norm_rope_kernel(const uint16_t* __restrict__ x, int64_t rs, int64_t col,
+                                                           int64_t hs, const uint16_t* __restrict__ w, int do_norm,
+                                                           float eps, const float* __restrict__ cs, int rot,
+                                                           uint16_t* __restrict__ out, int64_t S, int H, int D) {
+  __shared__ float buf[8][256];
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  const int NS = (D + 31) >> 5, half = rot >> 1;
+  const int64_t rows = S * H;
+  for (int64_t row = (int64_t)blockIdx.x * 8 + wp; row < rows; row += (int64_t)gridDim.x * 8) {
+    const int64_t s = row / H;
+    const int h = (int)(row - s * H);
+    const uint16_t* xr = x + s * rs + col + (int64_t)h * hs;
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int d = 32 * i + lane;
+      v[i] = (i < NS && d < D) ? bf2f(__ldg(xr + d)) : 0.f;
+    }
+    if (do_norm) {
+      float t[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        float a = __fmul_rn(v[i], v[i]);
+        if (i < NS) {
+#pragma unroll
+          for (int o = 16; o > 0; o >>= 1) a = __fadd_rn(a, __shfl_xor_sync(0xffffffffu, a, o));
+        }
+        t[i] = a;
+      }
+      const float ss = __fadd_rn(__fadd_rn(__fadd_rn(t[0], t[4]), __fadd_rn(t[2], t[6])),
+                                 __fadd_rn(__fadd_rn(t[1], t[5]), __fadd_rn(t[3], t[7])));
+      const float inv = rsqrtf(__fadd_rn(__fdiv_rn(ss, (float)D), eps));
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int d = 32 * i + lane;
+        if (i < NS) v[i] = __fmul_rn(__fmul_rn(v[i], inv), (w && d < D) ? bf2f(__ldg(w + d)) : 1.f);
+      }
+    }
+    if (half > 0) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (i < NS) buf[wp][32 * i + lane] = v[i];
+      __syncwarp();
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int d = 32 * i + lane;
+      if (i >= NS || d >= D) continue;
+      float o = v[i];
+      if (d < rot) {
+        const int j = d < half ? d : d - half;
+        const float c = __ldg(cs + s * half + j), sn = __ldg(cs + (S + s) * half + j);
+        o = d < half ? rope_lo(v[i], c, buf[wp][d + half], sn) : rope_hi(v[i], c, buf[wp][d - half], sn);
+      }
+      out[row * D + d] = f2bf_ref(o);
+    }
+    if (half > 0) __syncwarp();  // the row buffer is rewritten by the next row
+  }
+}
+
+// The D = 128 form used inside the attention front end: lane l holds dims 4l .. 4l+3.  The reference's slice
+// w = l / 8 and lane 4 (l % 8) + j, so its xor levels 16, 8, 4 are lanes xor 4, 2, 1 here and levels 2, 1 stay in
+// the thread; the slice sums meet over lanes xor 16 and 8.  Rotation partners (half % 4 == 0) are lanes l +- half/4,
+// same j.  Returns the row as the reference's bf16 q / k values (in f32).
+__device__ __forceinline__ void norm_rope_row128(float (&v)[4], int lane, const uint16_t* __restrict__ w,
+                                                 int do_norm, float eps, const float* __restrict__ cs, int half,
+                                                 int64_t s, int64_t S) {
+  if (do_norm) {
+    float a[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) a[j] = __fmul_rn(v[j], v[j]);
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) a[j] = __fadd_rn(a[j], __shfl_xor_sync(0xffffffffu, a[j], o));
+    }
+    float t = __fadd_rn(__fadd_rn(a[0], a[2]), __fadd_rn(a[1], a[3]));
+    t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 16));
+    t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 8));
+    const float inv = rsqrtf(__fadd_rn(__fdiv_rn(t, 128.f), eps));
+    float wv[4] = {1.f, 1.f, 1.f, 1.f};
+    if (w) {
+      const uint2 wr = __ldg(reinterpret_cast<const uint2*>(w) + lane);
+      wv[0] = __uint_as_float(wr.x << 16);
+      wv[1] = __uint_as_float(wr.x & 0xffff0000u);
+      wv[2] = __uint_as_float(wr.y << 16);
+      wv[3] = __uint_as_float(wr.y & 0xffff0000u);
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = __fmul_rn(__fmul_rn(v[j], inv), wv[j]);
+  }
+  if (half > 0) {
+    const int q = half >> 2, d0 = 4 * lane;
+    float up[4], dn[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      up[j] = __shfl_down_sync(0xffffffffu, v[j], q);
+      dn[j] = __shfl_up_sync(0xffffffffu, v[j], q);
+    }
+    if (d0 < 2 * half) {
+      const bool lo = d0 < half;
+      const int jj = lo ? d0 : d0 - half;
+      const float4 c = __ldg(reinterpret_cast<const float4*>(cs + s * half + jj));
+      const float4 sn = __ldg(reinterpret_cast<const float4*>(cs + (S + s) * half + jj));
+      const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {sn.x, sn.y, sn.z, sn.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = lo ? rope_lo(v[j], cc[j], up[j], ss[j]) : rope_hi(v[j], cc[j], dn[j], ss[j]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) v[j] = bf2f(f2bf_ref(v[j]));
+}
+
+__device__ __forceinline__ void load_row128(const uint16_t* __restrict__ p, int lane, float (&v)[4]) {
+  const uint2 r = __ldg(reinterpret_cast<const uint2*>(p) + lane);
+  v[0] = __uint_as_float(r.x << 16);
+  v[1] = __uint_as_float(r.x & 0xffff0000u);
+  v[2] = __uint_as_float(r.y << 16);
+  v[3] = __uint_as_float(r.y & 0xffff0000u);
+}
+
+// K column sums of the normalised, rotated K rows, chunked as kmean_partial_kernel: warp = (chunk, head), rows of
+// the chunk in order.  part[p, h*128 + d].
+__global__ void __launch_bounds__(256) kmean_rope_partial_kernel(const uint16_t* __restrict__ x, int64_t rs,
+                                                                 int64_t col, const uint16_t* __restrict__ w,
+                                                                 int do_norm, float eps,
+                                                                 const float* __restrict__ cs, int half,
+                                                                 float* __restrict__ part, int64_t S, int H,
+                                                                 int rows_per) {
+  const int lane = threadIdx.x & 31;
+  const int h = blockIdx.y * 8 + (threadIdx.x >> 5);
+  if (h >= H) return;
+  const int64_t r0 = (int64_t)blockIdx.x * rows_per;
+  const int64_t r1 = r0 + rows_per < S ? r0 + rows_per : S;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  constexpr int U = 4;
+  int64_t r = r0;
+  for (; r + U <= r1; r += U) {
+    float v[U][4];
+#pragma unroll
+    for (int u = 0; u < U; ++u) load_row128(x + (r + u) * rs + col + (int64_t)h * HD, lane, v[u]);
+#pragma unroll
+    for (int u = 0; u < U; ++u) norm_rope_row128(v[u], lane, w, do_norm, eps, cs, half, r + u, S);
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[j] = __fadd_rn(acc[j], v[u][j]);
+  }
+  for (; r < r1; ++r) {
+    float v[4];
+    load_row128(x + r * rs + col + (int64_t)h * HD, lane, v);
+    norm_rope_row128(v, lane, w, do_norm, eps, cs, half, r, S);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[j] = __fadd_rn(acc[j], v[j]);
+  }
+  reinterpret_cast<float4*>(part + (int64_t)blockIdx.x * H * HD + (int64_t)h * HD)[lane] =
+      make_float4(acc[0], acc[1], acc[2], acc[3]);
+}
+
+// Normalise + rotate + (K: subtract the column mean) + quantise, as qk_norm_rope then quant_heads.  CTA = (128-token
+// block, head), warp = 16 tokens of the block.  Per-token scales, or (BLOCK) one scale per block.  Writes every
+// scale entry of the block, zero past S.
+template <bool BLOCK>
+__global__ void __launch_bounds__(256) qk_rope_quant_kernel(const uint16_t* __restrict__ x, int64_t rs, int64_t col,
+                                                            const uint16_t* __restrict__ w, int do_norm, float eps,
+                                                            const float* __restrict__ cs, int half,
+                                                            const float* __restrict__ mean,
+                                                            int8_t* __restrict__ codes, float* __restrict__ scales,
+                                                            int64_t S, int64_t Sp) {
+  __shared__ float red[8];
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+  const int h = blockIdx.y;
+  const int64_t s0 = (int64_t)blockIdx.x * 128 + wp * 16;
+  float mv[4] = {0.f, 0.f, 0.f, 0.f};
+  if (mean) {
+    const float4 m4 = __ldg(reinterpret_cast<const float4*>(mean + (int64_t)h * HD) + lane);
+    mv[0] = m4.x; mv[1] = m4.y; mv[2] = m4.z; mv[3] = m4.w;
+  }
+  float v[16][4];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    if (s0 + k < S) load_row128(x + (s0 + k) * rs + col + (int64_t)h * HD, lane, v[k]);
+    else v[k][0] = v[k][1] = v[k][2] = v[k][3] = 0.f;
+  }
+  float bm = 0.f;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const int64_t s = s0 + k;
+    if (s < S) {  // warp-uniform
+      norm_rope_row128(v[k], lane, w, do_norm, eps, cs, half, s, S);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[k][j] = __fsub_rn(v[k][j], mv[j]);
+    }
+    float m = fmaxf(fmaxf(fabsf(v[k][0]), fabsf(v[k][1])), fmaxf(fabsf(v[k][2]), fabsf(v[k][3])));
+    if (BLOCK) {
+      bm = fmaxf(bm, m);
+    } else {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      const float sc = fmaxf(__fdiv_rn(m, 127.f), 1e-20f);
+      if (s < S) {
+        const float inv = __fdiv_rn(1.f, sc);
+        const uint32_t p = q127(v[k][0], inv) | (q127(v[k][1], inv) << 8) | (q127(v[k][2], inv) << 16) |
+                           (q127(v[k][3], inv) << 24);
+        reinterpret_cast<uint32_t*>(codes + ((int64_t)h * S + s) * HD)[lane] = p;
+      }
+      if (lane == 0 && s < Sp) scales[(int64_t)h * Sp + s] = s < S ? sc : 0.f;
+    }
+  }
+  if (BLOCK) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
+    if (lane == 0) red[wp] = bm;
+    __syncthreads();
+    float m = red[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) m = fmaxf(m, red[i]);
+    const float sc = fmaxf(__fdiv_rn(m, 127.f), 1e-20f);
+    const float inv = __fdiv_rn(1.f, sc);
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const int64_t s = s0 + k;
+      if (s < S) {
+        const uint32_t p = q127(v[k][0], inv) | (q127(v[k][1], inv) << 8) | (q127(v[k][2], inv) << 16) |
+                           (q127(v[k][3], inv) << 24);
+        reinterpret_cast<uint32_t*>(codes + ((int64_t)h * S + s) * HD)[lane] = p;
+      }
+      if (lane == 0) scales[(int64_t)h * Sp + s] = s < S ? sc : 0.f;
+    }
+  }
+}
+
+}  // namespace
+
 // ------------------------------------------------------------------------------------------------ launchers
 
 size_t kmean_workspace_bytes(int64_t S, int64_t H) {
@@ -293,6 +560,46 @@ cudaError_t launch_v_layout(const uint16_t* x, int64_t rs, int64_t col, uint16_t
   const bool vec = (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && rs % 8 == 0 && col % 8 == 0;
   if (vec) v_layout_kernel<true><<<grid, 256, 0, st>>>(x, rs, col, vt, S, Sp, keep_bf16 ? 1 : 0);
   else v_layout_kernel<false><<<grid, 256, 0, st>>>(x, rs, col, vt, S, Sp, keep_bf16 ? 1 : 0);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_qk_norm_rope(const uint16_t* x, int64_t rs, int64_t col, int64_t hs, const uint16_t* w,
+                                int do_norm, float eps, const float* cs, int rot, uint16_t* out, int64_t S, int64_t H,
+                                int64_t D, cudaStream_t st) {
+  if (S <= 0 || H <= 0 || D <= 0) return cudaSuccess;
+  const int64_t rows = S * H;
+  int64_t blocks = (rows + 7) / 8;
+  const int64_t cap = (int64_t)sm_count(0) * 16;
+  if (blocks > cap) blocks = cap;
+  qk_norm_rope_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, rs, col, hs, w, do_norm, eps, cs, rot, out, S, (int)H,
+                                                        (int)D);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_kmean_rope(const uint16_t* x, int64_t rs, int64_t col, const uint16_t* w, int do_norm, float eps,
+                              const float* cs, int rot, int64_t S, int64_t H, float* mean, float* part,
+                              cudaStream_t st) {
+  if (S <= 0 || H <= 0) return cudaSuccess;
+  int parts, rows_per;
+  kmean_partition(S, parts, rows_per);
+  kmean_rope_partial_kernel<<<dim3((unsigned)parts, (unsigned)((H + 7) / 8)), 256, 0, st>>>(
+      x, rs, col, w, do_norm, eps, cs, rot / 2, part, S, (int)H, rows_per);
+  const int C = (int)(H * HD);
+  const float inv_s = (float)(1.0 / (double)S);
+  kmean_final_kernel<<<(C + 255) / 256, 256, 0, st>>>(part, parts, mean, C, inv_s);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_qk_rope_quant(const uint16_t* x, int64_t rs, int64_t col, const uint16_t* w, int do_norm,
+                                 float eps, const float* cs, int rot, const float* mean, int8_t* codes, float* scales,
+                                 int64_t S, int64_t H, bool block128, cudaStream_t st) {
+  if (S <= 0 || H <= 0) return cudaSuccess;
+  const int64_t Sp = (S + 127) / 128 * 128;
+  const dim3 grid((unsigned)(Sp / 128), (unsigned)H);
+  if (block128)
+    qk_rope_quant_kernel<true><<<grid, 256, 0, st>>>(x, rs, col, w, do_norm, eps, cs, rot / 2, mean, codes, scales, S, Sp);
+  else
+    qk_rope_quant_kernel<false><<<grid, 256, 0, st>>>(x, rs, col, w, do_norm, eps, cs, rot / 2, mean, codes, scales, S, Sp);
   return cudaGetLastError();
 }
 

@@ -122,6 +122,8 @@ __device__ __forceinline__ uint32_t code_of(float t) {
 // by TMA (the row viewed as [K*es/128] x 128-byte lines, 128-byte swizzle) into a 3-stage ring, two rows ahead
 // of the compute; with the swizzle each thread's 16-byte reads of its own line are bank-conflict free.
 constexpr int kQStages = 3;
+// MOD keeps two rows in flight: its shared-memory table slices (below) would otherwise cost a CTA per SM.
+constexpr int kQStagesMod = 2;
 
 // ROT_ONLY: write bf16(rotated row) to `ybf` instead of codes and scales (rotate_activation, weights.rs:482-489,
 // for the paths that quantize a pre-rotated activation).
@@ -144,12 +146,13 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
                                                          int8_t* __restrict__ q, float* __restrict__ scale,
                                                          int64_t M, int K, int box_rows, int boxes_per_row,
                                                          int* err, uint16_t* __restrict__ ybf, const ModArgs mod) {
+  constexpr int NST = MOD ? kQStagesMod : kQStages;
   extern __shared__ uint8_t qsm_raw[];
   // align by offsetting the __shared__ array itself, so the compiler keeps shared-space (LDS/STS) accesses
   uint8_t* qsm = qsm_raw + ((1024u - (smem_u32(qsm_raw) & 1023u)) & 1023u);
-  __shared__ uint64_t full[kQStages];
+  __shared__ uint64_t full[NST];
   __shared__ unsigned s_max[3], s_max2[3];
-  __shared__ float s_red[17];
+  __shared__ float s_red[2][16];
   __shared__ int s_abort;
   constexpr int ES = sizeof(Tin);
   constexpr int LINES = 64 * ES / 128;  // 128-byte lines per thread: 1 (16-bit) or 2 (f32)
@@ -160,7 +163,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
   const uint32_t stage_bytes = (row_bytes + 1023u) & ~1023u;
 
   if (t == 0) {
-    for (int s = 0; s < kQStages; ++s) mbar_init(&full[s], 1);
+    for (int s = 0; s < NST; ++s) mbar_init(&full[s], 1);
     s_max[0] = s_max[1] = s_max[2] = 0u;
     s_max2[0] = s_max2[1] = s_max2[2] = 0u;
     s_abort = 0;
@@ -181,29 +184,82 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
   auto row_of = [&](int64_t i) -> int64_t { return MOD ? rb0 + i : rb0 + i * (int64_t)gridDim.x; };
   if (t == 0) {
     tma_prefetch_desc(&tmx);
-    for (int s = 0; s < kQStages; ++s) {
+    for (int s = 0; s < NST; ++s) {
       const int64_t r = row_of(s);
       if (r < rend) issue(r, s);
     }
   }
   uint32_t tab_idx = 0xffffffffu;  // MOD: table row held in this thread's shared-memory slice
-  if (MOD && owner) {
-    // the norm weight of the thread's columns, once: 16-byte word c at wsm + (c * blockDim + t) * 16
-    uint8_t* wsm = qsm + (size_t)kQStages * stage_bytes + (size_t)blockDim.x * 256;
-    const uint4* wv = reinterpret_cast<const uint4*>(mod.w + 64 * t);
+  const int nown = 4 * G;           // owner threads (the table slices' stride)
+  // MOD: rms_modulate's 16 group sums of squares of the landed row at `base` (128-byte-swizzled lines) -> dst[16].
+  // The next row's sums are formed under the current row's max barrier, so a row costs one CTA barrier.
+  auto partials = [&](const uint8_t* base, float* dst) {
+    const int nw = blockDim.x >> 5, wp = t >> 5, ln = t & 31;
+    if (blockDim.x >= 64) {
+      // thread m < 64 holds the partials of reference threads 8m .. 8m+7 (one 16-byte piece per 512-element
+      // stride, conflict-free); the reference's 32-thread xor trees are 4 neighbouring lanes here: levels 16 and
+      // 8 cross lanes (xor 2, xor 1), levels 4, 2, 1 stay inside the thread
+      float a[8];
 #pragma unroll
-    for (int c = 0; c < 8; ++c) *reinterpret_cast<uint4*>(wsm + ((size_t)c * blockDim.x + t) * 16) = __ldg(wv + c);
+      for (int i = 0; i < 8; ++i) a[i] = 0.f;
+      if (t < 64) {
+        for (int c0 = 8 * t; c0 < K; c0 += 512) {
+          const int line = c0 >> 6, ch = (c0 >> 3) & 7;
+          const uint4 r8 = *reinterpret_cast<const uint4*>(base + line * 128 + ((ch ^ (line & 7)) << 4));
+          const uint32_t ww[4] = {r8.x, r8.y, r8.z, r8.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const float x0 = __uint_as_float(ww[i] << 16), x1 = __uint_as_float(ww[i] & 0xffff0000u);
+            a[2 * i] = __fmaf_rn(x0, x0, a[2 * i]);
+            a[2 * i + 1] = __fmaf_rn(x1, x1, a[2 * i + 1]);
+          }
+        }
+      }
+#pragma unroll
+      for (int lo = 2; lo >= 1; lo >>= 1) {  // tree levels 16 (lanes xor 2) and 8 (lanes xor 1)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) a[i] = __fadd_rn(a[i], __shfl_xor_sync(0xffffffffu, a[i], lo));
+      }
+#pragma unroll
+      for (int o = 4; o >= 1; o >>= 1) {  // tree levels 4, 2, 1
+        float b[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) b[i] = __fadd_rn(a[i], a[i ^ o]);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) a[i] = b[i];
+      }
+      if (t < 64 && (t & 3) == 0) dst[t >> 2] = a[0];
+    } else {
+      for (int rw = wp; rw < 16; rw += nw) {
+        float sq = 0.f;
+        for (int c = 32 * rw + ln; c < K; c += 512) {
+          const int line = c >> 6, ch = (c >> 3) & 7;
+          const float xv = bf2f(*reinterpret_cast<const uint16_t*>(base + line * 128 + ((ch ^ (line & 7)) << 4) +
+                                                                   (c & 7) * 2));
+          sq = __fmaf_rn(xv, xv, sq);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sq = __fadd_rn(sq, __shfl_xor_sync(0xffffffffu, sq, o));
+        if (ln == 0) dst[rw] = sq;
+      }
+    }
+  };
+  bool stop = false;
+  if (MOD && rb0 < rend) {
+    const bool landed = mbar_wait_bounded(&full[0], 0u, &s_abort, err, kDevTimeoutFull);
+    partials(qsm, s_red[0]);
+    stop = !__syncthreads_and(landed);
   }
   int it = 0;
   for (int64_t row = row_of(0); row < rend; row = row_of(++it)) {
-    const int stage = it % kQStages;
+    const int stage = it % NST;
     if (MOD && owner) {
       // The thread's bf16 scale / shift values of the row's table row live in its slice of shared memory
-      // (16-byte word i at tab + (i * blockDim + t) * 16, columns 4i .. 4i+3 as scale pairs then shift pairs:
+      // (16-byte word i at tab + (i * 4G + t) * 16, columns 4i .. 4i+3 as scale pairs then shift pairs:
       // conflict-free), reloaded, before the row has landed, only when the table index changes.
       const uint32_t ridx = __ldg(mod.idx + row);
       if (ridx != tab_idx) {
-        uint8_t* tab = qsm + (size_t)kQStages * stage_bytes;
+        uint8_t* tab = qsm + (size_t)NST * stage_bytes;
         const float4* scv = reinterpret_cast<const float4*>(mod.scale + (int64_t)ridx * K + 64 * t);
         const float4* shv = reinterpret_cast<const float4*>(mod.shift + (int64_t)ridx * K + 64 * t);
 #pragma unroll 4
@@ -214,75 +270,26 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
           asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(o[1]) : "f"(a.w), "f"(a.z));
           asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(o[2]) : "f"(b.y), "f"(b.x));
           asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(o[3]) : "f"(b.w), "f"(b.z));
-          *reinterpret_cast<uint4*>(tab + ((size_t)q4 * blockDim.x + t) * 16) = make_uint4(o[0], o[1], o[2], o[3]);
+          *reinterpret_cast<uint4*>(tab + ((size_t)q4 * nown + t) * 16) = make_uint4(o[0], o[1], o[2], o[3]);
         }
         tab_idx = ridx;
       }
     }
-    const bool landed = mbar_wait_bounded(&full[stage], (uint32_t)(it / kQStages) & 1u, &s_abort, err, kDevTimeoutFull);
-    if (!__syncthreads_and(landed)) break;  // the whole CTA gives up together (barriers follow)
     float inv_rms = 0.f;
-    if (MOD) {
-      // the 512 partial sums of rms_modulate's row block, read from the landed row (128-byte-swizzled lines)
-      const uint8_t* base = qsm + (size_t)stage * stage_bytes;
-      const int nw = blockDim.x >> 5, wp = t >> 5, ln = t & 31;
-      if (blockDim.x >= 64) {
-        // thread m < 64 holds the partials of reference threads 8m .. 8m+7 (one 16-byte piece per 512-element
-        // stride, conflict-free); the reference's 32-thread xor trees are 4 neighbouring lanes here: levels 16 and
-        // 8 cross lanes (xor 2, xor 1), levels 4, 2, 1 stay inside the thread
-        float a[8];
+    if (!MOD) {
+      const bool landed = mbar_wait_bounded(&full[stage], (uint32_t)(it / NST) & 1u, &s_abort, err, kDevTimeoutFull);
+      if (!__syncthreads_and(landed)) break;  // the whole CTA gives up together (barriers follow)
+    } else {
+      if (stop) break;  // the row did not land (the CTA agreed under the previous barrier)
+      // the reference's last xor tree over its 16 group sums, as lane 0 forms it (level 16 adds zeros)
+      const float* g = s_red[it & 1];
+      float a8[8], a4[4];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) a[i] = 0.f;
-        if (t < 64) {
-          for (int c0 = 8 * t; c0 < K; c0 += 512) {
-            const int line = c0 >> 6, ch = (c0 >> 3) & 7;
-            const uint4 r8 = *reinterpret_cast<const uint4*>(base + line * 128 + ((ch ^ (line & 7)) << 4));
-            const uint32_t ww[4] = {r8.x, r8.y, r8.z, r8.w};
+      for (int i = 0; i < 8; ++i) a8[i] = __fadd_rn(g[i], g[i + 8]);
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const float x0 = __uint_as_float(ww[i] << 16), x1 = __uint_as_float(ww[i] & 0xffff0000u);
-              a[2 * i] = __fmaf_rn(x0, x0, a[2 * i]);
-              a[2 * i + 1] = __fmaf_rn(x1, x1, a[2 * i + 1]);
-            }
-          }
-        }
-#pragma unroll
-        for (int lo = 2; lo >= 1; lo >>= 1) {  // tree levels 16 (lanes xor 2) and 8 (lanes xor 1)
-#pragma unroll
-          for (int i = 0; i < 8; ++i) a[i] = __fadd_rn(a[i], __shfl_xor_sync(0xffffffffu, a[i], lo));
-        }
-#pragma unroll
-        for (int o = 4; o >= 1; o >>= 1) {  // tree levels 4, 2, 1
-          float b[8];
-#pragma unroll
-          for (int i = 0; i < 8; ++i) b[i] = __fadd_rn(a[i], a[i ^ o]);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) a[i] = b[i];
-        }
-        if (t < 64 && (t & 3) == 0) s_red[t >> 2] = a[0];
-      } else {
-        for (int rw = wp; rw < 16; rw += nw) {
-          float sq = 0.f;
-          for (int c = 32 * rw + ln; c < K; c += 512) {
-            const int line = c >> 6, ch = (c >> 3) & 7;
-            const float xv = bf2f(*reinterpret_cast<const uint16_t*>(base + line * 128 + ((ch ^ (line & 7)) << 4) +
-                                                                     (c & 7) * 2));
-            sq = __fmaf_rn(xv, xv, sq);
-          }
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) sq = __fadd_rn(sq, __shfl_xor_sync(0xffffffffu, sq, o));
-          if (ln == 0) s_red[rw] = sq;
-        }
-      }
-      __syncthreads();
-      if (wp == 0) {
-        float tt = ln < 16 ? s_red[ln] : 0.f;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) tt = __fadd_rn(tt, __shfl_xor_sync(0xffffffffu, tt, o));
-        if (ln == 0) s_red[16] = tt;
-      }
-      __syncthreads();
-      inv_rms = rsqrtf(__fadd_rn(__fdiv_rn(s_red[16], (float)K), mod.eps));
+      for (int i = 0; i < 4; ++i) a4[i] = __fadd_rn(a8[i], a8[i + 4]);
+      const float tot = __fadd_rn(__fadd_rn(a4[0], a4[2]), __fadd_rn(a4[1], a4[3]));
+      inv_rms = rsqrtf(__fadd_rn(__fdiv_rn(tot, (float)K), mod.eps));
     }
     // The thread's 64 values as 32 register pairs: v2[k] = elements (2k, 2k + 1).  Pairs of neighbouring elements
     // follow the same butterfly through digits 1..3, so those stages run as paired f32x2 operations.
@@ -293,16 +300,15 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
       // the roundings are cvt.rn (nearest even, as the reference's f2bf for every finite value; a NaN stays a
       // NaN).  One 16-byte chunk at a time keeps the register footprint of the pass small.
       uint8_t* own = qsm + (size_t)stage * stage_bytes + (size_t)t * 128;
-      const uint8_t* tab = qsm + (size_t)kQStages * stage_bytes;
-      const uint8_t* wsm = tab + (size_t)blockDim.x * 256;
+      const uint8_t* tab = qsm + (size_t)NST * stage_bytes;
       const f2 inv2 = pk(inv_rms, inv_rms), one2 = pk(1.f, 1.f);
 #pragma unroll 1
       for (int c = 0; c < 8; ++c) {
         uint4* px = reinterpret_cast<uint4*>(own + ((c ^ (t & 7)) << 4));
         const uint4 raw = *px;
-        const uint4 w8 = *reinterpret_cast<const uint4*>(wsm + ((size_t)c * blockDim.x + t) * 16);
-        const uint4 tb0 = *reinterpret_cast<const uint4*>(tab + ((size_t)(2 * c) * blockDim.x + t) * 16);
-        const uint4 tb1 = *reinterpret_cast<const uint4*>(tab + ((size_t)(2 * c + 1) * blockDim.x + t) * 16);
+        const uint4 w8 = __ldg(reinterpret_cast<const uint4*>(mod.w + 64 * t) + c);
+        const uint4 tb0 = *reinterpret_cast<const uint4*>(tab + ((size_t)(2 * c) * nown + t) * 16);
+        const uint4 tb1 = *reinterpret_cast<const uint4*>(tab + ((size_t)(2 * c + 1) * nown + t) * 16);
         const uint32_t xx[4] = {raw.x, raw.y, raw.z, raw.w}, ww[4] = {w8.x, w8.y, w8.z, w8.w};
         const uint32_t sp[4] = {tb0.x, tb0.y, tb1.x, tb1.y}, hp[4] = {tb0.z, tb0.w, tb1.z, tb1.w};
         uint32_t o[4];
@@ -424,11 +430,23 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
     const unsigned mw = __reduce_max_sync(0xffffffffu, __float_as_uint(m));
     const int slot = it % 3;
     if ((t & 31) == 0 && !ROT_ONLY) atomicMax(&s_max[slot], mw);
-    __syncthreads();  // the whole row is read out of `stage` and its max is complete
+    if (MOD) {
+      // the next row's group sums (it was issued a row earlier), under this row's barrier
+      bool ok = true;
+      const int64_t nx = row_of(it + 1);
+      if (nx < rend) {
+        const int ns = (it + 1) % NST;
+        ok = mbar_wait_bounded(&full[ns], (uint32_t)((it + 1) / NST) & 1u, &s_abort, err, kDevTimeoutFull);
+        partials(qsm + (size_t)ns * stage_bytes, s_red[(it + 1) & 1]);
+      }
+      stop = !__syncthreads_and(ok);  // the whole row is read out of `stage` and its max is complete
+    } else {
+      __syncthreads();  // the whole row is read out of `stage` and its max is complete
+    }
     if (t == 0) {
       s_max[(it + 1) % 3] = 0u;
       s_max2[(it + 1) % 3] = 0u;
-      const int64_t nr = row_of(it + kQStages);
+      const int64_t nr = row_of(it + NST);
       if (nr < rend) {
         fence_proxy_async_smem();
         issue(nr, stage);
@@ -538,10 +556,10 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
   __syncthreads();
   if (t == 0) {
     int dummy = 0;
-    for (int k = 0; k < kQStages; ++k) {
-      const int i2 = it + k;  // loads issued for iterations it .. it+kQStages-1 may be pending
+    for (int k = 0; k < NST; ++k) {
+      const int i2 = it + k;  // loads issued for iterations it .. it+NST-1 may be pending
       const int64_t r = row_of(i2);
-      if (r < rend) mbar_wait_bounded(&full[i2 % kQStages], (uint32_t)(i2 / kQStages) & 1u, &dummy, err, kDevTimeoutDrain);
+      if (r < rend) mbar_wait_bounded(&full[i2 % NST], (uint32_t)(i2 / NST) & 1u, &dummy, err, kDevTimeoutDrain);
     }
   }
   __syncthreads();
@@ -607,9 +625,9 @@ static cudaError_t launch_rows(const void* x, int8_t* q, float* scale, int64_t M
   auto fn = q_encode_fn();
   if (!fn) return cudaErrorInvalidValue;
   const size_t stage_bytes = ((size_t)K * ES + 1023) / 1024 * 1024;
-  // MOD adds each thread's 64 columns of the current adaLN table row (bf16 scale / shift, 256 bytes) and of the
-  // norm weight (bf16, 128 bytes)
-  const size_t smem = 1024 + kQStages * stage_bytes + (MOD ? (size_t)threads * 384 : 0);
+  // MOD adds each owner thread's 64 columns of the current adaLN table row (bf16 scale / shift, 256 bytes); the
+  // norm weight, the same for every row, is read through L1
+  const size_t smem = 1024 + (MOD ? kQStagesMod : kQStages) * stage_bytes + (MOD ? (size_t)4 * G * 256 : 0);
   auto kern = quant_rows_kernel<ORDER, Tin, ROT_ONLY, MOD>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;

@@ -71,6 +71,10 @@ SIGNATURES = {
     "h3q_attention_workspace_size": (_sz, [_i64, _i64, _int]),
     "h3q_attention": (_int, [_vp, _vp, _vp, _vp, _i64, _i64, _int, _vp, _sz, _vp]),
     "h3q_attention_qkv": (_int, [_vp, _vp, _vp, _i64, _i64, _vp, _i64, _i64, _int, _vp, _sz, _vp]),
+    "h3q_qk_norm_rope": (_int, [_vp, _i64, _i64, _i64, _vp, _int, ctypes.c_float, _vp, _int, _vp, _i64, _i64, _i64,
+                                _vp]),
+    "h3q_attend_qkv": (_int, [_vp, _i64, _i64, _i64, _i64, _vp, _vp, _int, ctypes.c_float, _vp, _int, _vp, _i64, _i64,
+                              _int, _vp, _sz, _vp]),
     "h3q_attention_rows_workspace_size": (_sz, [_i64, _i64, _i64, _int]),
     "h3q_attention_rows": (_int, [_vp, _i64, _vp, _vp, _i64, _i64, _vp, _i64, _i64, _int, _vp, _sz, _vp]),
     "h3q_attn_kmean_workspace_size": (_sz, [_i64, _i64]),
@@ -351,6 +355,46 @@ def attention_qkv(q, k, qkv, v_col: int, flags: int = 0):
     ws = torch.empty(max(need, 1), dtype=torch.uint8, device=q.device)
     check(lib().h3q_attention_qkv(_p(q), _p(k), _p(qkv), qkv.shape[1], v_col, _p(out), S, H, flags, _p(ws),
                                   ws.numel(), _stream(q.device)))
+    return out
+
+
+def qk_norm_rope(x, col_off: int, heads: int, head_dim: int, norm=None, table=None, rot: int = 0,
+                 head_stride: int | None = None):
+    """kernels::qk_norm_rope(_strided) (kernels.rs:745-800) for bf16 x [S, width]: norm = (weight or None, eps) or
+    None; table = f32 [2, S, rot/2] cos / sin or None.  Returns bf16 [S, heads, head_dim]."""
+    import torch
+    S, width = x.shape
+    do_norm, w, eps = (0, None, 0.0) if norm is None else (1, norm[0], float(norm[1]))
+    if w is not None:
+        w = w.to(torch.bfloat16).contiguous()
+    if table is not None:
+        table = table.to(torch.float32).contiguous()
+    _cuda(x, w, table)
+    out = torch.empty((S, heads, head_dim), dtype=torch.bfloat16, device=x.device)
+    check(lib().h3q_qk_norm_rope(_p(x), width, col_off, head_dim if head_stride is None else head_stride, _p(w),
+                                 do_norm, eps, _p(table), rot if table is not None else 0, _p(out), S, heads,
+                                 head_dim, _stream(x.device)))
+    return out
+
+
+def attend_qkv(qkv, heads: int, norms=None, eps: float = 1e-6, rope=None, rot: int = 0, flags: int = 0):
+    """The DiT's attention step (dit.rs:741-757) on a fused qkv [S, 3 * heads * 128]: q/k RMSNorm (norms = (q weight,
+    k weight) or None) and RoPE (rope = f32 [2, S, rot/2] or None) fused into the int8 attention's front end.
+    Returns bf16 [S, heads * 128]."""
+    import torch
+    S, width = qkv.shape
+    inner = heads * 128
+    qw, kw = (None, None) if norms is None else (norms[0].to(torch.bfloat16).contiguous(),
+                                                 norms[1].to(torch.bfloat16).contiguous())
+    if rope is not None:
+        rope = rope.to(torch.float32).contiguous()
+    _cuda(qkv, qw, kw, rope)
+    out = torch.empty((S, inner), dtype=torch.bfloat16, device=qkv.device)
+    need = lib().h3q_attention_workspace_size(S, heads, flags)
+    ws = torch.empty(max(need, 1), dtype=torch.uint8, device=qkv.device)
+    check(lib().h3q_attend_qkv(_p(qkv), width, 0, inner, 2 * inner, _p(qw), _p(kw), int(norms is not None), eps,
+                               _p(rope), rot if rope is not None else 0, _p(out), S, heads, flags, _p(ws), ws.numel(),
+                               _stream(qkv.device)))
     return out
 
 

@@ -247,6 +247,26 @@ h3q_status h3q_attention_rows(const uint16_t* q, int64_t Sq, const uint16_t* k, 
                               int64_t v_row_stride, int64_t v_col, uint16_t* out, int64_t S, int64_t H, int flags,
                               void* workspace, size_t workspace_bytes, void* stream);
 
+/* Per-head RMSNorm + split-half RoPE, qk_norm_rope (kernels.rs:86-126; op and launch :682-800): for every token s
+ * and head h, the D <= 256 values x[s * row_stride + col_off + h * head_stride + d] (bf16) -> out bf16 [S, H, D].
+ * do_norm: v * rsqrtf(mean(v^2) + eps) * w[d] (w bf16 [D], or NULL for none); then, with a table, the first rot
+ * dims are rotated in halves: rope f32 [2, S, rot/2] holds cos then sin (NULL: no rotation).  rot even, <= D.
+ * Bit-exact with the reference's kernel (same reduction order, same hardware rsqrtf, the same FMA contraction). */
+h3q_status h3q_qk_norm_rope(const uint16_t* x, int64_t row_stride, int64_t col_off, int64_t head_stride,
+                            const uint16_t* w, int do_norm, float eps, const float* rope, int rot, uint16_t* out,
+                            int64_t S, int64_t H, int64_t D, void* stream);
+
+/* The DiT's attention step, attend (dit.rs:741-757) with head_dim 128: q = qk_norm_rope(qkv, q_col), k =
+ * qk_norm_rope(qkv, k_col) (norm weights q_norm / k_norm when do_norm, rope table and rot as h3q_qk_norm_rope),
+ * then attention_qkv(q, k, qkv, v_col) -> out bf16 [S, H, 128].  The normalised, rotated q and k never reach
+ * memory: the rotation runs inside the K mean and the Q / K quantisation, and the result equals that sequence
+ * bit for bit.  qkv bf16 [S, qkv_width], 8-byte aligned, width and q / k columns multiples of 4; rot % 8 == 0
+ * (other rot: H3Q_ERR_UNSUPPORTED).  Workspace: h3q_attention_workspace_size(S, H, flags). */
+h3q_status h3q_attend_qkv(const uint16_t* qkv, int64_t qkv_width, int64_t q_col, int64_t k_col, int64_t v_col,
+                          const uint16_t* q_norm, const uint16_t* k_norm, int do_norm, float eps, const float* rope,
+                          int rot, uint16_t* out, int64_t S, int64_t H, int flags, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
 /* The stages, for callers that keep the intermediates. */
 /* Workspace bytes of h3q_attn_kmean (the per-chunk column sums). */
 size_t h3q_attn_kmean_workspace_size(int64_t S, int64_t H);

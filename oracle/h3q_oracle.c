@@ -759,3 +759,43 @@ H3O_API void h3o_rms_modulate(const uint16_t* x, const uint16_t* w, float eps, c
         }
     }
 }
+
+/* qk_norm_rope (kernels.rs:86-126) for bf16 x: per (token s, head h) row of D <= 256 values at
+ * x[s * rs + col + h * hs + d] -> out bf16 [S, H, D].  The sum of squares follows the kernel's reduction: a 32-lane
+ * xor tree over each 32-dim slice (thread d sits at lane d % 32 of warp d / 32), then an xor tree over the slice
+ * sums (absent slices zero).  inv = 1 / sqrtf(ss / D + eps) stands for the device's rsqrtf (an approximate
+ * instruction: the two can differ in the last bit).  v = (v * inv) * w[d] (w NULL: 1).  With rot > 0 the first rot
+ * dims rotate in halves with cos / sin = cs[0 or 1][s][d mod half]: fma(v, cos, -(partner * sin)) below half,
+ * fma(v, cos, partner * sin) above -- the association the reference's compiled kernel uses (one rounded product,
+ * one fused).  out = f2bf. */
+H3O_API void h3o_qk_norm_rope(const uint16_t* x, int64_t rs, int64_t col, int64_t hs, const uint16_t* w, int do_norm,
+                              float eps, const float* cs, int rot, uint16_t* out, int64_t S, int64_t H, int64_t D) {
+    const int NS = (int)((D + 31) / 32), half = rot / 2;
+    for (int64_t s = 0; s < S; ++s) {
+        for (int64_t h = 0; h < H; ++h) {
+            const uint16_t* xr = x + s * rs + col + h * hs;
+            float v[256], red[32];
+            for (int d = 0; d < 32 * NS; ++d) v[d] = d < D ? bf2f(xr[d]) : 0.f;
+            if (do_norm) {
+                for (int i = 0; i < 32; ++i) {
+                    float sq[32];
+                    for (int l = 0; l < 32; ++l) sq[l] = i < NS ? v[32 * i + l] * v[32 * i + l] : 0.f;
+                    red[i] = i < NS ? xor_tree32(sq) : 0.f;
+                }
+                const float ss = xor_tree32(red);
+                const float inv = 1.0f / sqrtf(ss / (float)D + eps);
+                for (int d = 0; d < D; ++d) v[d] = (v[d] * inv) * (w ? bf2f(w[d]) : 1.f);
+            }
+            uint16_t* o = out + (s * H + h) * D;
+            for (int d = 0; d < D; ++d) {
+                float r = v[d];
+                if (d < rot) {
+                    const int j = d < half ? d : d - half;
+                    const float c = cs[s * half + j], sn = cs[(S + s) * half + j];
+                    r = d < half ? fmaf(v[d], c, -(v[d + half] * sn)) : fmaf(v[d], c, v[d - half] * sn);
+                }
+                o[d] = f2bf(r);
+            }
+        }
+    }
+}

@@ -453,6 +453,52 @@ def rms_modulate(x_bf16, w_bf16, eps: float, scale, shift, idx) -> np.ndarray:
     return out
 
 
+def qk_norm_rope(x_bf16, col_off: int, heads: int, head_dim: int, w_bf16=None, eps: float = 1e-6,
+                 do_norm: bool = True, cs=None, rot: int = 0, head_stride: int | None = None) -> np.ndarray:
+    """qk_norm_rope (kernels.rs:86-126) on bf16 bits x [S, width]; w bf16 bits [D] or None; cs f32 [2, S, rot/2] or
+    None.  bf16 bits [S, heads, head_dim].  1 / sqrtf stands for the device's rsqrtf."""
+    x = np.ascontiguousarray(x_bf16, dtype=np.uint16)
+    S, width = x.shape
+    out = np.empty((S, heads, head_dim), dtype=np.uint16)
+    wv = None if w_bf16 is None else np.ascontiguousarray(w_bf16, dtype=np.uint16)
+    csv = None if cs is None else np.ascontiguousarray(cs, dtype=np.float32)
+    lib().h3o_qk_norm_rope(_p(x), c_i64(width), c_i64(col_off), c_i64(head_dim if head_stride is None else head_stride),
+                           _p(wv) if wv is not None else None, c_int(1 if do_norm else 0), c_f32(eps),
+                           _p(csv) if csv is not None else None, c_int(rot if csv is not None else 0), _p(out), c_i64(S),
+                           c_i64(heads), c_i64(head_dim))
+    return out
+
+
+def attend_qkv(qkv_bf16, heads: int, qw=None, kw=None, do_norm: bool = True, eps: float = 1e-6, cs=None,
+               rot: int = 0, flags: int = 0) -> np.ndarray:
+    """The DiT's attend (dit.rs:741-757): qk_norm_rope of q and k out of the fused qkv, then attention_qkv with V
+    from the qkv rows.  bf16 bits [S, heads, 128]."""
+    S = qkv_bf16.shape[0]
+    inner = heads * 128
+    q = qk_norm_rope(qkv_bf16, 0, heads, 128, qw, eps, do_norm, cs, rot)
+    k = qk_norm_rope(qkv_bf16, inner, heads, 128, kw, eps, do_norm, cs, rot)
+    block = bool(flags & ATTN_SCALE_BLOCK128)
+    km = attn_kmean(k)
+    q8, qs = attn_quant_heads(q, None, block)
+    k8, ks = attn_quant_heads(k, km, block)
+    return attn_forward(q8, qs, k8, ks, np.ascontiguousarray(qkv_bf16), qkv_bf16.shape[1], 2 * inner,
+                        bool(flags & ATTN_PV_BF16))
+
+
+def make_rope_inputs(seed: int, S: int, H: int, D: int = 128, rot: int = 96):
+    """DiT-like inputs of the attention step: a fused qkv bf16 [S, 3 H D] ~N(0, 1) with per-token magnitudes in
+    [1, 4], norm weights bf16 ~1 + N(0, 0.2), and a rope table [2, S, rot/2] of cos / sin of angles in [0, 100)
+    rounded through bf16 (as the DiT stores it, dit.rs:803-819)."""
+    rng = np.random.default_rng(seed)
+    qkv = rng.standard_normal((S, 3 * H * D)).astype(np.float32) * (1 + 3 * rng.random((S, 1), dtype=np.float32))
+    qw = (1.0 + 0.2 * rng.standard_normal(D)).astype(np.float32)
+    kw = (1.0 + 0.2 * rng.standard_normal(D)).astype(np.float32)
+    ang = (100.0 * rng.random((S, rot // 2))).astype(np.float32)
+    cs = np.stack([np.cos(ang), np.sin(ang)]).astype(np.float32)
+    cs = bf16_bits_to_f32(f32_to_bf16_bits(cs)).reshape(2, S, rot // 2)
+    return f32_to_bf16_bits(qkv), f32_to_bf16_bits(qw), f32_to_bf16_bits(kw), np.ascontiguousarray(cs)
+
+
 def make_modulate_inputs(seed: int, S: int, C: int, R: int = 3):
     """DiT-like inputs of rms_modulate: x bf16 ~N(0, 1) with 8 outlier channels x20, norm weight bf16 ~1 + N(0, 0.1),
     adaLN scale / shift tables f32 ~N(0, 0.5) with R rows, idx u32 [S] in [0, R)."""

@@ -26,7 +26,7 @@ def lib() -> ctypes.CDLL:
         _LIB = ctypes.CDLL(path())
         for name in ("h3ref_quant_rows", "h3ref_quant_rows_linear", "h3ref_int8_epilogue", "h3ref_dequant_i8",
                      "h3ref_dequant_nvfp4", "h3ref_gate_add", "h3ref_gemm_s8", "h3ref_col_sum",
-                     "h3ref_quant_heads", "h3ref_v_to_f16", "h3ref_attn_qk8", "h3ref_rms_modulate"):
+                     "h3ref_quant_heads", "h3ref_v_to_f16", "h3ref_attn_qk8", "h3ref_rms_modulate", "h3ref_qk_norm_rope"):
             getattr(_LIB, name).restype = ctypes.c_int
     return _LIB
 
@@ -136,4 +136,19 @@ def rms_modulate(x, w, eps: float, scale, shift, idx):
     out = torch.empty_like(x)
     _check(lib().h3ref_rms_modulate(_ptr(x), 2, _ptr(w), ctypes.c_float(eps), _ptr(scale), _ptr(shift), _ptr(idx),
                                     _ptr(out), S, C, _stream()), "ref rms_modulate")
+    return out
+
+
+def qk_norm_rope(x, col_off: int, head_stride: int, H: int, D: int, w, eps: float, do_norm: bool, cs, rot: int):
+    """qk_norm_rope (kernels.rs:86-126), the reference's launch: x bf16 [S, width] -> bf16 [S, H, D]; w bf16 [D] or
+    None; cs f32 [2, S, rot/2] or None (rot is then 0)."""
+    import torch
+    S, width = x.shape
+    out = torch.empty((S, H, D), dtype=torch.bfloat16, device=x.device)
+    if cs is None:
+        rot = 0
+    _check(lib().h3ref_qk_norm_rope(_ptr(x), 2, ctypes.c_ulonglong(width), ctypes.c_ulonglong(col_off),
+                                    ctypes.c_ulonglong(head_stride), _ptr(w), 2, int(w is not None), int(do_norm),
+                                    ctypes.c_float(eps), _ptr(cs), rot, _ptr(out), 2, S, H, D, _stream()),
+           "ref qk_norm_rope")
     return out

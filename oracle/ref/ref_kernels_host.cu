@@ -73,4 +73,16 @@ int h3ref_rms_modulate(const void* x, int kind, const void* w, float eps, const 
   return (int)cudaGetLastError();
 }
 
+// QkNormRope::cuda_fwd launch (kernels.rs:722-729): one CTA of roundup(D, 32) threads per (token, head) row
+int h3ref_qk_norm_rope(const void* x, int xkind, unsigned long long row_stride, unsigned long long col_off,
+                       unsigned long long head_stride, const void* w, int wkind, int has_w, int do_norm, float eps,
+                       const float* cs, int rot, void* out, int okind, int S, int H, int D, void* stream) {
+  if (S == 0 || H == 0) return 0;
+  const unsigned threads = (unsigned)((D + 31) / 32 * 32);
+  qk_norm_rope<<<(unsigned)(S * H), threads, 0, (cudaStream_t)stream>>>(x, xkind, row_stride, col_off, head_stride, w,
+                                                                      wkind, has_w, do_norm, eps, cs, rot, out,
+                                                                      okind, S, H, D);
+  return (int)cudaGetLastError();
+}
+
 }  // extern "C"

@@ -70,3 +70,26 @@ def test_fused_quant_feeds_the_gemm(cuda):
     y2 = h3q.gemm_s8(h3q.rms_modulate(x, w, EPS, sc, sh, idx), wt, ws, b, rotate=True)
     assert torch.equal(y.view(torch.int16), y2.view(torch.int16))
     assert h3q.device_status() == 0
+
+
+@pytest.mark.parametrize("S,C", [(6000, 1024), (4000, 5120), (1500, 16384)])
+@pytest.mark.parametrize("blocked", [False, True])
+def test_many_rows_per_cta(cuda, S, C, blocked):
+    """Enough rows that every CTA works through a block of them (the next row's sums are formed under the current
+    row's barrier, the table slice is reloaded when the index changes): per-row random table rows, and table rows
+    that change every 700 tokens (a latent frame)."""
+    _, (x, w, sc, sh, idx) = _inputs(S ^ C, S, C, cuda)
+    if blocked:
+        idx = ((torch.arange(S, device=cuda) // 700) % sc.shape[0]).to(torch.int32)
+    y = h3q.rms_modulate(x, w, EPS, sc, sh, idx)
+    q, xs = h3q.rms_modulate_quant(x, w, EPS, sc, sh, idx)
+    q2, xs2 = h3q.quant_rows(y, True)
+    assert torch.equal(q, q2)
+    assert torch.equal(xs.view(torch.int32), xs2.view(torch.int32))
+    if R.available():
+        assert torch.equal(y.view(torch.int16), R.rms_modulate(x, w, EPS, sc, sh, idx).view(torch.int16))
+    else:
+        want = O.rms_modulate(bf16_bits(x), bf16_bits(w), EPS, sc.cpu().numpy(), sh.cpu().numpy(),
+                              idx.cpu().numpy().astype(np.uint32))
+        assert (bf16_bits(y) == want).mean() > 0.99
+    assert h3q.device_status() == 0
