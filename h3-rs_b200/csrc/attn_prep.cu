@@ -338,175 +338,260 @@ __global__ void __launch_bounds__(256) qk_norm_rope_kernel(const uint16_t* __res
   }
 }
 
-// The D = 128 form used inside the attention front end: lane l holds dims 4l .. 4l+3.  The reference's slice
-// w = l / 8 and lane 4 (l % 8) + j, so its xor levels 16, 8, 4 are lanes xor 4, 2, 1 here and levels 2, 1 stay in
-// the thread; the slice sums meet over lanes xor 16 and 8.  Rotation partners (half % 4 == 0) are lanes l +- half/4,
-// same j.  Returns the row as the reference's bf16 q / k values (in f32).
-__device__ __forceinline__ void norm_rope_row128(float (&v)[4], int lane, const uint16_t* __restrict__ w,
-                                                 int do_norm, float eps, const float* __restrict__ cs, int half,
-                                                 int64_t s, int64_t S) {
+// The D = 128 forms.  Slice layout: lane 4r + w of a warp holds dims 32w .. 32w+31 of row r (r < 8) -- exactly the
+// 32 values the reference's warp w reduces, so its 32-lane xor tree runs inside the thread (level 16 pairs dims j
+// and j + 16, ...) and the four slice sums meet over lanes xor 2 then xor 1.  The rotation reads partners from a
+// per-warp row buffer of 8 x 128 f32 whose 16-byte chunks are swizzled by the writing lane (conflict-free).
+constexpr int kRowsPerWarp = 8;
+
+__device__ __forceinline__ int buf_off(int ls, int chunk) { return 32 * ls + 4 * (chunk ^ (ls & 7)); }
+
+__device__ __forceinline__ void load_slice(const uint16_t* __restrict__ p, uint32_t (&raw)[16]) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p) + c);
+    raw[4 * c] = u.x;
+    raw[4 * c + 1] = u.y;
+    raw[4 * c + 2] = u.z;
+    raw[4 * c + 3] = u.w;
+  }
+}
+
+__device__ __forceinline__ float lo16(uint32_t u) { return __uint_as_float(u << 16); }
+__device__ __forceinline__ float hi16(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
+__device__ __forceinline__ float elem(const uint32_t (&p)[16], int i) { return (i & 1) ? hi16(p[i >> 1]) : lo16(p[i >> 1]); }
+
+// bf16x2 of (a, b), a in the low half: nearest even with the reference's f2bf NaN pattern 0x7fc0 (cvt.rn agrees
+// with f2bf on every other input).
+__device__ __forceinline__ uint32_t pack_bf16_ref(float a, float b) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(b), "f"(a));
+  if ((r & 0x7fffu) > 0x7f80u) r = (r & 0xffff0000u) | 0x7fc0u;
+  if ((r & 0x7fff0000u) > 0x7f800000u) r = (r & 0xffffu) | 0x7fc00000u;
+  return r;
+}
+
+// qk_norm_rope of the thread's slice of row (token s): packed bf16 in (raw) -> the reference's packed bf16 q / k
+// values out (res).  `w` points at the slice's 32 norm weights (or is NULL); half % 4 == 0.  Every lane of the warp
+// takes part (shuffles, the row buffer).  Values stream through in 4-dim chunks, so only the packed slices stay live.
+__device__ __forceinline__ void slice_norm_rope(const uint32_t (&raw)[16], uint32_t (&res)[16], int lane,
+                                                const uint16_t* __restrict__ w, int do_norm, float eps,
+                                                const float* __restrict__ cs, int half, int64_t s, int64_t S,
+                                                float* buf) {
+  const int sl = lane & 3;
+  float inv = 1.f;
   if (do_norm) {
-    float a[4];
+    float a[16];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) a[j] = __fmul_rn(v[j], v[j]);
-#pragma unroll
-    for (int o = 4; o > 0; o >>= 1) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) a[j] = __fadd_rn(a[j], __shfl_xor_sync(0xffffffffu, a[j], o));
+    for (int i = 0; i < 16; ++i) {
+      const float x0 = elem(raw, i), x1 = elem(raw, i + 16);
+      a[i] = __fadd_rn(__fmul_rn(x0, x0), __fmul_rn(x1, x1));
     }
-    float t = __fadd_rn(__fadd_rn(a[0], a[2]), __fadd_rn(a[1], a[3]));
-    t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 16));
-    t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 8));
-    const float inv = rsqrtf(__fadd_rn(__fdiv_rn(t, 128.f), eps));
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1)
+#pragma unroll
+      for (int i = 0; i < o; ++i) a[i] = __fadd_rn(a[i], a[i + o]);
+    float t = __fadd_rn(a[0], __shfl_xor_sync(0xffffffffu, a[0], 2));
+    t = __fadd_rn(t, __shfl_xor_sync(0xffffffffu, t, 1));
+    inv = rsqrtf(__fadd_rn(__fdiv_rn(t, 128.f), eps));
+  }
+  // normalised chunk c: (x * inv) * w
+  auto norm4 = [&](int c, float (&n)[4]) {
     float wv[4] = {1.f, 1.f, 1.f, 1.f};
-    if (w) {
-      const uint2 wr = __ldg(reinterpret_cast<const uint2*>(w) + lane);
-      wv[0] = __uint_as_float(wr.x << 16);
-      wv[1] = __uint_as_float(wr.x & 0xffff0000u);
-      wv[2] = __uint_as_float(wr.y << 16);
-      wv[3] = __uint_as_float(wr.y & 0xffff0000u);
+    if (do_norm && w) {
+      const uint2 wr = __ldg(reinterpret_cast<const uint2*>(w) + c);
+      wv[0] = lo16(wr.x); wv[1] = hi16(wr.x); wv[2] = lo16(wr.y); wv[3] = hi16(wr.y);
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) v[j] = __fmul_rn(__fmul_rn(v[j], inv), wv[j]);
-  }
+    for (int i = 0; i < 4; ++i) {
+      const float x = elem(raw, 4 * c + i);
+      n[i] = do_norm ? __fmul_rn(__fmul_rn(x, inv), wv[i]) : x;
+    }
+  };
   if (half > 0) {
-    const int q = half >> 2, d0 = 4 * lane;
-    float up[4], dn[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      up[j] = __shfl_down_sync(0xffffffffu, v[j], q);
-      dn[j] = __shfl_up_sync(0xffffffffu, v[j], q);
+    for (int c = 0; c < 8; ++c) {
+      float n[4];
+      norm4(c, n);
+      *reinterpret_cast<float4*>(buf + buf_off(lane, c)) = make_float4(n[0], n[1], n[2], n[3]);
     }
-    if (d0 < 2 * half) {
-      const bool lo = d0 < half;
-      const int jj = lo ? d0 : d0 - half;
-      const float4 c = __ldg(reinterpret_cast<const float4*>(cs + s * half + jj));
-      const float4 sn = __ldg(reinterpret_cast<const float4*>(cs + (S + s) * half + jj));
-      const float cc[4] = {c.x, c.y, c.z, c.w}, ss[4] = {sn.x, sn.y, sn.z, sn.w};
+    __syncwarp();
+    const int r4 = lane & ~3;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) v[j] = lo ? rope_lo(v[j], cc[j], up[j], ss[j]) : rope_hi(v[j], cc[j], dn[j], ss[j]);
+    for (int c = 0; c < 8; ++c) {
+      const float4 own = *reinterpret_cast<const float4*>(buf + buf_off(lane, c));
+      float v[4] = {own.x, own.y, own.z, own.w};
+      const int d = 32 * sl + 4 * c;
+      if (d < 2 * half) {
+        const bool lo = d < half;
+        const int p = lo ? d + half : d - half, ls = r4 + (p >> 5);
+        const float4 pv = *reinterpret_cast<const float4*>(buf + buf_off(ls, (p & 31) >> 2));
+        const int jj = lo ? d : d - half;
+        const float4 c4 = __ldg(reinterpret_cast<const float4*>(cs + s * half + jj));
+        const float4 s4 = __ldg(reinterpret_cast<const float4*>(cs + (S + s) * half + jj));
+        const float pp[4] = {pv.x, pv.y, pv.z, pv.w}, cc[4] = {c4.x, c4.y, c4.z, c4.w}, ss[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = lo ? rope_lo(v[i], cc[i], pp[i], ss[i]) : rope_hi(v[i], cc[i], pp[i], ss[i]);
+      }
+      res[2 * c] = pack_bf16_ref(v[0], v[1]);
+      res[2 * c + 1] = pack_bf16_ref(v[2], v[3]);
+    }
+    __syncwarp();  // the buffer is rewritten next
+  } else {
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      float n[4];
+      norm4(c, n);
+      res[2 * c] = pack_bf16_ref(n[0], n[1]);
+      res[2 * c + 1] = pack_bf16_ref(n[2], n[3]);
     }
   }
+}
+
+// Standalone qk_norm_rope for D = 128, rot % 8 == 0 and 16-byte aligned rows: CTA of 8 warps = 64 tokens, looping
+// over `hb` heads (the tokens' rope rows stay in L1); out = f2bf exactly (NaN -> 0x7fc0).
+__global__ void __launch_bounds__(256) qk_norm_rope128_kernel(const uint16_t* __restrict__ x, int64_t rs, int64_t col,
+                                                              int64_t hs, const uint16_t* __restrict__ w, int do_norm,
+                                                              float eps, const float* __restrict__ cs, int half,
+                                                              uint16_t* __restrict__ out, int64_t S, int H, int hb) {
+  __shared__ __align__(16) float buf[8][kRowsPerWarp * 128];
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5, sl = lane & 3;
+  const int64_t s = (int64_t)blockIdx.x * 64 + wp * kRowsPerWarp + (lane >> 2);
+  const bool valid = s < S;
+  const int h1 = min(H, (int)(blockIdx.y + 1) * hb);
+  for (int h = blockIdx.y * hb; h < h1; ++h) {
+    uint32_t raw[16], res[16];
+    if (valid) load_slice(x + s * rs + col + (int64_t)h * hs + 32 * sl, raw);
+    else {
 #pragma unroll
-  for (int j = 0; j < 4; ++j) v[j] = bf2f(f2bf_ref(v[j]));
+      for (int i = 0; i < 16; ++i) raw[i] = 0u;
+    }
+    slice_norm_rope(raw, res, lane, w ? w + 32 * sl : nullptr, do_norm, eps, cs, half, valid ? s : 0, S, buf[wp]);
+    if (valid) {
+      uint4* dst = reinterpret_cast<uint4*>(out + (s * H + h) * HD + 32 * sl);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) dst[c] = make_uint4(res[4 * c], res[4 * c + 1], res[4 * c + 2], res[4 * c + 3]);
+    }
+  }
 }
 
-__device__ __forceinline__ void load_row128(const uint16_t* __restrict__ p, int lane, float (&v)[4]) {
-  const uint2 r = __ldg(reinterpret_cast<const uint2*>(p) + lane);
-  v[0] = __uint_as_float(r.x << 16);
-  v[1] = __uint_as_float(r.x & 0xffff0000u);
-  v[2] = __uint_as_float(r.y << 16);
-  v[3] = __uint_as_float(r.y & 0xffff0000u);
-}
-
-// K column sums of the normalised, rotated K rows, chunked as kmean_partial_kernel: warp = (chunk, head), rows of
-// the chunk in order.  part[p, h*128 + d].
+// K column sums of the normalised, rotated K rows, chunked as kmean_partial_kernel: warp = (chunk, head), 8 rows of
+// the chunk at a time in the slice layout, then turned through the row buffer so lane l adds dims 4l .. 4l+3 of the
+// 8 rows in row order.  part[p, h*128 + d].  CTA = 8 heads of one chunk (their rope rows are the same).
 __global__ void __launch_bounds__(256) kmean_rope_partial_kernel(const uint16_t* __restrict__ x, int64_t rs,
                                                                  int64_t col, const uint16_t* __restrict__ w,
                                                                  int do_norm, float eps,
                                                                  const float* __restrict__ cs, int half,
                                                                  float* __restrict__ part, int64_t S, int H,
                                                                  int rows_per) {
-  const int lane = threadIdx.x & 31;
-  const int h = blockIdx.y * 8 + (threadIdx.x >> 5);
+  __shared__ __align__(16) float buf[8][kRowsPerWarp * 128];
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5, sl = lane & 3;
+  const int h = blockIdx.y * 8 + wp;
   if (h >= H) return;
   const int64_t r0 = (int64_t)blockIdx.x * rows_per;
   const int64_t r1 = r0 + rows_per < S ? r0 + rows_per : S;
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
-  constexpr int U = 4;
-  int64_t r = r0;
-  for (; r + U <= r1; r += U) {
-    float v[U][4];
+  float* b = buf[wp];
+  for (int64_t g = r0; g < r1; g += kRowsPerWarp) {
+    const int64_t s = g + (lane >> 2);
+    const bool valid = s < r1;
+    uint32_t raw[16], res[16];
+    if (valid) load_slice(x + s * rs + col + (int64_t)h * HD + 32 * sl, raw);
+    else {
 #pragma unroll
-    for (int u = 0; u < U; ++u) load_row128(x + (r + u) * rs + col + (int64_t)h * HD, lane, v[u]);
+      for (int i = 0; i < 16; ++i) raw[i] = 0u;
+    }
+    slice_norm_rope(raw, res, lane, w ? w + 32 * sl : nullptr, do_norm, eps, cs, half, valid ? s : 0, S, b);
 #pragma unroll
-    for (int u = 0; u < U; ++u) norm_rope_row128(v[u], lane, w, do_norm, eps, cs, half, r + u, S);
-#pragma unroll
-    for (int u = 0; u < U; ++u)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) acc[j] = __fadd_rn(acc[j], v[u][j]);
-  }
-  for (; r < r1; ++r) {
-    float v[4];
-    load_row128(x + r * rs + col + (int64_t)h * HD, lane, v);
-    norm_rope_row128(v, lane, w, do_norm, eps, cs, half, r, S);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) acc[j] = __fadd_rn(acc[j], v[j]);
+    for (int c = 0; c < 8; ++c)
+      *reinterpret_cast<float4*>(b + buf_off(lane, c)) =
+          make_float4(lo16(res[2 * c]), hi16(res[2 * c]), lo16(res[2 * c + 1]), hi16(res[2 * c + 1]));
+    __syncwarp();
+    const int nr = (int)(r1 - g < kRowsPerWarp ? r1 - g : kRowsPerWarp);
+    for (int r = 0; r < nr; ++r) {
+      const int ls = 4 * r + (lane >> 3);
+      const float4 f = *reinterpret_cast<const float4*>(b + buf_off(ls, lane & 7));
+      acc[0] = __fadd_rn(acc[0], f.x);
+      acc[1] = __fadd_rn(acc[1], f.y);
+      acc[2] = __fadd_rn(acc[2], f.z);
+      acc[3] = __fadd_rn(acc[3], f.w);
+    }
+    __syncwarp();
   }
   reinterpret_cast<float4*>(part + (int64_t)blockIdx.x * H * HD + (int64_t)h * HD)[lane] =
       make_float4(acc[0], acc[1], acc[2], acc[3]);
 }
 
-// Normalise + rotate + (K: subtract the column mean) + quantise, as qk_norm_rope then quant_heads.  CTA = (128-token
-// block, head), warp = 16 tokens of the block.  Per-token scales, or (BLOCK) one scale per block.  Writes every
-// scale entry of the block, zero past S.
+// Normalise + rotate + (K: subtract the column mean) + quantise, as qk_norm_rope then quant_heads.  8 tokens per
+// warp (slice layout); a CTA covers 64 tokens (per-token scales) or, with BLOCK, one 128-token scale block, and
+// loops over `hb` heads.  Writes every scale entry of its tokens, zero past S.
 template <bool BLOCK>
-__global__ void __launch_bounds__(256) qk_rope_quant_kernel(const uint16_t* __restrict__ x, int64_t rs, int64_t col,
+__global__ void __launch_bounds__(BLOCK ? 512 : 256, BLOCK ? 2 : 3) qk_rope_quant_kernel(const uint16_t* __restrict__ x, int64_t rs, int64_t col,
                                                             const uint16_t* __restrict__ w, int do_norm, float eps,
                                                             const float* __restrict__ cs, int half,
                                                             const float* __restrict__ mean,
                                                             int8_t* __restrict__ codes, float* __restrict__ scales,
-                                                            int64_t S, int64_t Sp) {
-  __shared__ float red[8];
-  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
-  const int h = blockIdx.y;
-  const int64_t s0 = (int64_t)blockIdx.x * 128 + wp * 16;
-  float mv[4] = {0.f, 0.f, 0.f, 0.f};
-  if (mean) {
-    const float4 m4 = __ldg(reinterpret_cast<const float4*>(mean + (int64_t)h * HD) + lane);
-    mv[0] = m4.x; mv[1] = m4.y; mv[2] = m4.z; mv[3] = m4.w;
-  }
-  float v[16][4];
+                                                            int64_t S, int64_t Sp, int H, int hb) {
+  extern __shared__ __align__(16) float qbuf[];  // warps x 8 x 128
+  __shared__ float red[2][16];
+  constexpr int TOK = BLOCK ? 128 : 64;  // tokens per CTA: the scale block, or 8 warps of 8
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5, sl = lane & 3;
+  const int64_t s = (int64_t)blockIdx.x * TOK + wp * kRowsPerWarp + (lane >> 2);
+  const bool valid = s < S;
+  float* b = qbuf + wp * kRowsPerWarp * 128;
+  const int h0 = blockIdx.y * hb, h1 = min(H, h0 + hb);
+  for (int h = h0; h < h1; ++h) {
+    uint32_t raw[16], res[16];
+    if (valid) load_slice(x + s * rs + col + (int64_t)h * HD + 32 * sl, raw);
+    else {
 #pragma unroll
-  for (int k = 0; k < 16; ++k) {
-    if (s0 + k < S) load_row128(x + (s0 + k) * rs + col + (int64_t)h * HD, lane, v[k]);
-    else v[k][0] = v[k][1] = v[k][2] = v[k][3] = 0.f;
-  }
-  float bm = 0.f;
-#pragma unroll
-  for (int k = 0; k < 16; ++k) {
-    const int64_t s = s0 + k;
-    if (s < S) {  // warp-uniform
-      norm_rope_row128(v[k], lane, w, do_norm, eps, cs, half, s, S);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) v[k][j] = __fsub_rn(v[k][j], mv[j]);
+      for (int i = 0; i < 16; ++i) raw[i] = 0u;
     }
-    float m = fmaxf(fmaxf(fabsf(v[k][0]), fabsf(v[k][1])), fmaxf(fabsf(v[k][2]), fabsf(v[k][3])));
+    slice_norm_rope(raw, res, lane, w ? w + 32 * sl : nullptr, do_norm, eps, cs, half, valid ? s : 0, S, b);
+    // v = bf16 value - mean (quant_heads), formed twice: for the row maximum and for the codes
+    const float4* mp = reinterpret_cast<const float4*>(mean + (int64_t)h * HD + 32 * sl);
+    auto centred = [&](int c, float (&v)[4]) {
+      v[0] = lo16(res[2 * c]); v[1] = hi16(res[2 * c]); v[2] = lo16(res[2 * c + 1]); v[3] = hi16(res[2 * c + 1]);
+      const float4 m4 = mean ? __ldg(mp + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[0] = __fsub_rn(v[0], m4.x); v[1] = __fsub_rn(v[1], m4.y);
+      v[2] = __fsub_rn(v[2], m4.z); v[3] = __fsub_rn(v[3], m4.w);
+    };
+    float m = 0.f;
+    if (valid) {
+#pragma unroll
+      for (int c = 0; c < 8; ++c) {
+        float v[4];
+        centred(c, v);
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3]))));
+      }
+    }
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
     if (BLOCK) {
-      bm = fmaxf(bm, m);
-    } else {
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-      const float sc = fmaxf(__fdiv_rn(m, 127.f), 1e-20f);
-      if (s < S) {
-        const float inv = __fdiv_rn(1.f, sc);
-        const uint32_t p = q127(v[k][0], inv) | (q127(v[k][1], inv) << 8) | (q127(v[k][2], inv) << 16) |
-                           (q127(v[k][3], inv) << 24);
-        reinterpret_cast<uint32_t*>(codes + ((int64_t)h * S + s) * HD)[lane] = p;
-      }
-      if (lane == 0 && s < Sp) scales[(int64_t)h * Sp + s] = s < S ? sc : 0.f;
+      for (int o = 4; o < 32; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      const int par = (h - h0) & 1;  // two slots: the next head's writes cannot meet this head's reads
+      if (lane == 0) red[par][wp] = m;
+      __syncthreads();
+      m = red[par][0];
+#pragma unroll
+      for (int i = 1; i < 16; ++i) m = fmaxf(m, red[par][i]);
     }
-  }
-  if (BLOCK) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, o));
-    if (lane == 0) red[wp] = bm;
-    __syncthreads();
-    float m = red[0];
-#pragma unroll
-    for (int i = 1; i < 8; ++i) m = fmaxf(m, red[i]);
     const float sc = fmaxf(__fdiv_rn(m, 127.f), 1e-20f);
-    const float inv = __fdiv_rn(1.f, sc);
+    if (valid) {
+      const float inv = __fdiv_rn(1.f, sc);
+      uint32_t p[8];
 #pragma unroll
-    for (int k = 0; k < 16; ++k) {
-      const int64_t s = s0 + k;
-      if (s < S) {
-        const uint32_t p = q127(v[k][0], inv) | (q127(v[k][1], inv) << 8) | (q127(v[k][2], inv) << 16) |
-                           (q127(v[k][3], inv) << 24);
-        reinterpret_cast<uint32_t*>(codes + ((int64_t)h * S + s) * HD)[lane] = p;
+      for (int c = 0; c < 8; ++c) {
+        float v[4];
+        centred(c, v);
+        p[c] = q127(v[0], inv) | (q127(v[1], inv) << 8) | (q127(v[2], inv) << 16) | (q127(v[3], inv) << 24);
       }
-      if (lane == 0) scales[(int64_t)h * Sp + s] = s < S ? sc : 0.f;
+      uint4* dst = reinterpret_cast<uint4*>(codes + ((int64_t)h * S + s) * HD + 32 * sl);
+      dst[0] = make_uint4(p[0], p[1], p[2], p[3]);
+      dst[1] = make_uint4(p[4], p[5], p[6], p[7]);
     }
+    if (sl == 0 && s < Sp) scales[(int64_t)h * Sp + s] = valid ? sc : 0.f;
   }
 }
 
@@ -567,6 +652,16 @@ cudaError_t launch_qk_norm_rope(const uint16_t* x, int64_t rs, int64_t col, int6
                                 int do_norm, float eps, const float* cs, int rot, uint16_t* out, int64_t S, int64_t H,
                                 int64_t D, cudaStream_t st) {
   if (S <= 0 || H <= 0 || D <= 0) return cudaSuccess;
+  const bool a16 = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 15u) == 0 &&
+                   rs % 8 == 0 && col % 8 == 0 && hs % 8 == 0;
+  const bool wa = !w || (reinterpret_cast<uintptr_t>(w) & 15u) == 0;
+  const bool ca = rot == 0 || (reinterpret_cast<uintptr_t>(cs) & 15u) == 0;
+  if (D == HD && rot % 8 == 0 && a16 && wa && ca) {
+    const int hb = H < 8 ? (int)H : 8;
+    const dim3 grid((unsigned)((S + 63) / 64), (unsigned)((H + hb - 1) / hb));
+    qk_norm_rope128_kernel<<<grid, 256, 0, st>>>(x, rs, col, hs, w, do_norm, eps, cs, rot / 2, out, S, (int)H, hb);
+    return cudaGetLastError();
+  }
   const int64_t rows = S * H;
   int64_t blocks = (rows + 7) / 8;
   const int64_t cap = (int64_t)sm_count(0) * 16;
@@ -595,11 +690,17 @@ cudaError_t launch_qk_rope_quant(const uint16_t* x, int64_t rs, int64_t col, con
                                  int64_t S, int64_t H, bool block128, cudaStream_t st) {
   if (S <= 0 || H <= 0) return cudaSuccess;
   const int64_t Sp = (S + 127) / 128 * 128;
-  const dim3 grid((unsigned)(Sp / 128), (unsigned)H);
-  if (block128)
-    qk_rope_quant_kernel<true><<<grid, 256, 0, st>>>(x, rs, col, w, do_norm, eps, cs, rot / 2, mean, codes, scales, S, Sp);
-  else
-    qk_rope_quant_kernel<false><<<grid, 256, 0, st>>>(x, rs, col, w, do_norm, eps, cs, rot / 2, mean, codes, scales, S, Sp);
+  const int tok = block128 ? 128 : 64, threads = tok * 4;
+  // heads per CTA: the tokens' rope rows are read from L2 once per CTA; keep at least ~3 CTAs per SM busy
+  const int64_t blocks = Sp / tok;
+  int hb = 8;
+  while (hb > 1 && blocks * ((H + hb - 1) / hb) < 3 * (int64_t)sm_count(0)) hb >>= 1;
+  const dim3 grid((unsigned)blocks, (unsigned)((H + hb - 1) / hb));
+  const size_t smem = (size_t)(threads / 32) * kRowsPerWarp * 128 * sizeof(float);
+  auto kern = block128 ? qk_rope_quant_kernel<true> : qk_rope_quant_kernel<false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, threads, smem, st>>>(x, rs, col, w, do_norm, eps, cs, rot / 2, mean, codes, scales, S, Sp, (int)H, hb);
   return cudaGetLastError();
 }
 
