@@ -248,6 +248,43 @@ def attention_c4(dev, peaks: dict, reps: int = 5, S: int = 32760, H: int = 40) -
                     "burst, serial"}
 
 
+def attend_step_c4(dev, reps: int = 5, S: int = 32760, H: int = 40, rot: int = 96) -> dict:
+    """The DiT's whole attention step (dit.rs:741-757) at config 4's shape: q / k RMSNorm + RoPE out of the fused
+    qkv [S, 3 H 128], then the int8 attention with V read from the qkv rows (block-128 scales, bf16 P.V).  "fused"
+    is h3q_attend_qkv (the normalised, rotated q / k never reach memory); "unfused" is h3q_qk_norm_rope twice then
+    h3q_attention_qkv, as the reference runs it.  The rope table is [2, S, 48] (three axes of 16 frequencies)."""
+    import torch
+    import h3q
+    g = torch.Generator(device=dev).manual_seed(43)
+    inner = H * 128
+    qkv = (2.0 * torch.randn((S, 3 * inner), generator=g, device=dev)).to(torch.bfloat16)
+    qw = (1 + 0.2 * torch.randn(128, generator=g, device=dev)).to(torch.bfloat16)
+    kw = (1 + 0.2 * torch.randn(128, generator=g, device=dev)).to(torch.bfloat16)
+    ang = 100.0 * torch.rand((S, rot // 2), generator=g, device=dev)
+    cs = torch.stack([ang.cos(), ang.sin()]).to(torch.bfloat16).float().contiguous()
+    flags = h3q.ATTN_SCALE_BLOCK128 | h3q.ATTN_PV_BF16
+
+    def unfused():
+        q = h3q.qk_norm_rope(qkv, 0, H, 128, (qw, 1e-6), cs, rot)
+        k = h3q.qk_norm_rope(qkv, inner, H, 128, (kw, 1e-6), cs, rot)
+        return h3q.attention_qkv(q, k, qkv, 2 * inner, flags)
+
+    res = {}
+    for name, fn in (("fused", lambda: h3q.attend_qkv(qkv, H, (qw, kw), 1e-6, cs, rot, flags)), ("unfused", unfused)):
+        for _ in range(2):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        res[name + "_ms"] = round(e0.elapsed_time(e1) / reps, 3)
+    res["workload"] = f"DiT attention step: qk RMSNorm + RoPE (rot {rot}) + int8 attention, B1 H{H} D128 S{S}"
+    res["device_status"] = h3q.device_status(dev.index or 0)
+    return res
+
+
 def modulate_fused(dev, peaks: dict, reps: int = 10, M: int = 32760, C: int = 5120) -> dict:
     """The step in front of the qkv and fc1 linears: RMSNorm + adaLN modulate, then the rotated int8 quantizer.
     "two_pass" runs h3q_rms_modulate (bf16 row to memory) then h3q_quant_rows_i8, as the reference's
@@ -366,6 +403,25 @@ def run_profile_case(args) -> None:
                       "device_status": h3q.device_status(0)}))
 
 
+def run_profile_rope(args) -> None:
+    """qk_norm_rope of the q part of a fused qkv, S=16384, H=40, rot 96: warmup + steps launches of
+    qk_norm_rope128_kernel (q heads 168 MB in, 168 MB out)."""
+    import torch
+    import h3q
+    dev = torch.device("cuda", 0)
+    S, H = 16384, 40
+    g = torch.Generator(device=dev).manual_seed(3)
+    qkv = (2.0 * torch.randn((S, 3 * H * 128), generator=g, device=dev)).to(torch.bfloat16)
+    qw = (1 + 0.2 * torch.randn(128, generator=g, device=dev)).to(torch.bfloat16)
+    ang = 100.0 * torch.rand((S, 48), generator=g, device=dev)
+    cs = torch.stack([ang.cos(), ang.sin()]).to(torch.bfloat16).float().contiguous()
+    for _ in range(args.warmup + args.steps):
+        h3q.qk_norm_rope(qkv, 0, H, 128, (qw, 1e-6), cs, 96)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": f"qk_norm_rope S={S} H={H} rot=96", "launches": args.warmup + args.steps,
+                      "device_status": h3q.device_status(0)}))
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -377,6 +433,10 @@ def main() -> None:
                     help="small case for ncu captures: the two NVFP4 text-encoder linears only")
     ap.add_argument("--profile-attn", action="store_true",
                     help="small case for ncu captures: the attention pipeline at S=8192, H=4")
+    ap.add_argument("--profile-rope", action="store_true",
+                    help="small case for ncu captures: qk_norm_rope of the q heads at S=16384, H=40, rot 96")
+    ap.add_argument("--profile-modulate", action="store_true",
+                    help="small case for ncu captures: rms_modulate + rotated int8 quantization at M=8192, C=5120")
     ap.add_argument("--profile", action="store_true",
                     help="small case for ncu captures: one 4096-token fc1 linear (quant + GEMM), nothing else")
     args = ap.parse_args()
@@ -385,6 +445,13 @@ def main() -> None:
         return
     if args.profile:
         run_profile_case(args)
+        return
+    if args.profile_rope:
+        run_profile_rope(args)
+        return
+    if args.profile_modulate:
+        import torch
+        print(json.dumps(modulate_fused(torch.device("cuda", 0), load_peaks(), reps=args.steps, M=8192)))
         return
     if args.profile_nvfp4:
         import torch
@@ -551,6 +618,7 @@ def main() -> None:
     nv = nvfp4_c3(dev, load_peaks()) if rank == 0 else None
     att = attention_c4(dev, load_peaks()) if rank == 0 else None
     modq = modulate_fused(dev, load_peaks()) if rank == 0 else None
+    attend = attend_step_c4(dev) if rank == 0 else None
 
     cb = None
     if rank == 0 and ws_n == 1 and not args.no_cpu_baseline:
@@ -581,6 +649,7 @@ def main() -> None:
         "nvfp4_c3": nv,
         "attention_c4": att,
         "modulate_quant": modq,
+        "attend_step_c4": attend,
         "multi_gpu": extras,
         "cpu_baseline": cb, "e2e": e2e, "clocks": clk.summary(),
         "gpu_launches": 2 * launches,
