@@ -41,6 +41,17 @@ PATH_GEMM_S8, PATH_INT8_LINEAR, PATH_ROTATE_FUSED, PATH_ROTATE_SEPARATE, PATH_SW
 # name -> (restype, argtypes) of every symbol include/h3q.h declares
 SIGNATURES = {
     "h3q_last_error": (ctypes.c_char_p, []),
+    "h3q_checkpoint_open": (_int, [ctypes.c_char_p, ctypes.POINTER(_vp)]),
+    "h3q_checkpoint_close": (None, [_vp]),
+    "h3q_checkpoint_count": (_i64, [_vp]),
+    "h3q_checkpoint_name": (ctypes.c_char_p, [_vp, _i64]),
+    "h3q_checkpoint_has": (_int, [_vp, ctypes.c_char_p]),
+    "h3q_checkpoint_metadata": (ctypes.c_char_p, [_vp, ctypes.c_char_p]),
+    "h3q_checkpoint_info": (_int, [_vp, ctypes.c_char_p, ctypes.POINTER(_int), ctypes.POINTER(_int),
+                                   ctypes.POINTER(_i64), ctypes.POINTER(ctypes.c_uint64)]),
+    "h3q_checkpoint_read": (_int, [_vp, ctypes.c_char_p, _vp, ctypes.c_uint64]),
+    "h3q_checkpoint_upload": (_int, [_vp, ctypes.c_char_p, _vp, ctypes.c_uint64, _int, _vp]),
+    "h3q_checkpoint_qlinear": (_int, [_vp, ctypes.c_char_p, _vp]),
     "h3q_version": (ctypes.c_char_p, []),
     "h3q_available_arch": (_int, [_int]),
     "h3q_can_fuse_rotation": (_int, [_sz, _sz]),

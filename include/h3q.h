@@ -190,6 +190,56 @@ h3q_status h3q_qlinear_forward(const h3q_qlinear* layer, const void* x, int x_ki
                                void* out, void* workspace, size_t workspace_bytes, const h3q_switches* sw,
                                void* stream);
 
+/* ---------------------------------------------------------------------------------------------------------
+ * ComfyUI checkpoints: the safetensors files the reference reads with SafeFile (weights.rs:23-139) and the layer
+ * description QLinear::load derives from them (weights.rs:493-534).  Host code; uploads use the caller's stream.
+ * ------------------------------------------------------------------------------------------------------- */
+enum { /* storage dtypes (SafeFile::storage_dtype, weights.rs:99-112) */
+  H3Q_DT_F32 = 0, H3Q_DT_F16 = 1, H3Q_DT_BF16 = 2, H3Q_DT_I8 = 3, H3Q_DT_U8 = 4, H3Q_DT_F8_E4M3 = 5,
+  H3Q_DT_BOOL = 6, H3Q_DT_I32 = 7, H3Q_DT_I64 = 8, H3Q_DT_F64 = 9
+};
+typedef struct h3q_checkpoint h3q_checkpoint;
+
+/* SafeFile::open (weights.rs:33-58): reads and checks the header (every tensor's offsets inside the file and its
+ * byte count equal to its element count times its dtype size); tensor names lose the "model.diffusion_model."
+ * prefix as in the reference.  Close with h3q_checkpoint_close. */
+h3q_status h3q_checkpoint_open(const char* path, h3q_checkpoint** out);
+void h3q_checkpoint_close(h3q_checkpoint* f);
+/* Tensor names in sorted order (i < count); NULL past the end. */
+int64_t h3q_checkpoint_count(const h3q_checkpoint* f);
+const char* h3q_checkpoint_name(const h3q_checkpoint* f, int64_t i);
+/* SafeFile::has (weights.rs:60-62): 1 if the tensor exists. */
+int h3q_checkpoint_has(const h3q_checkpoint* f, const char* name);
+/* The "__metadata__" value of `key` (non-string values as their JSON text), or NULL. */
+const char* h3q_checkpoint_metadata(const h3q_checkpoint* f, const char* key);
+/* SafeFile::info / shape (weights.rs:64-78): storage dtype (H3Q_DT_*), rank, shape (up to 8 dims), bytes. */
+h3q_status h3q_checkpoint_info(const h3q_checkpoint* f, const char* name, int* dtype, int* ndim, int64_t* shape,
+                               uint64_t* nbytes);
+/* SafeFile::read_into (weights.rs:80-87): the tensor's bytes into host memory (pread). */
+h3q_status h3q_checkpoint_read(const h3q_checkpoint* f, const char* name, void* dst, uint64_t dst_bytes);
+/* The tensor's bytes to device memory: pread into two pinned staging buffers whose copies run on `stream`, so
+ * reading and copying overlap; returns when the data is on the device.  With interleave_halves the first
+ * dimension's two halves (gate rows, then up rows) land interleaved, row i of each half at rows 2i and 2i + 1:
+ * QLinear::interleave_swiglu (weights.rs:679-687, :765-800) done by the copy itself. */
+h3q_status h3q_checkpoint_upload(const h3q_checkpoint* f, const char* name, void* dst, uint64_t dst_bytes,
+                                 int interleave_halves, void* stream);
+
+typedef struct {
+  int format;             /* H3Q_FMT_* from "<prefix>.comfy_quant" ({"format": ...}; absent: dense) */
+  int convrot;            /* int8_tensorwise with "convrot": true -> "convrot_groupsize" (default 256); else 0 */
+  int64_t out_features;   /* weight rows */
+  int64_t in_features;    /* weight columns (NVFP4: twice the packed byte columns) */
+  int weight_dtype;       /* H3Q_DT_* of "<prefix>.weight" */
+  int scale_dtype;        /* H3Q_DT_* of "<prefix>.weight_scale" (int8: f32 per row or scalar; NVFP4: e4m3 blocks) */
+  int64_t scale_numel;    /* elements of "<prefix>.weight_scale" */
+  int has_bias;           /* "<prefix>.bias" exists */
+  int has_pre_quant_scale;/* NVFP4 AWQ "<prefix>.pre_quant_scale" exists ("<prefix>.weight_scale_2" is required) */
+} h3q_qlinear_spec;
+
+/* QLinear::load's format decision (weights.rs:495-525) for the layer at `prefix`: which tensors the layer has and
+ * how to run it.  Unknown formats fail with the reference's message. */
+h3q_status h3q_checkpoint_qlinear(const h3q_checkpoint* f, const char* prefix, h3q_qlinear_spec* spec);
+
 /* kernels::rms_modulate (kernels.rs:1201-1204, kernel :376-401) for bf16 rows: out = bf16(fma(n, 1 + bf16(scale[
  * idx[s], c]), bf16(shift[idx[s], c]))) with n = bf16((x * rsqrt(mean(x^2) + eps)) * w[c]), the mean summed in
  * the reference kernel's order.  x, out bf16 [S, C]; w bf16 [C]; scale, shift f32 [R, C]; idx u32 [S].  This build
