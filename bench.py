@@ -285,6 +285,66 @@ def attend_step_c4(dev, reps: int = 5, S: int = 32760, H: int = 40, rot: int = 9
     return res
 
 
+def streaming_c1(layers, M: int, dev, reps: int = 3) -> dict:
+    """The config-1 step with its weights kept in pinned host memory and streamed to the GPU through a 2-slot ring
+    (h3q_streamer; the reference's copy-stream uploads for weights that do not stay on the GPU, weights.rs:185-273):
+    the copy of linear i+1 runs on the copy stream while linear i computes.  Compared with the same step on resident
+    weights and with the copies alone; the weight bytes cross PCIe every step, so the bound is the slower of the
+    two."""
+    import torch
+    import h3q
+    from h3q.streaming import WeightStreamer
+    host = [(ly["w"].cpu().pin_memory(), ly["ws"].cpu().pin_memory(), ly["b"].cpu().pin_memory()) for ly in layers]
+    slot = max(w.numel() + 4 * (s.numel() + b.numel()) for w, s, b in host) + 1024
+    ws = WeightStreamer(slot, 2, dev)
+    L = h3q.lib()
+    sp = torch.cuda.current_stream(dev).cuda_stream
+
+    def linear(ly, w, s, b):
+        h3q.check(L.h3q_quant_rows_i8(ly["x"].data_ptr(), 2, ly["q"].data_ptr(), ly["xs"].data_ptr(), M, ly["k"], 1, sp))
+        h3q.check(L.h3q_gemm_s8_quantized(ly["q"].data_ptr(), ly["xs"].data_ptr(), w.data_ptr(), s.data_ptr(), ly["n"],
+                                          b.data_ptr(), ly["out"].data_ptr(), 2, M, ly["n"], ly["k"], h3q.EPI_LINEAR,
+                                          None, None, None, sp))
+
+    def streamed():
+        nxt = ws.fetch(list(host[0]))
+        for i, ly in enumerate(layers):
+            cur = nxt
+            if i + 1 < len(layers):
+                nxt = ws.fetch(list(host[i + 1]))
+            (w, s, b), k = cur
+            linear(ly, w, s, b)
+            ws.release(k)
+
+    def resident():
+        for ly in layers:
+            linear(ly, ly["w"], ly["ws"], ly["b"])
+
+    def copies_only():
+        for i in range(len(layers)):
+            _, k = ws.fetch(list(host[i]))
+            ws.release(k)
+
+    res = {}
+    for name, fn in (("resident", resident), ("streamed", streamed), ("copies_only", copies_only)):
+        for _ in range(2):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        res[name + "_ms"] = round(e0.elapsed_time(e1) / reps, 3)
+    wbytes = sum(w.numel() + 4 * (s.numel() + b.numel()) for w, s, b in host)
+    res["weight_bytes_per_step"] = wbytes
+    res["h2d_gbs"] = round(wbytes / (res["copies_only_ms"] * 1e-3) / 1e9, 1)
+    # the step can be no faster than the slower of its compute and its weight copies
+    res["overlap_efficiency"] = round(max(res["resident_ms"], res["copies_only_ms"]) / res["streamed_ms"], 3)
+    ws.close()
+    return res
+
+
 def modulate_fused(dev, peaks: dict, reps: int = 10, M: int = 32760, C: int = 5120) -> dict:
     """The step in front of the qkv and fc1 linears: RMSNorm + adaLN modulate, then the rotated int8 quantizer.
     "two_pass" runs h3q_rms_modulate (bf16 row to memory) then h3q_quant_rows_i8, as the reference's
@@ -619,6 +679,7 @@ def main() -> None:
     att = attention_c4(dev, load_peaks()) if rank == 0 else None
     modq = modulate_fused(dev, load_peaks()) if rank == 0 else None
     attend = attend_step_c4(dev) if rank == 0 else None
+    stream_c1 = streaming_c1(layers, M, dev) if rank == 0 else None
 
     cb = None
     if rank == 0 and ws_n == 1 and not args.no_cpu_baseline:
@@ -650,6 +711,7 @@ def main() -> None:
         "attention_c4": att,
         "modulate_quant": modq,
         "attend_step_c4": attend,
+        "weight_streaming_c1": stream_c1,
         "multi_gpu": extras,
         "cpu_baseline": cb, "e2e": e2e, "clocks": clk.summary(),
         "gpu_launches": 2 * launches,

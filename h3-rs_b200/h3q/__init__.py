@@ -41,6 +41,12 @@ PATH_GEMM_S8, PATH_INT8_LINEAR, PATH_ROTATE_FUSED, PATH_ROTATE_SEPARATE, PATH_SW
 # name -> (restype, argtypes) of every symbol include/h3q.h declares
 SIGNATURES = {
     "h3q_last_error": (ctypes.c_char_p, []),
+    "h3q_streamer_create": (_int, [_sz, _int, ctypes.POINTER(_vp)]),
+    "h3q_streamer_destroy": (None, [_vp]),
+    "h3q_streamer_slot_bytes": (_sz, [_vp]),
+    "h3q_streamer_fetch": (_int, [_vp, ctypes.POINTER(_vp), ctypes.POINTER(_sz), _int, _vp, ctypes.POINTER(_int),
+                                  ctypes.POINTER(_vp)]),
+    "h3q_streamer_release": (_int, [_vp, _int, _vp]),
     "h3q_checkpoint_open": (_int, [ctypes.c_char_p, ctypes.POINTER(_vp)]),
     "h3q_checkpoint_close": (None, [_vp]),
     "h3q_checkpoint_count": (_i64, [_vp]),

@@ -240,6 +240,27 @@ typedef struct {
  * how to run it.  Unknown formats fail with the reference's message. */
 h3q_status h3q_checkpoint_qlinear(const h3q_checkpoint* f, const char* prefix, h3q_qlinear_spec* spec);
 
+/* Weight streaming (weights.rs:185-273 upload_u8_async on a per-device copy stream; the per-block fetch of
+ * dit.rs:1160-1186): for weights that stay in host memory (pinned, for the copies to overlap), a ring of device
+ * slots filled on the streamer's own copy stream.  Everything is ordered by events on the device, the host never
+ * waits: a fetch into a slot waits (on the copy stream) for the release of the slot's previous contents and makes
+ * the compute stream wait for its copy.  The ring's slot count bounds how far uploads run ahead. */
+typedef struct h3q_streamer h3q_streamer;
+/* Set-up on the current device: `slots` device slots of slot_bytes (rounded up to 256) and a copy stream. */
+h3q_status h3q_streamer_create(size_t slot_bytes, int slots, h3q_streamer** out);
+/* Waits for the streamer's outstanding work and frees it. */
+void h3q_streamer_destroy(h3q_streamer* s);
+/* Bytes per slot (after rounding). */
+size_t h3q_streamer_slot_bytes(const h3q_streamer* s);
+/* Copies the n host regions src[i] (bytes[i] each) into the ring's next slot, each region at a 256-byte aligned
+ * offset, and returns the slot index and each region's device address (dst[i]).  Kernels enqueued on
+ * compute_stream after the call see the data.  The slot must not be held: release each slot (below) before the
+ * ring comes back to it. */
+h3q_status h3q_streamer_fetch(h3q_streamer* s, const void* const* src, const size_t* bytes, int n,
+                              void* compute_stream, int* slot, void** dst);
+/* Marks the slot free once compute_stream reaches this point: call it after enqueuing the slot's last reader. */
+h3q_status h3q_streamer_release(h3q_streamer* s, int slot, void* compute_stream);
+
 /* kernels::rms_modulate (kernels.rs:1201-1204, kernel :376-401) for bf16 rows: out = bf16(fma(n, 1 + bf16(scale[
  * idx[s], c]), bf16(shift[idx[s], c]))) with n = bf16((x * rsqrt(mean(x^2) + eps)) * w[c]), the mean summed in
  * the reference kernel's order.  x, out bf16 [S, C]; w bf16 [C]; scale, shift f32 [R, C]; idx u32 [S].  This build
