@@ -14,6 +14,7 @@ portable/kernels.rs:220-242) on the host cores, on a bounded row sample.  Under 
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import statistics
@@ -31,6 +32,7 @@ LINEARS = [("qkv", 5120, 15360), ("fc1", 5120, 13824), ("out", 5120, 5120), ("fc
 WORKLOAD = ("BASELINE c1: DiT-scale int8 ConvRot linears, M=32760 tokens; qkv 5120->15360, fc1 5120->13824, "
             "out 5120->5120, fc2 13824->5120; bf16 in/out, per-token int8 activations, int8 weights")
 NOMINAL_INT8_TOPS = 4500.0
+E2E_CHUNK = int(os.environ.get("H3Q_E2E_CHUNK", "2048"))  # rows per chunk of the host-memory path (e2e)
 
 
 def ops_per_step(m: int) -> float:
@@ -306,21 +308,26 @@ def streaming_c1(layers, M: int, dev, reps: int = 3) -> dict:
                                           b.data_ptr(), ly["out"].data_ptr(), 2, M, ly["n"], ly["k"], h3q.EPI_LINEAR,
                                           None, None, None, sp))
 
+    pending = []
+
     def streamed():
-        nxt = ws.fetch(list(host[0]))
+        # enqueue linear i, then fetch linear i+1: the fetch's wait lands on the compute stream after linear i, so
+        # the copy overlaps it (the first fetch of a step overlaps the previous step's last linear)
+        if not pending:
+            pending.append(ws.fetch(list(host[0])))
         for i, ly in enumerate(layers):
-            cur = nxt
-            if i + 1 < len(layers):
-                nxt = ws.fetch(list(host[i + 1]))
-            (w, s, b), k = cur
+            (w, s, b), k = pending.pop(0)
             linear(ly, w, s, b)
             ws.release(k)
+            pending.append(ws.fetch(list(host[(i + 1) % len(layers)])))
 
     def resident():
         for ly in layers:
             linear(ly, ly["w"], ly["ws"], ly["b"])
 
     def copies_only():
+        while pending:
+            ws.release(pending.pop(0)[1])
         for i in range(len(layers)):
             _, k = ws.fetch(list(host[i]))
             ws.release(k)
@@ -341,6 +348,9 @@ def streaming_c1(layers, M: int, dev, reps: int = 3) -> dict:
     res["h2d_gbs"] = round(wbytes / (res["copies_only_ms"] * 1e-3) / 1e9, 1)
     # the step can be no faster than the slower of its compute and its weight copies
     res["overlap_efficiency"] = round(max(res["resident_ms"], res["copies_only_ms"]) / res["streamed_ms"], 3)
+    torch.cuda.synchronize()
+    for (_, k) in pending:
+        ws.release(k)
     ws.close()
     return res
 
@@ -632,21 +642,21 @@ def main() -> None:
         with open(tpath) as f:
             traffic = json.load(f).get("dram_bytes_per_launch")
 
-    # end to end through the C ABI with host buffers: H2D of each linear's input, gemm_s8, D2H of its output
+    # end to end through the C ABI with host buffers: every linear's input comes from pinned host memory and its
+    # output goes back to it (h3q_host_pipeline_gemm_s8: chunked copies in and out overlapped with the GEMMs)
     e2e = None
     if rank == 0 or True:
         host_x = [ly["x"].cpu().pin_memory() for ly in layers]
         host_o = [torch.empty((M, ly["n"]), dtype=torch.bfloat16).pin_memory() for ly in layers]
-        wsp = torch.empty(max(L.h3q_gemm_s8_workspace_size(M, ly["k"]) for ly in layers), dtype=torch.uint8, device=dev)
-        xdev = [torch.empty_like(ly["x"]) for ly in layers]
+        pipe = ctypes.c_void_p()
+        h3q.check(L.h3q_host_pipeline_create(E2E_CHUNK, max(ly["k"] for ly in layers), max(ly["n"] for ly in layers),
+                                             ctypes.byref(pipe)))
 
         def e2e_step():
             for i, ly in enumerate(layers):
-                xdev[i].copy_(host_x[i], non_blocking=True)
-                h3q.check(L.h3q_gemm_s8(xdev[i].data_ptr(), ly["w"].data_ptr(), ly["ws"].data_ptr(), ly["n"],
-                                        ly["b"].data_ptr(), ly["out"].data_ptr(), M, ly["n"], ly["k"], 0, 1,
-                                        wsp.data_ptr(), wsp.numel(), sp))
-                host_o[i].copy_(ly["out"], non_blocking=True)
+                h3q.check(L.h3q_host_pipeline_gemm_s8(pipe, host_x[i].data_ptr(), ly["w"].data_ptr(),
+                                                      ly["ws"].data_ptr(), ly["n"], ly["b"].data_ptr(),
+                                                      host_o[i].data_ptr(), M, ly["n"], ly["k"], 0, 1, sp))
 
         e2e_step()
         torch.cuda.synchronize()
@@ -665,7 +675,9 @@ def main() -> None:
         e2e = {"value": ws_n * ops_per_step(M) / (e_ms * 1e-3) / 1e12, "unit": "TOPS",
                "h2d_bytes_per_step": int(sum(h.numel() * 2 for h in host_x)),
                "d2h_bytes_per_step": int(sum(h.numel() * 2 for h in host_o)), "ms_per_step": e_ms,
-               "path": "h3q_gemm_s8 (C ABI) with pinned host input/output, copies inside the timed region"}
+               "path": f"h3q_host_pipeline_gemm_s8 (C ABI): pinned host input and output, {E2E_CHUNK}-row chunks "
+                       "whose copies in and out overlap the GEMMs, copies inside the timed region"}
+        L.h3q_host_pipeline_destroy(pipe)
 
     extras = None
     if dist is not None:

@@ -41,6 +41,9 @@ PATH_GEMM_S8, PATH_INT8_LINEAR, PATH_ROTATE_FUSED, PATH_ROTATE_SEPARATE, PATH_SW
 # name -> (restype, argtypes) of every symbol include/h3q.h declares
 SIGNATURES = {
     "h3q_last_error": (ctypes.c_char_p, []),
+    "h3q_host_pipeline_create": (_int, [_i64, _i64, _i64, ctypes.POINTER(_vp)]),
+    "h3q_host_pipeline_destroy": (None, [_vp]),
+    "h3q_host_pipeline_gemm_s8": (_int, [_vp, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _int, _int, _vp]),
     "h3q_streamer_create": (_int, [_sz, _int, ctypes.POINTER(_vp)]),
     "h3q_streamer_destroy": (None, [_vp]),
     "h3q_streamer_slot_bytes": (_sz, [_vp]),
@@ -475,6 +478,43 @@ def attention_core(q8, qs, k8, ks, vt, flags: int = 0, scores: bool = False):
     check(lib().h3q_attention_core(_p(q8), _p(qs), _p(k8), _p(ks), _p(vt), _p(out), S, H, flags, _p(sc),
                                    _stream(q8.device)))
     return (out, sc) if scores else out
+
+
+class HostPipeline:
+    """gemm_s8 on pinned host activations with the copies in, the GEMMs and the copies out overlapped
+    (h3q_host_pipeline_*)."""
+
+    def __init__(self, chunk_rows: int, max_k: int, max_n: int, device=None):
+        import torch
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        h = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            check(lib().h3q_host_pipeline_create(chunk_rows, max_k, max_n, ctypes.byref(h)))
+        self._h = h
+
+    def close(self) -> None:
+        if self._h:
+            lib().h3q_host_pipeline_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def gemm_s8(self, x_host, w, ws, bias=None, swiglu: bool = False, rotate: bool = False, out=None):
+        """x_host bf16 [M, K] (pinned host) -> bf16 [M, N] (or [M, N/2]) in pinned host memory; stream-ordered on
+        the current stream (synchronize before reading the result)."""
+        import torch
+        ws = ws.to(torch.float32).contiguous()
+        m, k = x_host.shape
+        n = w.shape[0]
+        if out is None:
+            out = torch.empty((m, n // 2 if swiglu else n), dtype=torch.bfloat16, pin_memory=True)
+        check(lib().h3q_host_pipeline_gemm_s8(self._h, _p(x_host), _p(w), _p(ws), ws.numel(), _p(bias), _p(out), m, n,
+                                              k, int(swiglu), int(rotate), _stream(self.device)))
+        return out
 
 
 def default_switches() -> Switches:

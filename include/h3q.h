@@ -81,6 +81,21 @@ h3q_status h3q_gemm_s8(const uint16_t* x, const int8_t* w, const float* ws, int6
                        uint16_t* out, int64_t m, int64_t n, int64_t k, int swiglu, int rotate, void* workspace,
                        size_t workspace_bytes, void* stream);
 
+/* gemm_s8 on activations in host memory (no counterpart in the reference, whose ops take device tensors): the
+ * rows are processed in chunks whose copy in (one copy stream), GEMM (the caller's stream) and copy out (a second
+ * copy stream) overlap, double-buffered, so both PCIe directions and the tensor cores work at once.  Set-up
+ * allocates two chunk buffers for inputs of up to max_k columns and outputs of up to max_n columns, the GEMM's
+ * workspace and the streams. */
+typedef struct h3q_host_pipeline h3q_host_pipeline;
+h3q_status h3q_host_pipeline_create(int64_t chunk_rows, int64_t max_k, int64_t max_n, h3q_host_pipeline** out);
+void h3q_host_pipeline_destroy(h3q_host_pipeline* p);
+/* out_host [m, n] (or [m, n/2] with swiglu) = h3q_gemm_s8(x_host [m, k]) with host buffers (pinned, for the copies
+ * to overlap).  Ordered after the work already on `stream`; `stream` waits for the last copy out, so the output
+ * is in host memory once `stream` has reached that point, and one call's output can feed the next call. */
+h3q_status h3q_host_pipeline_gemm_s8(h3q_host_pipeline* p, const uint16_t* x_host, const int8_t* w, const float* ws,
+                                     int64_t ws_numel, const float* bias, uint16_t* out_host, int64_t m, int64_t n,
+                                     int64_t k, int swiglu, int rotate, void* stream);
+
 /* Workspace bytes h3q_int8_linear_ex needs. */
 size_t h3q_int8_linear_workspace_size(int64_t m, int64_t k);
 
@@ -254,8 +269,9 @@ void h3q_streamer_destroy(h3q_streamer* s);
 size_t h3q_streamer_slot_bytes(const h3q_streamer* s);
 /* Copies the n host regions src[i] (bytes[i] each) into the ring's next slot, each region at a 256-byte aligned
  * offset, and returns the slot index and each region's device address (dst[i]).  Kernels enqueued on
- * compute_stream after the call see the data.  The slot must not be held: release each slot (below) before the
- * ring comes back to it. */
+ * compute_stream after the call see the data: the call places the wait for the copy on compute_stream at this
+ * point, so enqueue the current layer's kernels first and fetch the next layer after them, and the copy overlaps
+ * them.  The slot must not be held: release each slot (below) before the ring comes back to it. */
 h3q_status h3q_streamer_fetch(h3q_streamer* s, const void* const* src, const size_t* bytes, int n,
                               void* compute_stream, int* slot, void** dst);
 /* Marks the slot free once compute_stream reaches this point: call it after enqueuing the slot's last reader. */

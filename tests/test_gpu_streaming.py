@@ -31,15 +31,16 @@ def test_streamed_layers_equal_resident_layers(cuda, slots):
     want = [h3q.gemm_s8(x, w.to(cuda), s.to(cuda), b.to(cuda), rotate=True) for w, s, b in layers]
     ws = WeightStreamer(N * K + 2 * 4 * N + 512, slots, cuda)
     got, pending = [], []
-    ahead = slots - 1  # layers fetched ahead of the one being computed
-    for i in range(min(ahead, len(layers))):
+    # up to `slots` layers resident; each layer's kernels are enqueued before the next fetch, so the copy of the
+    # next layer overlaps them
+    for i in range(min(slots, len(layers))):
         pending.append(ws.fetch(list(layers[i])))
     for i in range(len(layers)):
-        if i + ahead < len(layers):
-            pending.append(ws.fetch(list(layers[i + ahead])))
         (w, s, b), slot = pending.pop(0)
         got.append(h3q.gemm_s8(x, w, s, b, rotate=True))
         ws.release(slot)
+        if i + slots < len(layers):
+            pending.append(ws.fetch(list(layers[i + slots])))
     torch.cuda.synchronize()
     for a, b in zip(got, want):
         assert torch.equal(a.view(torch.int16), b.view(torch.int16))
