@@ -273,11 +273,10 @@ h3q_status h3q_attend_qkv(const uint16_t* qkv, int64_t qkv_width, int64_t q_col,
     if (cols[i] < 0 || qkv_width < cols[i] + H * HD)
       return fail(H3Q_ERR_ARG, "%s: columns [%lld, %lld) outside a qkv row of width %lld", what, (long long)cols[i],
                   (long long)(cols[i] + H * HD), (long long)qkv_width);
-  if ((reinterpret_cast<uintptr_t>(qkv) & 7u) || qkv_width % 4 || q_col % 4 || k_col % 4)
-    return fail(H3Q_ERR_ARG, "%s: qkv must be 8-byte aligned with width and q / k columns multiples of 4", what);
-  if (do_norm && ((q_norm && (reinterpret_cast<uintptr_t>(q_norm) & 7u)) ||
-                  (k_norm && (reinterpret_cast<uintptr_t>(k_norm) & 7u))))
-    return fail(H3Q_ERR_ARG, "%s: norm weights must be 8-byte aligned", what);
+  if (!aligned16(qkv) || qkv_width % 8 || q_col % 8 || k_col % 8)
+    return fail(H3Q_ERR_ARG, "%s: qkv must be 16-byte aligned with width and q / k columns multiples of 8", what);
+  if (do_norm && ((q_norm && !aligned16(q_norm)) || (k_norm && !aligned16(k_norm))))
+    return fail(H3Q_ERR_ARG, "%s: norm weights must be 16-byte aligned", what);
   if (!rope) rot = 0;
   if (rot < 0 || rot % 8 != 0 || rot > HD)
     return fail(H3Q_ERR_UNSUPPORTED, "%s: this build rotates rot %% 8 == 0 dims, rot <= 128 (rot = %d); use "

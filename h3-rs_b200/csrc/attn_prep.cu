@@ -595,6 +595,255 @@ __global__ void __launch_bounds__(BLOCK ? 512 : 256, BLOCK ? 2 : 3) qk_rope_quan
   }
 }
 
+// Pair layout (D = 128, rot % 32 == 0): thread t of a row's four holds the rotation pairs (j, j + half) for
+// j in [tQ, tQ + Q), Q = half / 4, and the unrotated dims [rot + tN, rot + tN + N), N = (128 - rot) / 4: 32 values,
+// each cos / sin entry read once and both elements of a pair in the same thread, so no exchange.  The sum of
+// squares still comes from the thread's 32-dim slice (the reference's order); that load brings the row into L1
+// for the pair-layout load after it.
+template <int ROT>
+struct Pairs {
+  static constexpr int HALF = ROT / 2, Q = HALF / 4, N = (128 - ROT) / 4;
+  static_assert(ROT % 32 == 0 && ROT <= 128, "pair layout: rot % 32 == 0");
+  // dim of value i (0..31) of thread t
+  __device__ static int dim(int t, int i) { return i < Q ? t * Q + i : (i < 2 * Q ? HALF + t * Q + (i - Q) : ROT + t * N + (i - 2 * Q)); }
+  __device__ static int seg_base(int t, int sgm) { return sgm == 0 ? t * Q : (sgm == 1 ? HALF + t * Q : ROT + t * N); }
+};
+
+// n bf16 values (n % 4 == 0, 8-byte aligned) -> f32
+template <int n>
+__device__ __forceinline__ void load_seg(const uint16_t* __restrict__ p, float* v) {
+#pragma unroll
+  for (int c = 0; c < n / 4; ++c) {
+    const uint2 u = __ldg(reinterpret_cast<const uint2*>(p) + c);
+    v[4 * c] = lo16(u.x);
+    v[4 * c + 1] = hi16(u.x);
+    v[4 * c + 2] = lo16(u.y);
+    v[4 * c + 3] = hi16(u.y);
+  }
+}
+
+template <int ROT>
+__device__ __forceinline__ void pair_norm_rope(const uint16_t* __restrict__ xr, int t, const uint16_t* __restrict__ w,
+                                               int do_norm, float eps, const float* __restrict__ cs, int64_t s,
+                                               int64_t S, uint32_t (&res)[16]) {
+  using L = Pairs<ROT>;
+  constexpr int Q = L::Q, N = L::N, HALF = L::HALF;
+  float inv = 1.f;
+  if (do_norm) {
+    uint32_t raw[16];
+    load_slice(xr + 32 * t, raw);
+    float a[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float x0 = elem(raw, i), x1 = elem(raw, i + 16);
+      a[i] = __fadd_rn(__fmul_rn(x0, x0), __fmul_rn(x1, x1));
+    }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1)
+#pragma unroll
+      for (int i = 0; i < o; ++i) a[i] = __fadd_rn(a[i], a[i + o]);
+    float tt = __fadd_rn(a[0], __shfl_xor_sync(0xffffffffu, a[0], 2));
+    tt = __fadd_rn(tt, __shfl_xor_sync(0xffffffffu, tt, 1));
+    inv = rsqrtf(__fadd_rn(__fdiv_rn(tt, 128.f), eps));
+  }
+  float v[32];
+  if (Q > 0) {
+    load_seg<Q>(xr + t * Q, v);
+    load_seg<Q>(xr + HALF + t * Q, v + Q);
+  }
+  if (N > 0) load_seg<N>(xr + ROT + t * N, v + 2 * Q);
+  if (do_norm) {
+    float wv[32];
+    if (w) {
+      if (Q > 0) {
+        load_seg<Q>(w + t * Q, wv);
+        load_seg<Q>(w + HALF + t * Q, wv + Q);
+      }
+      if (N > 0) load_seg<N>(w + ROT + t * N, wv + 2 * Q);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) wv[i] = 1.f;
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __fmul_rn(__fmul_rn(v[i], inv), wv[i]);
+  }
+  if (Q > 0) {
+    const float4* c4 = reinterpret_cast<const float4*>(cs + s * HALF + t * Q);
+    const float4* s4 = reinterpret_cast<const float4*>(cs + (S + s) * HALF + t * Q);
+#pragma unroll
+    for (int c = 0; c < Q / 4; ++c) {
+      const float4 cc = __ldg(c4 + c), ss = __ldg(s4 + c);
+      const float cv[4] = {cc.x, cc.y, cc.z, cc.w}, sv[4] = {ss.x, ss.y, ss.z, ss.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float a = v[4 * c + i], b = v[Q + 4 * c + i];
+        v[4 * c + i] = rope_lo(a, cv[i], b, sv[i]);
+        v[Q + 4 * c + i] = rope_hi(b, cv[i], a, sv[i]);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) res[i] = pack_bf16_ref(v[2 * i], v[2 * i + 1]);
+}
+
+// Standalone qk_norm_rope, pair layout: CTA of 8 warps = 64 tokens looping over `hb` heads.
+template <int ROT>
+__global__ void __launch_bounds__(256) qk_norm_rope_pairs_kernel(const uint16_t* __restrict__ x, int64_t rs,
+                                                                 int64_t col, int64_t hs,
+                                                                 const uint16_t* __restrict__ w, int do_norm,
+                                                                 float eps, const float* __restrict__ cs,
+                                                                 uint16_t* __restrict__ out, int64_t S, int H, int hb) {
+  using L = Pairs<ROT>;
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5, t = lane & 3;
+  int64_t s = (int64_t)blockIdx.x * 64 + wp * kRowsPerWarp + (lane >> 2);
+  const bool valid = s < S;
+  if (!valid) s = S - 1;  // a real row: its lanes compute alongside (shuffles) and store nothing
+  const int h1 = min(H, (int)(blockIdx.y + 1) * hb);
+  for (int h = blockIdx.y * hb; h < h1; ++h) {
+    uint32_t res[16];
+    pair_norm_rope<ROT>(x + s * rs + col + (int64_t)h * hs, t, w, do_norm, eps, cs, s, S, res);
+    if (valid) {
+      uint16_t* o = out + (s * H + h) * HD;
+      // segments of Q, Q and N values: 4 bf16 (one uint2) per store
+      int idx = 0;
+#pragma unroll
+      for (int sg = 0; sg < 3; ++sg) {
+        const int n = sg < 2 ? L::Q : L::N;
+        uint2* d = reinterpret_cast<uint2*>(o + L::seg_base(t, sg));
+#pragma unroll
+        for (int c = 0; c < n / 4; ++c) d[c] = make_uint2(res[idx / 2 + 2 * c], res[idx / 2 + 2 * c + 1]);
+        idx += n;
+      }
+    }
+  }
+}
+
+// K column sums, pair layout: as kmean_rope_partial_kernel, the rows turned through a padded row buffer.
+template <int ROT>
+__global__ void __launch_bounds__(256) kmean_rope_pairs_kernel(const uint16_t* __restrict__ x, int64_t rs,
+                                                               int64_t col, const uint16_t* __restrict__ w,
+                                                               int do_norm, float eps, const float* __restrict__ cs,
+                                                               float* __restrict__ part, int64_t S, int H,
+                                                               int rows_per) {
+  using L = Pairs<ROT>;
+  constexpr int RS = 132;  // padded row stride (floats)
+  __shared__ __align__(16) float buf[8][kRowsPerWarp * RS];
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5, t = lane & 3, r = lane >> 2;
+  const int h = blockIdx.y * 8 + wp;
+  if (h >= H) return;
+  const int64_t r0 = (int64_t)blockIdx.x * rows_per;
+  const int64_t r1 = r0 + rows_per < S ? r0 + rows_per : S;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  float* b = buf[wp];
+  for (int64_t g = r0; g < r1; g += kRowsPerWarp) {
+    int64_t s = g + r;
+    if (s >= r1) s = r1 - 1;  // a real row whose values are not added
+    uint32_t res[16];
+    pair_norm_rope<ROT>(x + s * rs + col + (int64_t)h * HD, t, w, do_norm, eps, cs, s, S, res);
+    int idx = 0;
+#pragma unroll
+    for (int sg = 0; sg < 3; ++sg) {
+      const int n = sg < 2 ? L::Q : L::N;
+      float4* d = reinterpret_cast<float4*>(b + r * RS + L::seg_base(t, sg));
+#pragma unroll
+      for (int c = 0; c < n / 4; ++c) {
+        const uint32_t p0 = res[idx / 2 + 2 * c], p1 = res[idx / 2 + 2 * c + 1];
+        d[c] = make_float4(lo16(p0), hi16(p0), lo16(p1), hi16(p1));
+      }
+      idx += n;
+    }
+    __syncwarp();
+    const int nr = (int)(r1 - g < kRowsPerWarp ? r1 - g : kRowsPerWarp);
+    for (int rr = 0; rr < nr; ++rr) {
+      const float4 f = *reinterpret_cast<const float4*>(b + rr * RS + 4 * lane);
+      acc[0] = __fadd_rn(acc[0], f.x);
+      acc[1] = __fadd_rn(acc[1], f.y);
+      acc[2] = __fadd_rn(acc[2], f.z);
+      acc[3] = __fadd_rn(acc[3], f.w);
+    }
+    __syncwarp();
+  }
+  reinterpret_cast<float4*>(part + (int64_t)blockIdx.x * H * HD + (int64_t)h * HD)[lane] =
+      make_float4(acc[0], acc[1], acc[2], acc[3]);
+}
+
+// Normalise + rotate + (K: subtract the column mean) + quantise, pair layout; CTA as qk_rope_quant_kernel.
+template <int ROT, bool BLOCK>
+__global__ void __launch_bounds__(BLOCK ? 512 : 256) qk_rope_quant_pairs_kernel(
+    const uint16_t* __restrict__ x, int64_t rs, int64_t col, const uint16_t* __restrict__ w, int do_norm, float eps,
+    const float* __restrict__ cs, const float* __restrict__ mean, int8_t* __restrict__ codes,
+    float* __restrict__ scales, int64_t S, int64_t Sp, int H, int hb) {
+  using L = Pairs<ROT>;
+  __shared__ float red[2][16];
+  constexpr int TOK = BLOCK ? 128 : 64;
+  const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5, t = lane & 3;
+  const int64_t s = (int64_t)blockIdx.x * TOK + wp * kRowsPerWarp + (lane >> 2);
+  const bool valid = s < S;
+  const int64_t sr = valid ? s : S - 1;  // rows past S compute on a real row and take no part
+  const int h0 = blockIdx.y * hb, h1 = min(H, h0 + hb);
+  for (int h = h0; h < h1; ++h) {
+    uint32_t res[16];
+    pair_norm_rope<ROT>(x + sr * rs + col + (int64_t)h * HD, t, w, do_norm, eps, cs, sr, S, res);
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      v[2 * i] = lo16(res[i]);
+      v[2 * i + 1] = hi16(res[i]);
+    }
+    {
+      int idx = 0;
+#pragma unroll
+      for (int sg = 0; sg < 3; ++sg) {
+        const int n = sg < 2 ? L::Q : L::N;
+        const float4* mp = reinterpret_cast<const float4*>(mean + (int64_t)h * HD + L::seg_base(t, sg));
+#pragma unroll
+        for (int c = 0; c < n / 4; ++c) {
+          const float4 m4 = mean ? __ldg(mp + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+          v[idx + 4 * c] = __fsub_rn(v[idx + 4 * c], m4.x);
+          v[idx + 4 * c + 1] = __fsub_rn(v[idx + 4 * c + 1], m4.y);
+          v[idx + 4 * c + 2] = __fsub_rn(v[idx + 4 * c + 2], m4.z);
+          v[idx + 4 * c + 3] = __fsub_rn(v[idx + 4 * c + 3], m4.w);
+        }
+        idx += n;
+      }
+    }
+    float m = 0.f;
+    if (valid) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) m = fmaxf(m, fabsf(v[i]));
+    }
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+    if (BLOCK) {
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      const int par = (h - h0) & 1;
+      if (lane == 0) red[par][wp] = m;
+      __syncthreads();
+      m = red[par][0];
+#pragma unroll
+      for (int i = 1; i < 16; ++i) m = fmaxf(m, red[par][i]);
+    }
+    const float sc = fmaxf(__fdiv_rn(m, 127.f), 1e-20f);
+    if (valid) {
+      const float inv = __fdiv_rn(1.f, sc);
+      int8_t* row = codes + ((int64_t)h * S + s) * HD;
+      int idx = 0;
+#pragma unroll
+      for (int sg = 0; sg < 3; ++sg) {
+        const int n = sg < 2 ? L::Q : L::N;
+        uint32_t* d = reinterpret_cast<uint32_t*>(row + L::seg_base(t, sg));
+#pragma unroll
+        for (int c = 0; c < n / 4; ++c)
+          d[c] = q127(v[idx + 4 * c], inv) | (q127(v[idx + 4 * c + 1], inv) << 8) |
+                 (q127(v[idx + 4 * c + 2], inv) << 16) | (q127(v[idx + 4 * c + 3], inv) << 24);
+        idx += n;
+      }
+    }
+    if (t == 0 && s < Sp) scales[(int64_t)h * Sp + s] = valid ? sc : 0.f;
+  }
+}
+
 }  // namespace
 
 // ------------------------------------------------------------------------------------------------ launchers
@@ -659,6 +908,15 @@ cudaError_t launch_qk_norm_rope(const uint16_t* x, int64_t rs, int64_t col, int6
   if (D == HD && rot % 8 == 0 && a16 && wa && ca) {
     const int hb = H < 8 ? (int)H : 8;
     const dim3 grid((unsigned)((S + 63) / 64), (unsigned)((H + hb - 1) / hb));
+    switch (rot) {  // rotation pairs held by one thread where the pairs split evenly over a row's four threads
+#define H3Q_PAIRS(R)                                                                                            \
+  case R:                                                                                                      \
+    qk_norm_rope_pairs_kernel<R><<<grid, 256, 0, st>>>(x, rs, col, hs, w, do_norm, eps, cs, out, S, (int)H, hb); \
+    return cudaGetLastError();
+      H3Q_PAIRS(0) H3Q_PAIRS(32) H3Q_PAIRS(64) H3Q_PAIRS(96) H3Q_PAIRS(128)
+#undef H3Q_PAIRS
+      default: break;
+    }
     qk_norm_rope128_kernel<<<grid, 256, 0, st>>>(x, rs, col, hs, w, do_norm, eps, cs, rot / 2, out, S, (int)H, hb);
     return cudaGetLastError();
   }
@@ -677,8 +935,18 @@ cudaError_t launch_kmean_rope(const uint16_t* x, int64_t rs, int64_t col, const 
   if (S <= 0 || H <= 0) return cudaSuccess;
   int parts, rows_per;
   kmean_partition(S, parts, rows_per);
-  kmean_rope_partial_kernel<<<dim3((unsigned)parts, (unsigned)((H + 7) / 8)), 256, 0, st>>>(
-      x, rs, col, w, do_norm, eps, cs, rot / 2, part, S, (int)H, rows_per);
+  const dim3 grid((unsigned)parts, (unsigned)((H + 7) / 8));
+  switch (rot) {
+#define H3Q_PAIRS(R)                                                                                             \
+  case R:                                                                                                       \
+    kmean_rope_pairs_kernel<R><<<grid, 256, 0, st>>>(x, rs, col, w, do_norm, eps, cs, part, S, (int)H, rows_per); \
+    break;
+    H3Q_PAIRS(0) H3Q_PAIRS(32) H3Q_PAIRS(64) H3Q_PAIRS(96) H3Q_PAIRS(128)
+#undef H3Q_PAIRS
+    default:
+      kmean_rope_partial_kernel<<<grid, 256, 0, st>>>(x, rs, col, w, do_norm, eps, cs, rot / 2, part, S, (int)H,
+                                                      rows_per);
+  }
   const int C = (int)(H * HD);
   const float inv_s = (float)(1.0 / (double)S);
   kmean_final_kernel<<<(C + 255) / 256, 256, 0, st>>>(part, parts, mean, C, inv_s);
@@ -696,6 +964,20 @@ cudaError_t launch_qk_rope_quant(const uint16_t* x, int64_t rs, int64_t col, con
   int hb = 8;
   while (hb > 1 && blocks * ((H + hb - 1) / hb) < 3 * (int64_t)sm_count(0)) hb >>= 1;
   const dim3 grid((unsigned)blocks, (unsigned)((H + hb - 1) / hb));
+  switch (rot) {
+#define H3Q_PAIRS(R)                                                                                               \
+  case R:                                                                                                         \
+    if (block128)                                                                                                 \
+      qk_rope_quant_pairs_kernel<R, true><<<grid, threads, 0, st>>>(x, rs, col, w, do_norm, eps, cs, mean, codes,  \
+                                                                    scales, S, Sp, (int)H, hb);                   \
+    else                                                                                                          \
+      qk_rope_quant_pairs_kernel<R, false><<<grid, threads, 0, st>>>(x, rs, col, w, do_norm, eps, cs, mean, codes, \
+                                                                     scales, S, Sp, (int)H, hb);                  \
+    return cudaGetLastError();
+    H3Q_PAIRS(0) H3Q_PAIRS(32) H3Q_PAIRS(64) H3Q_PAIRS(96) H3Q_PAIRS(128)
+#undef H3Q_PAIRS
+    default: break;
+  }
   const size_t smem = (size_t)(threads / 32) * kRowsPerWarp * 128 * sizeof(float);
   auto kern = block128 ? qk_rope_quant_kernel<true> : qk_rope_quant_kernel<false>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -347,7 +347,8 @@ h3q_status h3q_qk_norm_rope(const uint16_t* x, int64_t row_stride, int64_t col_o
  * qk_norm_rope(qkv, k_col) (norm weights q_norm / k_norm when do_norm, rope table and rot as h3q_qk_norm_rope),
  * then attention_qkv(q, k, qkv, v_col) -> out bf16 [S, H, 128].  The normalised, rotated q and k never reach
  * memory: the rotation runs inside the K mean and the Q / K quantisation, and the result equals that sequence
- * bit for bit.  qkv bf16 [S, qkv_width], 8-byte aligned, width and q / k columns multiples of 4; rot % 8 == 0
+ * bit for bit.  qkv bf16 [S, qkv_width], 16-byte aligned, width and q / k columns multiples of 8; norm weights
+ * 16-byte aligned; rot % 8 == 0
  * (other rot: H3Q_ERR_UNSUPPORTED).  Workspace: h3q_attention_workspace_size(S, H, flags). */
 h3q_status h3q_attend_qkv(const uint16_t* qkv, int64_t qkv_width, int64_t q_col, int64_t k_col, int64_t v_col,
                           const uint16_t* q_norm, const uint16_t* k_norm, int do_norm, float eps, const float* rope,

@@ -21,9 +21,11 @@ EPS = 1e-6
 TOL = 1e-2
 
 # (S, H, D, rot, norm weight, head stride factor): the DiT's q / k (D 128, rot 96), a full rotation, no rotation,
-# D not a multiple of 32, the widest head, a VAE-like interleaved layout (head stride 3 D, rot 48)
+# D not a multiple of 32, the widest head, a VAE-like interleaved layout (head stride 3 D, rot 48); at D 128 every
+# rot % 32 == 0 runs the pair layout, other rot % 8 == 0 the slice layout
 CASES = [(300, 40, 128, 96, True, 1), (200, 2, 128, 128, False, 1), (1000, 24, 128, 0, True, 1),
-         (33, 3, 80, 48, True, 1), (50, 4, 256, 128, True, 1), (77, 6, 64, 48, True, 3), (1, 1, 32, 32, False, 1)]
+         (33, 3, 80, 48, True, 1), (50, 4, 256, 128, True, 1), (77, 6, 64, 48, True, 3), (1, 1, 32, 32, False, 1),
+         (150, 5, 128, 64, True, 1), (90, 3, 128, 32, True, 3), (120, 4, 128, 48, True, 1), (64, 2, 128, 8, False, 1)]
 
 
 def _case(S, H, D, rot, use_w, hsf, seed):
@@ -77,7 +79,8 @@ def test_qk_norm_rope_reference_known_answer(cuda):
 
 @pytest.mark.parametrize("flags", [0, 1, 2, 3])
 @pytest.mark.parametrize("S,H,rot,norm", [(300, 4, 96, True), (1000, 3, 128, True), (2053, 2, 96, False),
-                                          (129, 2, 0, True), (4000, 1, 48, True)])
+                                          (129, 2, 0, True), (4000, 1, 48, True), (500, 2, 64, True),
+                                          (257, 3, 32, True), (1100, 9, 96, True)])
 def test_attend_qkv_equals_unfused(cuda, S, H, rot, norm, flags):
     """The fused front end gives the bits of qk_norm_rope -> attention_qkv (dit.rs:748-750)."""
     qkv, qw, kw, cs = O.make_rope_inputs(S + H, S, H, 128, max(rot, 8))
@@ -131,6 +134,8 @@ def test_attend_qkv_rejects_unsupported(cuda):
         h3q.attend_qkv(qkv, H, None, EPS, cs, 10)  # rot % 8 != 0
     with pytest.raises(h3q.H3QError):
         h3q.attend_qkv(qkv, H, None, EPS, None, 0, flags=8)
+    with pytest.raises(h3q.H3QError, match="multiples of 8"):
+        h3q.attend_qkv(torch.zeros((S, 3 * 128 + 4), dtype=torch.bfloat16, device=cuda), H, None, EPS, None, 0)
     x = torch.zeros((S, 600), dtype=torch.bfloat16, device=cuda)
     with pytest.raises(h3q.H3QError):
         h3q.qk_norm_rope(x, 0, 1, 300)  # head_dim > 256
