@@ -595,31 +595,29 @@ __global__ void __launch_bounds__(BLOCK ? 512 : 256, BLOCK ? 2 : 3) qk_rope_quan
   }
 }
 
-// Pair layout (D = 128, rot % 32 == 0): thread t of a row's four holds the rotation pairs (j, j + half) for
-// j in [tQ, tQ + Q), Q = half / 4, and the unrotated dims [rot + tN, rot + tN + N), N = (128 - rot) / 4: 32 values,
-// each cos / sin entry read once and both elements of a pair in the same thread, so no exchange.  The sum of
-// squares still comes from the thread's 32-dim slice (the reference's order); that load brings the row into L1
-// for the pair-layout load after it.
+// Pair layout (D = 128, rot % 32 == 0): thread t of a row's four holds the rotation pairs (j, j + half) for j in
+// the 4-pair chunks t, t + 4, t + 8, ... of [0, half) (Q = half / 4 pairs in all) and the unrotated dims in the same
+// interleave over [rot, 128) (N = (128 - rot) / 4 of them): 32 values, each cos / sin entry read once, both
+// elements of a pair in the same thread, and every load and store contiguous over the row's four threads.  The
+// sum of squares still comes from the thread's 32-dim slice (the reference's order); that load brings the row
+// into L1 for the pair-layout loads after it.
 template <int ROT>
 struct Pairs {
   static constexpr int HALF = ROT / 2, Q = HALF / 4, N = (128 - ROT) / 4;
   static_assert(ROT % 32 == 0 && ROT <= 128, "pair layout: rot % 32 == 0");
-  // dim of value i (0..31) of thread t
-  __device__ static int dim(int t, int i) { return i < Q ? t * Q + i : (i < 2 * Q ? HALF + t * Q + (i - Q) : ROT + t * N + (i - 2 * Q)); }
-  __device__ static int seg_base(int t, int sgm) { return sgm == 0 ? t * Q : (sgm == 1 ? HALF + t * Q : ROT + t * N); }
+  // first dim of chunk c (4 values) of segment sg (0: low pair halves, 1: high halves, 2: unrotated) of thread t
+  __device__ static int dim(int t, int sg, int c) { return (sg == 0 ? 0 : (sg == 1 ? HALF : ROT)) + 16 * c + 4 * t; }
+  __device__ static constexpr int count(int sg) { return sg < 2 ? Q : N; }
+  __device__ static constexpr int first(int sg) { return sg == 0 ? 0 : (sg == 1 ? Q : 2 * Q); }  // index in v[]
 };
 
-// n bf16 values (n % 4 == 0, 8-byte aligned) -> f32
-template <int n>
-__device__ __forceinline__ void load_seg(const uint16_t* __restrict__ p, float* v) {
-#pragma unroll
-  for (int c = 0; c < n / 4; ++c) {
-    const uint2 u = __ldg(reinterpret_cast<const uint2*>(p) + c);
-    v[4 * c] = lo16(u.x);
-    v[4 * c + 1] = hi16(u.x);
-    v[4 * c + 2] = lo16(u.y);
-    v[4 * c + 3] = hi16(u.y);
-  }
+// 4 bf16 values (8-byte aligned) -> f32
+__device__ __forceinline__ void load4(const uint16_t* __restrict__ p, float* v) {
+  const uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+  v[0] = lo16(u.x);
+  v[1] = hi16(u.x);
+  v[2] = lo16(u.y);
+  v[3] = hi16(u.y);
 }
 
 template <int ROT>
@@ -627,7 +625,7 @@ __device__ __forceinline__ void pair_norm_rope(const uint16_t* __restrict__ xr, 
                                                int do_norm, float eps, const float* __restrict__ cs, int64_t s,
                                                int64_t S, uint32_t (&res)[16]) {
   using L = Pairs<ROT>;
-  constexpr int Q = L::Q, N = L::N, HALF = L::HALF;
+  constexpr int Q = L::Q, HALF = L::HALF;
   float inv = 1.f;
   if (do_norm) {
     uint32_t raw[16];
@@ -647,19 +645,17 @@ __device__ __forceinline__ void pair_norm_rope(const uint16_t* __restrict__ xr, 
     inv = rsqrtf(__fadd_rn(__fdiv_rn(tt, 128.f), eps));
   }
   float v[32];
-  if (Q > 0) {
-    load_seg<Q>(xr + t * Q, v);
-    load_seg<Q>(xr + HALF + t * Q, v + Q);
-  }
-  if (N > 0) load_seg<N>(xr + ROT + t * N, v + 2 * Q);
+#pragma unroll
+  for (int sg = 0; sg < 3; ++sg)
+#pragma unroll
+    for (int c = 0; c < L::count(sg) / 4; ++c) load4(xr + L::dim(t, sg, c), v + L::first(sg) + 4 * c);
   if (do_norm) {
     float wv[32];
     if (w) {
-      if (Q > 0) {
-        load_seg<Q>(w + t * Q, wv);
-        load_seg<Q>(w + HALF + t * Q, wv + Q);
-      }
-      if (N > 0) load_seg<N>(w + ROT + t * N, wv + 2 * Q);
+#pragma unroll
+      for (int sg = 0; sg < 3; ++sg)
+#pragma unroll
+        for (int c = 0; c < L::count(sg) / 4; ++c) load4(w + L::dim(t, sg, c), wv + L::first(sg) + 4 * c);
     } else {
 #pragma unroll
       for (int i = 0; i < 32; ++i) wv[i] = 1.f;
@@ -668,11 +664,10 @@ __device__ __forceinline__ void pair_norm_rope(const uint16_t* __restrict__ xr, 
     for (int i = 0; i < 32; ++i) v[i] = __fmul_rn(__fmul_rn(v[i], inv), wv[i]);
   }
   if (Q > 0) {
-    const float4* c4 = reinterpret_cast<const float4*>(cs + s * HALF + t * Q);
-    const float4* s4 = reinterpret_cast<const float4*>(cs + (S + s) * HALF + t * Q);
 #pragma unroll
     for (int c = 0; c < Q / 4; ++c) {
-      const float4 cc = __ldg(c4 + c), ss = __ldg(s4 + c);
+      const float4 cc = __ldg(reinterpret_cast<const float4*>(cs + s * HALF + L::dim(t, 0, c)));
+      const float4 ss = __ldg(reinterpret_cast<const float4*>(cs + (S + s) * HALF + L::dim(t, 0, c)));
       const float cv[4] = {cc.x, cc.y, cc.z, cc.w}, sv[4] = {ss.x, ss.y, ss.z, ss.w};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -704,16 +699,13 @@ __global__ void __launch_bounds__(256) qk_norm_rope_pairs_kernel(const uint16_t*
     pair_norm_rope<ROT>(x + s * rs + col + (int64_t)h * hs, t, w, do_norm, eps, cs, s, S, res);
     if (valid) {
       uint16_t* o = out + (s * H + h) * HD;
-      // segments of Q, Q and N values: 4 bf16 (one uint2) per store
-      int idx = 0;
 #pragma unroll
-      for (int sg = 0; sg < 3; ++sg) {
-        const int n = sg < 2 ? L::Q : L::N;
-        uint2* d = reinterpret_cast<uint2*>(o + L::seg_base(t, sg));
+      for (int sg = 0; sg < 3; ++sg)
 #pragma unroll
-        for (int c = 0; c < n / 4; ++c) d[c] = make_uint2(res[idx / 2 + 2 * c], res[idx / 2 + 2 * c + 1]);
-        idx += n;
-      }
+        for (int c = 0; c < L::count(sg) / 4; ++c) {
+          const int i = (L::first(sg) + 4 * c) / 2;
+          *reinterpret_cast<uint2*>(o + L::dim(t, sg, c)) = make_uint2(res[i], res[i + 1]);
+        }
     }
   }
 }
@@ -740,18 +732,14 @@ __global__ void __launch_bounds__(256) kmean_rope_pairs_kernel(const uint16_t* _
     if (s >= r1) s = r1 - 1;  // a real row whose values are not added
     uint32_t res[16];
     pair_norm_rope<ROT>(x + s * rs + col + (int64_t)h * HD, t, w, do_norm, eps, cs, s, S, res);
-    int idx = 0;
 #pragma unroll
-    for (int sg = 0; sg < 3; ++sg) {
-      const int n = sg < 2 ? L::Q : L::N;
-      float4* d = reinterpret_cast<float4*>(b + r * RS + L::seg_base(t, sg));
+    for (int sg = 0; sg < 3; ++sg)
 #pragma unroll
-      for (int c = 0; c < n / 4; ++c) {
-        const uint32_t p0 = res[idx / 2 + 2 * c], p1 = res[idx / 2 + 2 * c + 1];
-        d[c] = make_float4(lo16(p0), hi16(p0), lo16(p1), hi16(p1));
+      for (int c = 0; c < L::count(sg) / 4; ++c) {
+        const int i = (L::first(sg) + 4 * c) / 2;
+        *reinterpret_cast<float4*>(b + r * RS + L::dim(t, sg, c)) =
+            make_float4(lo16(res[i]), hi16(res[i]), lo16(res[i + 1]), hi16(res[i + 1]));
       }
-      idx += n;
-    }
     __syncwarp();
     const int nr = (int)(r1 - g < kRowsPerWarp ? r1 - g : kRowsPerWarp);
     for (int rr = 0; rr < nr; ++rr) {
@@ -790,23 +778,18 @@ __global__ void __launch_bounds__(BLOCK ? 512 : 256) qk_rope_quant_pairs_kernel(
       v[2 * i] = lo16(res[i]);
       v[2 * i + 1] = hi16(res[i]);
     }
-    {
-      int idx = 0;
 #pragma unroll
-      for (int sg = 0; sg < 3; ++sg) {
-        const int n = sg < 2 ? L::Q : L::N;
-        const float4* mp = reinterpret_cast<const float4*>(mean + (int64_t)h * HD + L::seg_base(t, sg));
+    for (int sg = 0; sg < 3; ++sg)
 #pragma unroll
-        for (int c = 0; c < n / 4; ++c) {
-          const float4 m4 = mean ? __ldg(mp + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-          v[idx + 4 * c] = __fsub_rn(v[idx + 4 * c], m4.x);
-          v[idx + 4 * c + 1] = __fsub_rn(v[idx + 4 * c + 1], m4.y);
-          v[idx + 4 * c + 2] = __fsub_rn(v[idx + 4 * c + 2], m4.z);
-          v[idx + 4 * c + 3] = __fsub_rn(v[idx + 4 * c + 3], m4.w);
-        }
-        idx += n;
+      for (int c = 0; c < L::count(sg) / 4; ++c) {
+        const int i = L::first(sg) + 4 * c;
+        const float4 m4 = mean ? __ldg(reinterpret_cast<const float4*>(mean + (int64_t)h * HD + L::dim(t, sg, c)))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+        v[i] = __fsub_rn(v[i], m4.x);
+        v[i + 1] = __fsub_rn(v[i + 1], m4.y);
+        v[i + 2] = __fsub_rn(v[i + 2], m4.z);
+        v[i + 3] = __fsub_rn(v[i + 3], m4.w);
       }
-    }
     float m = 0.f;
     if (valid) {
 #pragma unroll
@@ -828,17 +811,14 @@ __global__ void __launch_bounds__(BLOCK ? 512 : 256) qk_rope_quant_pairs_kernel(
     if (valid) {
       const float inv = __fdiv_rn(1.f, sc);
       int8_t* row = codes + ((int64_t)h * S + s) * HD;
-      int idx = 0;
 #pragma unroll
-      for (int sg = 0; sg < 3; ++sg) {
-        const int n = sg < 2 ? L::Q : L::N;
-        uint32_t* d = reinterpret_cast<uint32_t*>(row + L::seg_base(t, sg));
+      for (int sg = 0; sg < 3; ++sg)
 #pragma unroll
-        for (int c = 0; c < n / 4; ++c)
-          d[c] = q127(v[idx + 4 * c], inv) | (q127(v[idx + 4 * c + 1], inv) << 8) |
-                 (q127(v[idx + 4 * c + 2], inv) << 16) | (q127(v[idx + 4 * c + 3], inv) << 24);
-        idx += n;
-      }
+        for (int c = 0; c < L::count(sg) / 4; ++c) {
+          const int i = L::first(sg) + 4 * c;
+          *reinterpret_cast<uint32_t*>(row + L::dim(t, sg, c)) =
+              q127(v[i], inv) | (q127(v[i + 1], inv) << 8) | (q127(v[i + 2], inv) << 16) | (q127(v[i + 3], inv) << 24);
+        }
     }
     if (t == 0 && s < Sp) scales[(int64_t)h * Sp + s] = valid ? sc : 0.f;
   }
