@@ -683,7 +683,7 @@ __device__ __forceinline__ void pair_norm_rope(const uint16_t* __restrict__ xr, 
 
 // Standalone qk_norm_rope, pair layout: CTA of 8 warps = 64 tokens looping over `hb` heads.
 template <int ROT>
-__global__ void __launch_bounds__(256) qk_norm_rope_pairs_kernel(const uint16_t* __restrict__ x, int64_t rs,
+__global__ void __launch_bounds__(256, 3) qk_norm_rope_pairs_kernel(const uint16_t* __restrict__ x, int64_t rs,
                                                                  int64_t col, int64_t hs,
                                                                  const uint16_t* __restrict__ w, int do_norm,
                                                                  float eps, const float* __restrict__ cs,
@@ -712,7 +712,7 @@ __global__ void __launch_bounds__(256) qk_norm_rope_pairs_kernel(const uint16_t*
 
 // K column sums, pair layout: as kmean_rope_partial_kernel, the rows turned through a padded row buffer.
 template <int ROT>
-__global__ void __launch_bounds__(256) kmean_rope_pairs_kernel(const uint16_t* __restrict__ x, int64_t rs,
+__global__ void __launch_bounds__(256, 3) kmean_rope_pairs_kernel(const uint16_t* __restrict__ x, int64_t rs,
                                                                int64_t col, const uint16_t* __restrict__ w,
                                                                int do_norm, float eps, const float* __restrict__ cs,
                                                                float* __restrict__ part, int64_t S, int H,
@@ -757,7 +757,7 @@ __global__ void __launch_bounds__(256) kmean_rope_pairs_kernel(const uint16_t* _
 
 // Normalise + rotate + (K: subtract the column mean) + quantise, pair layout; CTA as qk_rope_quant_kernel.
 template <int ROT, bool BLOCK>
-__global__ void __launch_bounds__(BLOCK ? 512 : 256) qk_rope_quant_pairs_kernel(
+__global__ void __launch_bounds__(BLOCK ? 512 : 256, BLOCK ? 1 : 3) qk_rope_quant_pairs_kernel(
     const uint16_t* __restrict__ x, int64_t rs, int64_t col, const uint16_t* __restrict__ w, int do_norm, float eps,
     const float* __restrict__ cs, const float* __restrict__ mean, int8_t* __restrict__ codes,
     float* __restrict__ scales, int64_t S, int64_t Sp, int H, int hb) {
