@@ -130,6 +130,21 @@ int h3q_available_arch(int device) {
 
 int h3q_can_fuse_rotation(size_t k, size_t group) { return group == 256 && k % 256 == 0 && k / 256 <= 64; }
 
+h3q_status h3q_init(int device) {
+  const char* what = "h3q_init";
+  if (!h3q_available_arch(device)) return fail(H3Q_ERR_UNSUPPORTED, "%s: device %d is not an sm_100 GPU", what, device);
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess) return fail(H3Q_ERR_CUDA, "%s: no device", what);
+  if (cudaSetDevice(device) != cudaSuccess) return fail(H3Q_ERR_ARG, "%s: bad device %d", what, device);
+  // the per-device state the entry points otherwise create on their first call: the device error word (a 4-byte
+  // allocation) and the SM count the persistent kernels size their grids by
+  h3q_status st = H3Q_OK;
+  if (!h3q::error_word_current()) st = fail(H3Q_ERR_CUDA, "%s: could not set up the device error word", what);
+  h3q::sm_count(device);
+  cudaSetDevice(prev);
+  return st;
+}
+
 h3q_status h3q_device_status(int device, int* code) {
   if (code) *code = 0;
   int prev = 0;

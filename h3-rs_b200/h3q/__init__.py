@@ -63,6 +63,7 @@ SIGNATURES = {
     "h3q_checkpoint_qlinear": (_int, [_vp, ctypes.c_char_p, _vp]),
     "h3q_version": (ctypes.c_char_p, []),
     "h3q_available_arch": (_int, [_int]),
+    "h3q_init": (_int, [_int]),
     "h3q_can_fuse_rotation": (_int, [_sz, _sz]),
     "h3q_device_status": (_int, [_int, ctypes.POINTER(_int)]),
     "h3q_quant_rows_i8": (_int, [_vp, _int, _vp, _vp, _i64, _i64, _int, _vp]),
@@ -159,6 +160,11 @@ def _cuda(*ts) -> None:
     for t in ts:
         if t is not None and (not t.is_cuda or not t.is_contiguous()):
             raise ValueError("h3q: expected contiguous CUDA tensors")
+
+
+def init(device: int = 0) -> None:
+    """h3q_init: the per-device set-up, done up front instead of on the first call."""
+    check(lib().h3q_init(device))
 
 
 def available_arch(device: int = 0) -> bool:

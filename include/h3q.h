@@ -52,6 +52,12 @@ const char* h3q_version(void);
 /* attn8::available_arch (attn8.rs:584-589): 1 when `device` can run these kernels (sm_100), else 0. */
 int h3q_available_arch(int device);
 
+/* Per-device set-up, once per device and optional: creates the state the entry points otherwise create on their
+ * first call on a device (the device error word, a 4-byte allocation, and the SM count), so that the first call
+ * of an entry point does not allocate it.  H3Q_ERR_UNSUPPORTED on a device that is not an sm_100 GPU.  Safe to
+ * call again. */
+h3q_status h3q_init(int device);
+
 /* kernels::can_fuse_rotation (kernels.rs:1081-1085): whether the rotation fuses into the quantizer for an
  * input width k and ConvRot group size.  Always on here (group 256, k % 256 == 0, k / 256 <= 64); the
  * reference gates it behind H3_FUSED_ROT=1 because its butterfly was slow on RTX 4090. */

@@ -88,3 +88,10 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(h3q, "_LIB", None)
     with pytest.raises(RuntimeError, match="not built"):
         h3q.lib()
+
+
+def test_init_rejects_a_missing_or_unsupported_device():
+    """h3q_init on a device index that is no sm_100 GPU (every index on a CPU-only host) fails cleanly."""
+    import h3q
+    assert h3q.lib().h3q_init(4096) == h3q.ERR_UNSUPPORTED
+    assert "not an sm_100 GPU" in h3q.last_error()
