@@ -7,7 +7,8 @@ The reference runs on a single GPU; partitioning follows the data:
   every rank when a caller needs one.
 * N-split linear: rank r holds the weight rows (output columns) nsplit_range(N, world, r) and the full activation;
   NSplitLinear writes each rank's column block into every rank's output inside the GEMM (peer memory over
-  NVLink, h3q_gemm_s8_allgather), or, as the comparison path, computes locally and all-gathers through NCCL.
+  NVLink, h3q_gemm_s8_allgather), or computes locally and all-gathers through NCCL; by default the faster of the
+  two for the number of ranks.
 * Query-sharded attention: rank r owns query rows row_range(S, world, r); K and V rows are gathered from all ranks
   and each rank attends its queries against every key (h3q_attention_rows).  Its rows equal the single-GPU
   result's (per-token scales).
@@ -134,9 +135,14 @@ class NSplitLinear:
 
     fused=True: one kernel per rank computes its columns and writes them into every rank's output buffer over
     NVLink; a one-element all-reduce after it is the barrier that makes the output complete.  fused=False: local
-    GEMM, then gather_columns (NCCL all-gather + relayout)."""
+    GEMM, then gather_columns (NCCL all-gather + relayout).  fused=None (the default) picks the faster one as
+    measured on B200 for the DiT linears: the fused kernel up to FUSED_MAX_RANKS ranks (2 GPUs: 4.6 ms against
+    8.8 ms for the four c1 linears), NCCL beyond (8 GPUs: 10.2 ms against 27.1 ms, where every output box becomes
+    seven small remote stores)."""
 
-    def __init__(self, w, ws, bias, group=None, fused: bool = True, rotate: bool = True):
+    FUSED_MAX_RANKS = 2
+
+    def __init__(self, w, ws, bias, group=None, fused: bool | None = None, rotate: bool = True):
         import torch
         dist = _dist()
         self.group = group
@@ -147,7 +153,7 @@ class NSplitLinear:
         ws = ws.to(torch.float32).reshape(-1)
         self.ws = (ws[self.n0:self.n1] if ws.numel() == self.n and self.n > 1 else ws[:1]).contiguous()
         self.bias = None if bias is None else bias.to(torch.float32)[self.n0:self.n1].contiguous()
-        self.fused = fused
+        self.fused = (self.world <= self.FUSED_MAX_RANKS) if fused is None else bool(fused)
         self.rotate = rotate
         self.bufs = None
         self._flag = None
