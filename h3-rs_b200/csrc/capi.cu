@@ -287,6 +287,25 @@ h3q_status h3q_gate_add(const void* x, const void* y, int kind, const float* gat
   return cuda_status(launch_gate_add(x, y, kind, gate, idx, out, s, c, (cudaStream_t)stream), what);
 }
 
+h3q_status h3q_rotate_activation(const uint16_t* x, uint16_t* y, int64_t m, int64_t k, void* stream) {
+  const char* what = "h3q_rotate_activation";
+  if (m < 0 || k < 0) return fail(H3Q_ERR_ARG, "%s: negative shape", what);
+  if (k % 256 != 0) return fail(H3Q_ERR_ARG, "ConvRot group 256 does not divide [%lld, %lld]", (long long)m, (long long)k);
+  if (k / 256 > 64) return fail(H3Q_ERR_UNSUPPORTED, "%s: this build rotates rows of up to 16384 columns", what);
+  if (m == 0 || k == 0) return H3Q_OK;
+  if (!x || !y) return fail(H3Q_ERR_ARG, "%s: null pointer", what);
+  if (!aligned16(x) || !aligned16(y)) return fail(H3Q_ERR_ARG, "%s: x and y must be 16-byte aligned", what);
+  return cuda_status(launch_rotate_bf16(x, y, m, k, error_word(), (cudaStream_t)stream), what);
+}
+
+h3q_status h3q_swiglu(const void* y, void* out, int kind, int64_t rows, int64_t f, int interleaved, void* stream) {
+  const char* what = "h3q_swiglu";
+  if (h3q_status st = check_kind(kind, what)) return st;
+  if (rows < 0 || f < 0) return fail(H3Q_ERR_ARG, "%s: negative shape", what);
+  if (rows * f == 0) return H3Q_OK;
+  if (!y || !out) return fail(H3Q_ERR_ARG, "%s: null pointer", what);
+  return cuda_status(launch_swiglu(y, out, kind, rows, f, interleaved ? 1 : 0, (cudaStream_t)stream), what);
+}
 
 static h3q_status rms_modulate_checks(const uint16_t* x, const uint16_t* w, const float* scale, const float* shift,
                                       const uint32_t* idx, const void* out, int64_t S, int64_t C, const char* what) {

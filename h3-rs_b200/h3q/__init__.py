@@ -64,6 +64,8 @@ SIGNATURES = {
     "h3q_version": (ctypes.c_char_p, []),
     "h3q_available_arch": (_int, [_int]),
     "h3q_init": (_int, [_int]),
+    "h3q_rotate_activation": (_int, [_vp, _vp, _i64, _i64, _vp]),
+    "h3q_swiglu": (_int, [_vp, _vp, _int, _i64, _i64, _int, _vp]),
     "h3q_can_fuse_rotation": (_int, [_sz, _sz]),
     "h3q_device_status": (_int, [_int, ctypes.POINTER(_int)]),
     "h3q_quant_rows_i8": (_int, [_vp, _int, _vp, _vp, _i64, _i64, _int, _vp]),
@@ -160,6 +162,25 @@ def _cuda(*ts) -> None:
     for t in ts:
         if t is not None and (not t.is_cuda or not t.is_contiguous()):
             raise ValueError("h3q: expected contiguous CUDA tensors")
+
+
+def rotate_activation(x):
+    """weights::rotate_activation(x, 256) for bf16 x [M, K]: bf16 [M, K]."""
+    import torch
+    _cuda(x)
+    y = torch.empty_like(x)
+    check(lib().h3q_rotate_activation(_p(x), _p(y), x.shape[0], x.shape[1], _stream(x.device)))
+    return y
+
+
+def swiglu(y, interleaved: bool = True):
+    """swiglu_interleaved / ops::swiglu on y [rows, 2F] (f32, f16 or bf16): [rows, F]."""
+    import torch
+    _cuda(y)
+    rows, n = y.shape
+    out = torch.empty((rows, n // 2), dtype=y.dtype, device=y.device)
+    check(lib().h3q_swiglu(_p(y), _p(out), _kind(y.dtype), rows, n // 2, int(interleaved), _stream(y.device)))
+    return out
 
 
 def init(device: int = 0) -> None:

@@ -144,6 +144,17 @@ h3q_status h3q_dequant_nvfp4(const uint8_t* q, const uint8_t* block_scale, const
 h3q_status h3q_gate_add(const void* x, const void* y, int kind, const float* gate, const uint32_t* idx, void* out,
                         int64_t s, int64_t c, void* stream);
 
+/* rotate_activation(x, 256) (weights.rs:482-489) for bf16 rows: y = x . H256 per 256-column group (H256 the
+ * normalised regular Hadamard of weights.rs:441-465), formed by the quantizer's f32 butterfly in its rot2 order and
+ * rounded to bf16 once.  The reference multiplies by H in bf16 through cuBLAS, whose rounding no reference test
+ * pins.  x, y bf16 [m, k]; k % 256 == 0, k <= 16384. */
+h3q_status h3q_rotate_activation(const uint16_t* x, uint16_t* y, int64_t m, int64_t k, void* stream);
+
+/* swiglu_interleaved (weights.rs:806-816; interleaved = 1: gate and up in adjacent columns) and ops::swiglu
+ * (ops.rs:39-44; interleaved = 0: gate = columns [0, f), up = [f, 2f)): out [rows, f] = silu(gate) * up with the
+ * bf16 re-roundings of the reference's epilogue, y [rows, 2f] and out of kind `kind` (0 f32, 1 f16, 2 bf16). */
+h3q_status h3q_swiglu(const void* y, void* out, int kind, int64_t rows, int64_t f, int interleaved, void* stream);
+
 /* Workspace bytes h3q_nvfp4_linear needs (the AWQ-scaled activations and, for narrow outputs, split-K partials). */
 size_t h3q_nvfp4_linear_workspace_size(int64_t m, int64_t n, int64_t k, int has_pre_quant_scale);
 
