@@ -387,6 +387,34 @@ def modulate_fused(dev, peaks: dict, reps: int = 10, M: int = 32760, C: int = 51
     return res
 
 
+def lora_merge(dev, reps: int = 3, n: int = 15360, k: int = 5120, rank: int = 64) -> dict:
+    """Load-time LoRA merge (QLinear::merge_loras, weights.rs:716-757) of the c1 qkv layer: dequantize, undo ConvRot,
+    add one rank-64 bf16 delta, rotate, requantize per row (h3q_lora_merge_i8).  Work counted: the delta's
+    2 n k r flops and the int8 weight read and written."""
+    import torch
+    import h3q
+    g = torch.Generator(device=dev).manual_seed(13)
+    w = torch.randint(-127, 128, (n, k), generator=g, device=dev, dtype=torch.int8)
+    s = torch.rand(n, generator=g, device=dev) * 1e-2 + 1e-3
+    a = (0.05 * torch.randn((rank, k), generator=g, device=dev)).to(torch.bfloat16)
+    b = (0.05 * torch.randn((n, rank), generator=g, device=dev)).to(torch.bfloat16)
+    loras = [(a, b, 0.5)]
+    out = torch.empty_like(w)
+    out_s = torch.empty(n, dtype=torch.float32, device=dev)
+    for _ in range(2):
+        h3q.lora_merge_i8(w, s, loras, out=out, out_scale=out_s)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        h3q.lora_merge_i8(w, s, loras, out=out, out_scale=out_s)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    return {"workload": f"int8 ConvRot layer [{n}, {k}] + one rank-{rank} bf16 delta", "ms": round(ms, 3),
+            "delta_tflops": round(2.0 * n * k * rank / (ms * 1e-3) / 1e12, 1),
+            "note": "includes the workspace allocation of each call; f32 FMA chains on the CUDA cores"}
+
+
 def _max_over_ranks(ms: float, dist, dev) -> float:
     import torch
     t = torch.tensor([ms], device=dev, dtype=torch.float64)
@@ -690,6 +718,7 @@ def main() -> None:
     nv = nvfp4_c3(dev, load_peaks()) if rank == 0 else None
     att = attention_c4(dev, load_peaks()) if rank == 0 else None
     modq = modulate_fused(dev, load_peaks()) if rank == 0 else None
+    lmerge = lora_merge(dev) if rank == 0 else None
     attend = attend_step_c4(dev) if rank == 0 else None
     stream_c1 = streaming_c1(layers, M, dev) if rank == 0 else None
 
@@ -722,6 +751,7 @@ def main() -> None:
         "nvfp4_c3": nv,
         "attention_c4": att,
         "modulate_quant": modq,
+        "lora_merge": lmerge,
         "attend_step_c4": attend,
         "weight_streaming_c1": stream_c1,
         "multi_gpu": extras,

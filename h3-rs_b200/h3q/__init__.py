@@ -32,6 +32,12 @@ class Switches(ctypes.Structure):
                 ("fused_rot_linear", ctypes.c_int)]
 
 
+class LoraDesc(ctypes.Structure):
+    """h3q_lora: one low-rank delta scale * (b @ a) (weights.rs LoraDelta)."""
+    _fields_ = [("a", ctypes.c_void_p), ("b", ctypes.c_void_p), ("rank", ctypes.c_int64), ("dtype", ctypes.c_int),
+                ("scale", ctypes.c_double)]
+
+
 FMT_DENSE, FMT_INT8, FMT_NVFP4 = 0, 1, 2
 ATTN_SCALE_TOKEN, ATTN_SCALE_BLOCK128, ATTN_PV_F16, ATTN_PV_BF16 = 0, 1, 0, 2
 PATH_GEMM_S8, PATH_INT8_LINEAR, PATH_ROTATE_FUSED, PATH_ROTATE_SEPARATE, PATH_SWIGLU_FUSED, PATH_SWIGLU_AFTER = (
@@ -61,6 +67,10 @@ SIGNATURES = {
     "h3q_checkpoint_read": (_int, [_vp, ctypes.c_char_p, _vp, ctypes.c_uint64]),
     "h3q_checkpoint_upload": (_int, [_vp, ctypes.c_char_p, _vp, ctypes.c_uint64, _int, _vp]),
     "h3q_checkpoint_qlinear": (_int, [_vp, ctypes.c_char_p, _vp]),
+    "h3q_lora_merge_i8_workspace_size": (_sz, [_i64, _i64]),
+    "h3q_lora_merge_i8": (_int, [_vp, _vp, _i64, _int, ctypes.POINTER(LoraDesc), _int, _vp, _vp, _i64, _i64, _vp,
+                                 _sz, _vp]),
+    "h3q_lora_merge_dense": (_int, [_vp, _int, ctypes.POINTER(LoraDesc), _int, _vp, _i64, _i64, _vp]),
     "h3q_version": (ctypes.c_char_p, []),
     "h3q_available_arch": (_int, [_int]),
     "h3q_init": (_int, [_int]),
@@ -544,6 +554,58 @@ class HostPipeline:
         return out
 
 
+def _lora_descs(loras, n: int, k: int, device):
+    """(a [r, k], b [n, r], scale) device tensors -> an h3q_lora array (and the tensors it points into)."""
+    import torch
+    descs = (LoraDesc * max(len(loras), 1))()
+    keep = []
+    for i, (a, b, scale) in enumerate(loras):
+        a, b = a.contiguous(), b.contiguous()
+        if a.dim() != 2 or b.dim() != 2 or a.shape[1] != k or b.shape[0] != n or b.shape[1] != a.shape[0]:
+            raise ValueError(f"LoRA {i}: a {tuple(a.shape)} and b {tuple(b.shape)} do not fit a [{n}, {k}] weight")
+        if a.dtype != b.dtype or a.dtype not in (torch.float32, torch.float16, torch.bfloat16):
+            raise ValueError(f"LoRA {i}: factors must share one of f32 / f16 / bf16")
+        if a.device != torch.device(device) or b.device != torch.device(device):
+            raise ValueError(f"LoRA {i}: factors must be on {device}")
+        keep += [a, b]
+        descs[i] = LoraDesc(a.data_ptr(), b.data_ptr(), a.shape[0], _kind(a.dtype), float(scale))
+    return descs, keep
+
+
+def lora_merge_i8(w, scale, loras, convrot: int = 256, out=None, out_scale=None):
+    """QLinear::merge_loras for an int8 layer (weights.rs:716-757): returns (w' int8 [n, k], s' f32 [n]).  loras is
+    a sequence of (a [r, k], b [n, r], scale) with scale = alpha / rank * strength.  With no LoRA the inputs come
+    back unchanged (the reference's early return)."""
+    import torch
+    _cuda(w, scale)
+    n, k = w.shape
+    if not loras:
+        return w, scale
+    descs, keep = _lora_descs(loras, n, k, w.device)
+    scale = scale.to(torch.float32).reshape(-1).contiguous()
+    out = torch.empty_like(w) if out is None else out
+    out_scale = torch.empty(n, dtype=torch.float32, device=w.device) if out_scale is None else out_scale
+    ws = torch.empty(max(lib().h3q_lora_merge_i8_workspace_size(n, k), 1), dtype=torch.uint8, device=w.device)
+    check(lib().h3q_lora_merge_i8(_p(w), _p(scale), scale.numel(), convrot, descs, len(loras), _p(out),
+                                  _p(out_scale), n, k, _p(ws), ws.numel(), _stream(w.device)))
+    del keep
+    return out, out_scale
+
+
+def lora_merge_dense(w, loras, out=None):
+    """QLinear::merge_loras for a dense layer (weights.rs:710-715): dtype(f32(w) + sum of the deltas)."""
+    import torch
+    _cuda(w)
+    n, k = w.shape
+    if not loras:
+        return w
+    descs, keep = _lora_descs(loras, n, k, w.device)
+    out = torch.empty_like(w) if out is None else out
+    check(lib().h3q_lora_merge_dense(_p(w), _kind(w.dtype), descs, len(loras), _p(out), n, k, _stream(w.device)))
+    del keep
+    return out
+
+
 def default_switches() -> Switches:
     return lib().h3q_default_switches()
 
@@ -584,3 +646,14 @@ class QLinear:
 
     def run_swiglu(self, x, switches: Switches | None = None):
         return self.forward(x, swiglu=True, switches=switches)
+
+    def merge_loras(self, loras) -> None:
+        """QLinear::merge_loras (weights.rs:692-761): fold (a, b, scale) deltas into the int8 weight and per-row
+        scales.  Interleaved (SwiGLU-paired) layers are left alone, as in the reference: merge before
+        interleaving."""
+        if not loras or self.desc.interleaved:
+            return
+        self.weight, self.scale = lora_merge_i8(self.weight, self.scale, loras, convrot=self.desc.convrot)
+        self.desc.weight = self.weight.data_ptr()
+        self.desc.scale = self.scale.data_ptr()
+        self.desc.scale_numel = self.scale.numel()

@@ -14,6 +14,7 @@ import json
 import numpy as np
 
 from . import FMT_DENSE, FMT_INT8, FMT_NVFP4, H3QError, QLinear, _stream, check, lib
+from . import lora_merge_dense as _lora_merge_dense
 from . import nvfp4_linear as _nvfp4_linear
 
 DT_F32, DT_F16, DT_BF16, DT_I8, DT_U8, DT_F8_E4M3, DT_BOOL, DT_I32, DT_I64, DT_F64 = range(10)
@@ -162,6 +163,11 @@ class DenseLinear:
         y = x @ self.weight.to(x.dtype).t()
         return y if self.bias is None else y + self.bias.to(x.dtype)
 
+    def merge_loras(self, loras) -> None:
+        """QLinear::merge_loras for a dense layer (weights.rs:710-715), through h3q_lora_merge_dense."""
+        if loras:
+            self.weight = _lora_merge_dense(self.weight.contiguous(), loras)
+
 
 def load_qlinear(f: SafeFile, prefix: str, device, compute_dtype=None, interleave_swiglu: bool = False):
     """QLinear::load (weights.rs:493-534) for the layer at `prefix`.  interleave_swiglu applies
@@ -197,4 +203,82 @@ def load_qlinear(f: SafeFile, prefix: str, device, compute_dtype=None, interleav
     raise H3QError(1, f"{prefix}: unknown format {spec.format}")
 
 
-__all__ = ["SafeFile", "QLinearSpec", "Nvfp4Linear", "DenseLinear", "load_qlinear", "interleave_rows", "DTYPE_NAMES"]
+class LoraDelta:
+    """One layer's low-rank pair (lora.rs:15-23): a [r, in] and b [out, r] as bf16 on the device, scale =
+    alpha / rank (1 without an alpha), and the optional `reshape_weight` target shape."""
+
+    def __init__(self, a, b, scale: float, reshape=None):
+        self.a, self.b, self.scale, self.reshape = a, b, scale, reshape
+
+
+class LoraFile:
+    """A ComfyUI-style LoRA file for the DiT (lora.rs:11-72): `<module>.lora_B/lora_A.weight` or
+    `<module>.lora_up/lora_down.weight`, optional `<module>.alpha` and `<module>.reshape_weight`, all under a
+    "diffusion_model." prefix when any name carries it."""
+
+    def __init__(self, path: str):
+        self.file = SafeFile(path)
+        self.prefix = "diffusion_model." if any(k.startswith("diffusion_model.") for k in self.file.names()) else ""
+
+    def close(self) -> None:
+        self.file.close()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def metadata(self, key: str) -> str | None:
+        return self.file.metadata(key)
+
+    def delta(self, module: str, device) -> LoraDelta | None:
+        """Lora::delta (lora.rs:42-71): the pair for `module` (a layer name without ".weight"), or None.  The
+        factors are loaded as bf16 (lora.rs:51-53) and flattened from dimension 1."""
+        import torch
+        p = self.prefix + module
+        if self.file.has(f"{p}.lora_B.weight"):
+            up, down = f"{p}.lora_B.weight", f"{p}.lora_A.weight"
+        elif self.file.has(f"{p}.lora_up.weight"):
+            up, down = f"{p}.lora_up.weight", f"{p}.lora_down.weight"
+        else:
+            return None
+        b = self.file.load(up, device).to(torch.bfloat16)
+        a = self.file.load(down, device).to(torch.bfloat16)
+        a = a.reshape(a.shape[0], -1)
+        b = b.reshape(b.shape[0], -1)
+        rank = float(a.shape[0])
+        scale = 1.0
+        if self.file.has(f"{p}.alpha"):
+            alpha = self.file.load(f"{p}.alpha", "cpu").to(torch.float32).reshape(-1)[0]
+            scale = float(alpha) / rank
+        reshape = None
+        if self.file.has(f"{p}.reshape_weight"):
+            reshape = [int(v) for v in self.file.read(f"{p}.reshape_weight").astype(np.int64).reshape(-1)]
+        return LoraDelta(a, b, scale, reshape)
+
+
+def apply_lora(layers: dict, lora: LoraFile, strength: float, device):
+    """The DiT's apply_lora + merge (dit.rs:654-690, :599-611) over `layers` (module name -> layer): each layer
+    with a matching pair of the right shape gets scale * strength * (b @ a) folded into its weight.  Returns
+    (merged, skipped) module names: a pair whose shapes do not match the layer or that carries reshape_weight is
+    skipped, as the reference does; NVFP4 layers are skipped too (the reference keeps its LoRAs on a runtime path,
+    weights.rs:708, that this library does not serve)."""
+    merged, skipped = [], []
+    for name, layer in layers.items():
+        d = lora.delta(name, device)
+        if d is None:
+            continue
+        out_f = layer.desc.out_features if isinstance(layer, QLinear) else layer.out_features
+        in_f = layer.desc.in_features if isinstance(layer, QLinear) else layer.in_features
+        if (d.a.shape[1] != in_f or d.b.shape[0] != out_f or d.reshape is not None
+                or isinstance(layer, Nvfp4Linear)):
+            skipped.append(name)
+            continue
+        layer.merge_loras([(d.a, d.b, d.scale * strength)])
+        merged.append(name)
+    return merged, skipped
+
+
+__all__ = ["SafeFile", "QLinearSpec", "Nvfp4Linear", "DenseLinear", "load_qlinear", "interleave_rows", "DTYPE_NAMES",
+           "LoraDelta", "LoraFile", "apply_lora"]

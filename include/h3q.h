@@ -272,6 +272,38 @@ typedef struct {
  * how to run it.  Unknown formats fail with the reference's message. */
 h3q_status h3q_checkpoint_qlinear(const h3q_checkpoint* f, const char* prefix, h3q_qlinear_spec* spec);
 
+/* One low-rank delta scale * (b @ a) of a layer (LoraDelta, weights.rs:399-405; lora.rs:15-23): a = lora_down /
+ * lora_A [rank, in_features], b = lora_up / lora_B [out_features, rank], row-major device tensors;
+ * scale = alpha / rank * strength (lora.rs:56-62, dit.rs:664), applied as an f32 multiply. */
+typedef struct {
+  const void* a;
+  const void* b;
+  int64_t rank;
+  int dtype;     /* H3Q_DT_BF16 (the reference loads its factors as bf16, lora.rs:51-53), H3Q_DT_F16 or H3Q_DT_F32 */
+  double scale;
+} h3q_lora;
+
+/* Workspace bytes for h3q_lora_merge_i8 to merge all n rows in one pass (a smaller workspace merges in row
+ * chunks; one row needs 256 + 4 k bytes). */
+size_t h3q_lora_merge_i8_workspace_size(int64_t n, int64_t k);
+
+/* QLinear::merge_loras for an int8 layer (weights.rs:716-757): per row, dequantize (q * s, w_scale per row when
+ * scale_numel == n, else one scalar), undo the ConvRot rotation (convrot 256; 0 = none), add the deltas in order,
+ * rotate again, and requantize: s' = max(max|w| * f32(1/127), 1e-30), q' = clamp(round(w / s'), -128, 127).
+ * w_out [n, k] int8 and scale_out [n] f32 may be w and w_scale (in place) unless w_scale is a scalar.  The
+ * reference leaves the order of its f32 matmul sums to the BLAS; this build's order (k-ordered fma chains for the
+ * deltas, the quantizer's butterfly for the rotations) is the one its oracle restates.  With n_loras == 0 nothing
+ * is written, as the reference returns early (weights.rs:693-695).  The workspace must be 256-byte aligned.  The
+ * caller merges before QLinear::interleave_swiglu, as the reference does (dit.rs:599-616). */
+h3q_status h3q_lora_merge_i8(const int8_t* w, const float* w_scale, int64_t scale_numel, int convrot,
+                             const h3q_lora* loras, int n_loras, int8_t* w_out, float* scale_out, int64_t n, int64_t k,
+                             void* workspace, size_t workspace_bytes, void* stream);
+
+/* QLinear::merge_loras for a dense layer (weights.rs:710-715): w_out = dtype(f32(w) + sum of the deltas), w and
+ * w_out [n, k] of dtype H3Q_DT_F32, H3Q_DT_F16 or H3Q_DT_BF16 (w_out may be w). */
+h3q_status h3q_lora_merge_dense(const void* w, int dtype, const h3q_lora* loras, int n_loras, void* w_out, int64_t n,
+                                int64_t k, void* stream);
+
 /* Weight streaming (weights.rs:185-273 upload_u8_async on a per-device copy stream; the per-block fetch of
  * dit.rs:1160-1186): for weights that stay in host memory (pinned, for the copies to overlap), a ring of device
  * slots filled on the streamer's own copy stream.  Everything is ordered by events on the device, the host never

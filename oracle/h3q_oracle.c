@@ -799,3 +799,84 @@ H3O_API void h3o_qk_norm_rope(const uint16_t* x, int64_t rs, int64_t col, int64_
         }
     }
 }
+
+/* ---------------------------------------------------------------- LoRA merge (load time) */
+
+/* The summed deltas of row i: tot[c] = sum over LoRAs l, in order, of f32(scale_l) * (b_l[i, :] . a_l[:, c]),
+ * each dot product the j-ordered chain fmaf(b[i, j], a[j, c], acc) from 0 (weights.rs:696-707 forms b @ a as an
+ * f32 matmul whose order the BLAS picks; this is the order the CUDA library fixes).  acc is scratch [k]. */
+static void lora_row_delta(int n_loras, const float* const* a, const float* const* b, const int64_t* ranks,
+                           const double* scales, int64_t i, int64_t k, float* tot, float* acc) {
+    for (int l = 0; l < n_loras; ++l) {
+        for (int64_t c = 0; c < k; ++c) acc[c] = 0.f;
+        for (int64_t j = 0; j < ranks[l]; ++j) {
+            const float bv = b[l][i * ranks[l] + j];
+            const float* ar = a[l] + j * k;
+            for (int64_t c = 0; c < k; ++c) acc[c] = fmaf(bv, ar[c], acc[c]);
+        }
+        const float sc = (float)scales[l];
+        for (int64_t c = 0; c < k; ++c) {
+            const float d = acc[c] * sc;
+            tot[c] = l == 0 ? d : tot[c] + d;
+        }
+    }
+}
+
+/*
+ * QLinear::merge_loras for an int8 layer (weights.rs:716-757), row by row: w = (float)q * s (dequant_i8,
+ * kernels.rs:40-48); with ConvRot w = rotate_activation(w) (back to the plain basis, weights.rs:727-730, here the
+ * quantizer's butterfly rot2_group); w = w + deltas; rotate again; s' = max(max|w| * f32(1/127), 1e-30) (candle's
+ * `/ 127.0` is an affine multiply by f32(1/127), then clamp(1e-30, MAX)); q' = clamp(round(w / s'), -128, 127)
+ * (IEEE division, round half away from zero, weights.rs:735-738).  LoRA factors arrive as f32 (bf16 widened).
+ * n_loras == 0 writes nothing (weights.rs:693-695).
+ */
+H3O_API int h3o_lora_merge_i8(const int8_t* q, const float* scale, int per_row, int convrot, int n_loras,
+                              const float* const* a, const float* const* b, const int64_t* ranks,
+                              const double* scales, int8_t* q_out, float* scale_out, int64_t n, int64_t k) {
+    if (convrot != 0 && (convrot != 256 || k % 256 != 0)) return 1;
+    if (n_loras == 0) return 0;
+    float* w = (float*)malloc((size_t)k * sizeof(float));
+    float* tot = (float*)malloc((size_t)k * sizeof(float));
+    float* acc = (float*)malloc((size_t)k * sizeof(float));
+    if (!w || !tot || !acc) {
+        free(w); free(tot); free(acc);
+        return 2;
+    }
+    for (int64_t i = 0; i < n; ++i) {
+        const float s = per_row ? scale[i] : scale[0];
+        for (int64_t c = 0; c < k; ++c) w[c] = (float)q[i * k + c] * s;
+        if (convrot)
+            for (int64_t g = 0; g < k; g += 256) rot2_group(w + g);
+        lora_row_delta(n_loras, a, b, ranks, scales, i, k, tot, acc);
+        for (int64_t c = 0; c < k; ++c) w[c] = w[c] + tot[c];
+        if (convrot)
+            for (int64_t g = 0; g < k; g += 256) rot2_group(w + g);
+        float m = 0.f;
+        for (int64_t c = 0; c < k; ++c) m = fmaxf(m, fabsf(w[c]));
+        const float sc = fmaxf(m * (float)(1.0 / 127.0), 1e-30f);
+        scale_out[i] = sc;
+        for (int64_t c = 0; c < k; ++c) {
+            const float r = roundf(w[c] / sc);
+            q_out[i * k + c] = (int8_t)(int)fminf(fmaxf(r, -128.f), 127.f);
+        }
+    }
+    free(w); free(tot); free(acc);
+    return 0;
+}
+
+/* QLinear::merge_loras for a dense layer (weights.rs:710-715) before the cast back: out = f32(w) + deltas (f32;
+ * the caller rounds to the weight's dtype). */
+H3O_API void h3o_lora_merge_dense(const float* w, int n_loras, const float* const* a, const float* const* b,
+                                  const int64_t* ranks, const double* scales, float* out, int64_t n, int64_t k) {
+    float* tot = (float*)malloc((size_t)k * sizeof(float));
+    float* acc = (float*)malloc((size_t)k * sizeof(float));
+    if (!tot || !acc) {
+        free(tot); free(acc);
+        return;
+    }
+    for (int64_t i = 0; i < n; ++i) {
+        lora_row_delta(n_loras, a, b, ranks, scales, i, k, tot, acc);
+        for (int64_t c = 0; c < k; ++c) out[i * k + c] = n_loras ? w[i * k + c] + tot[c] : w[i * k + c];
+    }
+    free(tot); free(acc);
+}

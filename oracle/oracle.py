@@ -510,3 +510,72 @@ def make_modulate_inputs(seed: int, S: int, C: int, R: int = 3):
     shift = (0.5 * rng.standard_normal((R, C))).astype(np.float32)
     idx = rng.integers(0, R, S).astype(np.uint32)
     return f32_to_bf16_bits(x), f32_to_bf16_bits(w), scale, shift, idx
+
+
+# ----------------------------------------------------------------------------- LoRA merge (weights.rs:692-761)
+
+def _lora_ptrs(loras):
+    """(a [r, k], b [n, r], scale) with f32 (or bf16-widened) factors -> the C oracle's pointer arrays."""
+    m = max(len(loras), 1)
+    pa, pb = (c_vp * m)(), (c_vp * m)()
+    ranks, scales = np.zeros(m, dtype=np.int64), np.zeros(m, dtype=np.float64)
+    keep = []
+    for i, (a, b, s) in enumerate(loras):
+        a = np.ascontiguousarray(a, dtype=np.float32)
+        b = np.ascontiguousarray(b, dtype=np.float32)
+        keep += [a, b]
+        pa[i], pb[i] = a.ctypes.data, b.ctypes.data
+        ranks[i], scales[i] = a.shape[0], float(s)
+    return pa, pb, ranks, scales, keep
+
+
+def lora_merge_i8(q: np.ndarray, scale: np.ndarray, loras, convrot: int = 256):
+    """QLinear::merge_loras for an int8 layer (weights.rs:716-757): dequantize, rotate back, add the deltas,
+    rotate, requantize per row.  loras: (a f32 [r, k], b f32 [n, r], scale).  Returns (q' int8 [n, k],
+    s' f32 [n]); with no LoRA the inputs come back (weights.rs:693-695)."""
+    q = np.ascontiguousarray(q, dtype=np.int8)
+    n, k = q.shape
+    scale = np.ascontiguousarray(scale, dtype=np.float32).reshape(-1)
+    if not loras:
+        return q, scale
+    pa, pb, ranks, scales, keep = _lora_ptrs(loras)
+    qo = np.empty((n, k), dtype=np.int8)
+    so = np.empty(n, dtype=np.float32)
+    rc = lib().h3o_lora_merge_i8(_p(q), _p(scale), c_int(1 if scale.size == n else 0), c_int(convrot),
+                                 c_int(len(loras)), pa, pb, _p(ranks), _p(scales), _p(qo), _p(so), c_i64(n), c_i64(k))
+    if rc != 0:
+        raise ValueError("unsupported LoRA merge arguments")
+    del keep
+    return qo, so
+
+
+def lora_merge_dense(w: np.ndarray, loras) -> np.ndarray:
+    """QLinear::merge_loras for a dense layer before the cast back (weights.rs:710-715): f32(w) + deltas."""
+    w = np.ascontiguousarray(w, dtype=np.float32)
+    n, k = w.shape
+    pa, pb, ranks, scales, keep = _lora_ptrs(loras)
+    out = np.empty((n, k), dtype=np.float32)
+    lib().h3o_lora_merge_dense(_p(w), c_int(len(loras)), pa, pb, _p(ranks), _p(scales), _p(out), c_i64(n), c_i64(k))
+    del keep
+    return out
+
+
+def lora_merge_i8_f64(q: np.ndarray, scale: np.ndarray, loras, convrot: int = 256):
+    """The same merge in f64 with the exact rotation (x @ H), no rounding until the codes: an order-free
+    restatement of weights.rs:716-757 for checking the f32 oracle.  Returns (codes int8, scales f64)."""
+    q = np.asarray(q, dtype=np.int8)
+    n, k = q.shape
+    scale = np.asarray(scale, dtype=np.float32).reshape(-1)
+    s = scale.astype(np.float64) if scale.size == n else np.full(n, float(scale[0]))
+    w = q.astype(np.float64) * s[:, None]
+    H = hadamard(256).astype(np.float64) if convrot else None
+    rot = (lambda x: (x.reshape(-1, 256) @ H).reshape(x.shape)) if convrot else (lambda x: x)
+    w = rot(w)
+    for a, b, sc in loras:
+        w = w + float(np.float32(sc)) * (np.asarray(b, np.float64) @ np.asarray(a, np.float64))
+    w = rot(w)
+    m = np.abs(w).max(axis=1)
+    so = np.maximum(m / 127.0, 1e-30)
+    r = w / so[:, None]
+    codes = np.clip(np.sign(r) * np.floor(np.abs(r) + 0.5), -128, 127).astype(np.int8)
+    return codes, so
