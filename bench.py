@@ -535,6 +535,8 @@ def main() -> None:
                     help="small case for ncu captures: qk_norm_rope of the q heads at S=16384, H=40, rot 96")
     ap.add_argument("--profile-modulate", action="store_true",
                     help="small case for ncu captures: rms_modulate + rotated int8 quantization at M=8192, C=5120")
+    ap.add_argument("--profile-lora", action="store_true",
+                    help="small case for ncu captures: the LoRA merge of a 4096 x 5120 int8 layer, rank 64")
     ap.add_argument("--profile", action="store_true",
                     help="small case for ncu captures: one 4096-token fc1 linear (quant + GEMM), nothing else")
     args = ap.parse_args()
@@ -550,6 +552,10 @@ def main() -> None:
     if args.profile_modulate:
         import torch
         print(json.dumps(modulate_fused(torch.device("cuda", 0), load_peaks(), reps=args.steps, M=8192)))
+        return
+    if args.profile_lora:
+        import torch
+        print(json.dumps(lora_merge(torch.device("cuda", 0), reps=args.steps, n=4096)))
         return
     if args.profile_nvfp4:
         import torch

@@ -19,8 +19,11 @@
 //
 // Layout: one CTA per (32 rows) x (256 columns = one rotation group); thread (row r, quarter j) owns the row's 64
 // contiguous columns 64j .. 64j+63, so rotation digits 0-2 run in registers and digit 3 crosses the row's four
-// lanes by shuffles.  The deltas are register-accumulated from k-chunks of A and B staged in shared memory as
-// f32.  int8 layers write the merged f32 rows to a workspace and the row maxima by atomics; a second kernel
+// lanes by shuffles.  The deltas are computed in a different thread layout first: thread (warp w, lane l) owns an
+// 8-row x 8-column micro-tile (rows 8w .. 8w+7, columns 4l .. 4l+3 and 128+4l .. 128+4l+3), register-accumulated
+// from rank chunks of A and B staged in shared memory as f32, two columns per paired fma.rn.f32x2, so every staged
+// value feeds eight FMAs (each element's chain is the same sequence of rounded fmas in either layout).  The summed
+// delta tile then passes once through shared memory into the rotation layout.  int8 layers write the merged f32 rows to a workspace and the row maxima by atomics; a second kernel
 // requantizes.  Rows are processed in chunks that fit the caller's workspace.
 #include <cstdarg>
 #include <cstdint>
@@ -28,6 +31,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include "../../include/h3q.h"
+#include "ptx.cuh"
 
 namespace h3q {
 void set_last_error(const char* msg);
@@ -117,9 +121,9 @@ __device__ __forceinline__ void rotate256(float (&v)[64]) {
 }
 
 template <bool I8, bool ROT>
-__global__ void __launch_bounds__(kThreads) lora_merge_kernel(const MergeArgs p) {
+__global__ void __launch_bounds__(kThreads, 1) lora_merge_kernel(const MergeArgs p) {
   __shared__ __align__(16) float As[kChunk][4 * kSeg];  // read as float4
-  __shared__ float Bs[kRows][kChunk + 1];
+  __shared__ __align__(16) float Bs[kChunk][kRows];      // transposed: (rank entry, row)
   const int t = threadIdx.x, r = t >> 2, j = t & 3;
   const int64_t rloc = (int64_t)blockIdx.y * kRows + r;  // row within the chunk
   const int64_t row = p.row0 + rloc;
@@ -127,50 +131,107 @@ __global__ void __launch_bounds__(kThreads) lora_merge_kernel(const MergeArgs p)
   const int64_t cg = (int64_t)blockIdx.x * kCols;         // first column of the CTA
   const int64_t c0 = cg + 64 * j;                          // first column of the thread
   const int nv = p.k - c0 >= 64 ? 64 : (p.k - c0 > 0 ? (int)(p.k - c0) : 0);
+  // delta micro-tile of the thread: rows 8 mw .. 8 mw + 7, columns 4 ml .. 4 ml + 3 and 128 + 4 ml .. + 3; element
+  // pairs [4 i + h] = row 8 mw + i, columns (c_h, c_h + 1) with c_0 = 4 ml, c_1 = 4 ml + 2, c_2 = 128 + 4 ml, c_3 = +2
+  const int mw = t >> 5, ml = t & 31;
+  const int ca = ((4 * ml) >> 6) * kSeg + ((4 * ml) & 63);                  // staged-A offset of column 4 ml
+  const int cb = ((128 + 4 * ml) >> 6) * kSeg + ((128 + 4 * ml) & 63);      // and of column 128 + 4 ml
 
-  float tot[64];
+  h3q::f2 tot2[32];
 #pragma unroll
-  for (int i = 0; i < 64; ++i) tot[i] = 0.f;
+  for (int i = 0; i < 32; ++i) tot2[i] = h3q::pk(0.f, 0.f);
   for (int l = 0; l < p.n_loras; ++l) {
     const Term tm = p.l[l];
-    float acc[64];
+    h3q::f2 acc2[32];
 #pragma unroll
-    for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+    for (int i = 0; i < 32; ++i) acc2[i] = h3q::pk(0.f, 0.f);
+    // bf16 factors whose column group is whole and 16-byte aligned are staged 8 values per load
+    const bool vec_a = tm.kind == 2 && (p.k & 7) == 0 && cg + kCols <= p.k &&
+                       (reinterpret_cast<uintptr_t>(tm.a) & 15u) == 0;
     for (int64_t j0 = 0; j0 < tm.rank; j0 += kChunk) {
       const int nj = tm.rank - j0 < kChunk ? (int)(tm.rank - j0) : kChunk;
       __syncthreads();  // the previous chunk has been consumed
-      for (int idx = t; idx < kChunk * kCols; idx += kThreads) {
-        const int jj = idx >> 8, c = idx & (kCols - 1);
-        float a = 0.f;
-        if (jj < nj && cg + c < p.k) a = ld_f32(tm.a, tm.kind, (j0 + jj) * p.k + cg + c);
-        As[jj][(c >> 6) * kSeg + (c & 63)] = a;
+      if (vec_a) {
+        for (int idx = t; idx < kChunk * (kCols / 8); idx += kThreads) {
+          const int jj = idx >> 5, c = (idx & 31) * 8;
+          uint4 raw = make_uint4(0u, 0u, 0u, 0u);
+          if (jj < nj)
+            raw = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(tm.a) + (j0 + jj) * p.k + cg + c);
+          float4* dst = reinterpret_cast<float4*>(&As[jj][(c >> 6) * kSeg + (c & 63)]);
+          dst[0] = make_float4(__uint_as_float(raw.x << 16), __uint_as_float(raw.x & 0xffff0000u),
+                               __uint_as_float(raw.y << 16), __uint_as_float(raw.y & 0xffff0000u));
+          dst[1] = make_float4(__uint_as_float(raw.z << 16), __uint_as_float(raw.z & 0xffff0000u),
+                               __uint_as_float(raw.w << 16), __uint_as_float(raw.w & 0xffff0000u));
+        }
+      } else {
+        for (int idx = t; idx < kChunk * kCols; idx += kThreads) {
+          const int jj = idx >> 8, c = idx & (kCols - 1);
+          float a = 0.f;
+          if (jj < nj && cg + c < p.k) a = ld_f32(tm.a, tm.kind, (j0 + jj) * p.k + cg + c);
+          As[jj][(c >> 6) * kSeg + (c & 63)] = a;
+        }
       }
       for (int idx = t; idx < kRows * kChunk; idx += kThreads) {
-        const int rr = idx / kChunk, jj = idx % kChunk;
+        const int rr = idx % kRows, jj = idx / kRows;  // rows fastest: conflict-free transposed stores
         const int64_t rl = (int64_t)blockIdx.y * kRows + rr;
         float b = 0.f;
         if (jj < nj && rl < p.rows) b = ld_f32(tm.b, tm.kind, (p.row0 + rl) * tm.rank + j0 + jj);
-        Bs[rr][jj] = b;
+        Bs[jj][rr] = b;
       }
       __syncthreads();
       for (int jj = 0; jj < nj; ++jj) {
-        const float bv = Bs[r][jj];
-        const float4* ap = reinterpret_cast<const float4*>(&As[jj][j * kSeg]);
+        const float4 a0 = *reinterpret_cast<const float4*>(&As[jj][ca]);
+        const float4 a1 = *reinterpret_cast<const float4*>(&As[jj][cb]);
+        const float4 b0 = *reinterpret_cast<const float4*>(&Bs[jj][8 * mw]);
+        const float4 b1 = *reinterpret_cast<const float4*>(&Bs[jj][8 * mw + 4]);
+        const float bv[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+        const h3q::f2 a00 = h3q::pk(a0.x, a0.y), a01 = h3q::pk(a0.z, a0.w);
+        const h3q::f2 a10 = h3q::pk(a1.x, a1.y), a11 = h3q::pk(a1.z, a1.w);
 #pragma unroll
-        for (int c4 = 0; c4 < 16; ++c4) {
-          const float4 a4 = ap[c4];
-          acc[4 * c4] = __fmaf_rn(bv, a4.x, acc[4 * c4]);
-          acc[4 * c4 + 1] = __fmaf_rn(bv, a4.y, acc[4 * c4 + 1]);
-          acc[4 * c4 + 2] = __fmaf_rn(bv, a4.z, acc[4 * c4 + 2]);
-          acc[4 * c4 + 3] = __fmaf_rn(bv, a4.w, acc[4 * c4 + 3]);
+        for (int i = 0; i < 8; ++i) {
+          const h3q::f2 b2 = h3q::pk(bv[i], bv[i]);
+          acc2[4 * i] = h3q::fma2(b2, a00, acc2[4 * i]);
+          acc2[4 * i + 1] = h3q::fma2(b2, a01, acc2[4 * i + 1]);
+          acc2[4 * i + 2] = h3q::fma2(b2, a10, acc2[4 * i + 2]);
+          acc2[4 * i + 3] = h3q::fma2(b2, a11, acc2[4 * i + 3]);
         }
       }
     }
 #pragma unroll
-    for (int i = 0; i < 64; ++i) {
-      const float d = __fmul_rn(acc[i], tm.scale);
-      tot[i] = l == 0 ? d : __fadd_rn(tot[i], d);
+    for (int i = 0; i < 32; ++i) {
+      float a0, a1, t0, t1;
+      h3q::upk(acc2[i], a0, a1);
+      h3q::upk(tot2[i], t0, t1);
+      const float d0 = __fmul_rn(a0, tm.scale), d1 = __fmul_rn(a1, tm.scale);
+      tot2[i] = l == 0 ? h3q::pk(d0, d1) : h3q::pk(__fadd_rn(t0, d0), __fadd_rn(t1, d1));
     }
+  }
+  // the summed delta tile into the rotation layout, through the A staging area (32 rows x 4 x kSeg floats)
+  float tot[64];
+  if (p.n_loras > 0) {
+    __syncthreads();  // the last chunk has been consumed
+    float* ds = &As[0][0];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float x0, x1, x2, x3, y0, y1, y2, y3;
+      h3q::upk(tot2[4 * i], x0, x1);
+      h3q::upk(tot2[4 * i + 1], x2, x3);
+      h3q::upk(tot2[4 * i + 2], y0, y1);
+      h3q::upk(tot2[4 * i + 3], y2, y3);
+      float* drow = ds + (8 * mw + i) * (4 * kSeg);
+      *reinterpret_cast<float4*>(drow + ca) = make_float4(x0, x1, x2, x3);
+      *reinterpret_cast<float4*>(drow + cb) = make_float4(y0, y1, y2, y3);
+    }
+    __syncthreads();
+    const float4* src = reinterpret_cast<const float4*>(ds + r * (4 * kSeg) + j * kSeg);
+#pragma unroll
+    for (int c4 = 0; c4 < 16; ++c4) {
+      const float4 v4 = src[c4];
+      tot[4 * c4] = v4.x; tot[4 * c4 + 1] = v4.y; tot[4 * c4 + 2] = v4.z; tot[4 * c4 + 3] = v4.w;
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 64; ++i) tot[i] = 0.f;
   }
 
   float v[64];
