@@ -173,7 +173,7 @@ def config_block(n_gpus: int) -> dict:
 def nvfp4_c3(dev, peaks: dict, reps: int = 10) -> dict:
     """the text encoder's NVFP4+AWQ linears at 512 prompt tokens (5120 -> 25600 and
     25600 -> 5120), fused fp4-decode + bf16 tcgen05 GEMM; CUDA-event time per layer and TFLOP/s against the measured
-    bf16 peak (the tensor cores run bf16 here: the activations stay bf16)."""
+    bf16 peak (the tensor cores run bf16 here, because the reference keeps the activations bf16)."""
     import torch
     import h3q
     g = torch.Generator(device=dev).manual_seed(99)

@@ -346,10 +346,10 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
 #pragma unroll
       for (int k = 0; k < 32; ++k) v2[k] = pk(0.f, 0.f);
     }
-    // Digit 3 crosses the quad.  Transpose through shared memory in two rounds of 32 columns, each thread
+    // Digit 3 crosses the quad.  Transpose through shared memory in two passes of 32 columns, each thread
     // writing into its own (already consumed) 128-byte line of this stage: afterwards thread j holds, for all
-    // four digit-3 values, columns 8j..8j+7 (round 0) and 32+8j..32+8j+7 (round 1) of its group.
-    f2 u2[4][8];  // u2[d3][i] = columns (2i, 2i + 1) of the thread's two 8-column slices, in round order
+    // four digit-3 values, columns 8j..8j+7 (pass 0) and 32+8j..32+8j+7 (pass 1) of its group.
+    f2 u2[4][8];  // u2[d3][i] = columns (2i, 2i + 1) of the thread's two 8-column slices, in pass order
     if (ORDER != 0) {
       // digit 0 (element offsets 1): within a pair, so scalar, with the reference's first-stage sum order
 #pragma unroll
@@ -513,7 +513,7 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
     if (t == 0) scale[row] = s;
     if (owner) {
       const f2 inv2 = pk(inv, inv), rnd2 = pk(12582912.0f, 12582912.0f), zero2 = pk(0.f, 0.f);
-      uint32_t w[16];  // w[2*h + k]: bytes of slice h's columns 4k .. 4k+3 (h = 2 d3 + round)
+      uint32_t w[16];  // w[2*h + k]: bytes of slice h's columns 4k .. 4k+3 (h = 2 d3 + pass)
 #pragma unroll
       for (int h = 0; h < 8; ++h) {
         const int d3 = h >> 1, i0 = 4 * (h & 1);
