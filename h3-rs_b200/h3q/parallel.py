@@ -189,18 +189,32 @@ class NSplitLinear:
             self.bufs = None
 
 
+def gather_full(local, total: int, group=None):
+    """gather_rows without the staging copies when every rank holds the same number of rows (total divisible by
+    the world size): one all-gather straight into the full [total, ...] tensor, rank blocks in rank order."""
+    dist = _dist()
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    if total % world != 0:
+        return gather_rows(local, total, group)
+    lo, hi = row_range(total, world, rank)
+    if local.shape[0] != hi - lo:
+        raise ValueError(f"gather_full: rank {rank} holds {local.shape[0]} rows, expected {(lo, hi)}")
+    out = local.new_empty((total,) + tuple(local.shape[1:]))
+    dist.all_gather_into_tensor(out, local.contiguous(), group=group)
+    return out
+
+
 def sharded_attention(q_local, k_local, v_local, total: int, group=None, flags: int = 0, rows_op=None):
     """Query-sharded attention: this rank's rows q_local, k_local, v_local ([s_r, H, 128], row_range order) ->
-    its output rows [s_r, H, 128], attending over the keys and values of every rank.  K and V travel together in
-    one all-gather.  rows_op(q, k, v, flags) defaults to h3q.attention_rows."""
-    import torch
-    kv = gather_rows(torch.stack([k_local, v_local], dim=1), total, group)
-    k_full, v_full = kv[:, 0].contiguous(), kv[:, 1].contiguous()
+    its output rows [s_r, H, 128], attending over the keys and values of every rank.  K and V are each gathered
+    straight into full tensors (gather_full).  rows_op(q, k, v, flags) defaults to h3q.attention_rows."""
+    k_full = gather_full(k_local, total, group)
+    v_full = gather_full(v_local, total, group)
     if rows_op is None:
         H = q_local.shape[1]
         return _attention_rows(q_local, k_full, v_full.reshape(total, H * 128), H * 128, 0, flags)
     return rows_op(q_local, k_full, v_full, flags)
 
 
-__all__ = ["row_range", "nsplit_range", "gather_rows", "gather_columns", "PeerBuffers", "NSplitLinear",
+__all__ = ["row_range", "nsplit_range", "gather_rows", "gather_full", "gather_columns", "PeerBuffers", "NSplitLinear",
            "sharded_attention", "H3QError"]

@@ -32,6 +32,10 @@ def _worker(rank: int, world: int, port: int, errors):
         x = torch.arange(7 * 3, dtype=torch.float32).reshape(7, 3)
         lo, hi = P.row_range(7, world, rank)
         assert torch.equal(P.gather_rows(x[lo:hi], 7), x)
+        assert torch.equal(P.gather_full(x[lo:hi], 7), x)  # uneven blocks: falls back to gather_rows
+        x8 = torch.arange(8 * 3, dtype=torch.float32).reshape(8, 3)
+        lo8, hi8 = P.row_range(8, world, rank)
+        assert torch.equal(P.gather_full(x8[lo8:hi8], 8), x8)  # even blocks: one all-gather into the result
 
         # N split: each rank's oracle linear on its weight rows, column blocks gathered = the full linear
         M, K, N = 40, 512, 600
@@ -51,6 +55,12 @@ def _worker(rank: int, world: int, port: int, errors):
             return torch.from_numpy(O.attention_rows(_bits(ql), _bits(kf), _bits(vf), flags).astype(np.int32))
 
         ti = lambda a: torch.from_numpy(a.astype(np.int32))
+        out = P.sharded_attention(ti(q[lo:hi]), ti(k[lo:hi]), ti(v[lo:hi]), S, rows_op=rows_op)
+        np.testing.assert_array_equal(_bits(out), O.attention(q, k, v)[lo:hi])
+        # an odd token count: uneven row blocks
+        S = 301
+        q, k, v = O.make_attn_inputs(10, S, H, 3.0)
+        lo, hi = P.row_range(S, world, rank)
         out = P.sharded_attention(ti(q[lo:hi]), ti(k[lo:hi]), ti(v[lo:hi]), S, rows_op=rows_op)
         np.testing.assert_array_equal(_bits(out), O.attention(q, k, v)[lo:hi])
         dist.barrier()
