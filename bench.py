@@ -431,6 +431,52 @@ def lora_merge(dev, reps: int = 3, n: int = 15360, k: int = 5120, rank: int = 64
             "note": "includes the workspace allocation of each call; f32 FMA chains on the CUDA cores"}
 
 
+def dit_block_c4(dev, reps: int = 3, S: int = 32760, H: int = 40, F: int = 13824, rot: int = 96) -> dict:
+    """One whole DiT block (Dit::run_block, dit.rs:969-1021) at config 4's shape: modulate, qkv, the attention step,
+    out + gated residual, modulate, fc1 + SwiGLU, fc2 + gated residual.  "ops" issues the reference's calls one by
+    one (h3q.dit.run_block_ops); "fused" is h3q.dit.run_block (the modulation feeds the quantizer, SwiGLU and the
+    gated residuals run in the GEMM epilogues).  gemm_tops counts the four linears' 2 S N K only."""
+    import torch
+    import h3q
+    from h3q import dit as D
+    g = torch.Generator(device=dev).manual_seed(47)
+    C = H * 128
+
+    def lin(n, k):
+        return D.Linear(torch.randint(-127, 128, (n, k), generator=g, device=dev, dtype=torch.int8),
+                        torch.rand(n, generator=g, device=dev) * 2e-3 + 5e-4,
+                        0.02 * torch.randn(n, generator=g, device=dev))
+    nw = lambda: (1 + 0.1 * torch.randn(C, generator=g, device=dev)).to(torch.bfloat16)
+    hw = lambda: (1 + 0.2 * torch.randn(128, generator=g, device=dev)).to(torch.bfloat16)
+    blk = D.Block(lin(3 * C, C), lin(C, C), lin(2 * F, C), lin(C, F), nw(), nw(), hw(), hw(), H)
+    tab = lambda: 0.5 * torch.randn((6, C), generator=g, device=dev)
+    gate = lambda: torch.rand((6, C), generator=g, device=dev)
+    idx = ((torch.arange(S, device=dev) // 1560) % 6).to(torch.int32)
+    ang = 100.0 * torch.rand((S, rot // 2), generator=g, device=dev)
+    cs = torch.stack([ang.cos(), ang.sin()]).to(torch.bfloat16).float().contiguous()
+    cx = D.StepCtx(tab(), tab(), gate(), tab(), tab(), gate(), idx, cs, rot,
+                   h3q.ATTN_SCALE_BLOCK128 | h3q.ATTN_PV_BF16)
+    x = torch.randn((S, C), generator=g, device=dev).to(torch.bfloat16)
+    res = {}
+    for name, fn in (("fused", D.run_block), ("ops", D.run_block_ops)):
+        for _ in range(2):
+            fn(x, blk, cx)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn(x, blk, cx)
+        e1.record()
+        torch.cuda.synchronize()
+        res[name + "_ms"] = round(e0.elapsed_time(e1) / reps, 3)
+    ops = 2.0 * S * C * (3 * C + C + 2 * F + F)
+    res["gemm_tops_per_block"] = round(ops / 1e12, 2)
+    res["same_bits"] = bool(torch.equal(D.run_block(x, blk, cx).view(torch.int16),
+                                        D.run_block_ops(x, blk, cx).view(torch.int16)))
+    res["workload"] = f"DiT block S{S} C{C} H{H} F{F} (fc1 {2 * F} interleaved rows), rope rot {rot}"
+    res["device_status"] = h3q.device_status(dev.index or 0)
+    return res
+
+
 def _max_over_ranks(ms: float, dist, dev) -> float:
     import torch
     t = torch.tensor([ms], device=dev, dtype=torch.float64)
@@ -750,6 +796,7 @@ def main() -> None:
     lmerge = lora_merge(dev) if rank == 0 else None
     attend = attend_step_c4(dev) if rank == 0 else None
     stream_c1 = streaming_c1(layers, M, dev) if rank == 0 else None
+    block = dit_block_c4(dev) if rank == 0 else None
 
     cb = None
     if rank == 0 and ws_n == 1 and not args.no_cpu_baseline:
@@ -785,6 +832,7 @@ def main() -> None:
         "lora_merge": lmerge,
         "attend_step_c4": attend,
         "weight_streaming_c1": stream_c1,
+        "dit_block_c4": block,
         "multi_gpu": extras,
         "cpu_baseline": cb, "e2e": e2e, "clocks": clocks,
         "gpu_launches": 2 * launches,
