@@ -67,17 +67,21 @@ class StepCtx:
     flags: int = 0
 
 
-def run_block_ops(x, b: Block, cx: StepCtx):
-    """The block as the reference issues it (dit.rs:981-1017), one library call per reference call."""
+def run_block_ops(x, b: Block, cx: StepCtx, trace: dict | None = None):
+    """The block as the reference issues it (dit.rs:981-1017), one library call per reference call.  With a dict
+    as trace, each intermediate is kept in it under the reference's name (n1, qkv, att, o, x1, n2, h, m, y)."""
     n1 = rms_modulate(x, b.norm1, b.eps, cx.scale_msa, cx.shift_msa, cx.idx)
     qkv = gemm_s8(n1, b.qkv.w, b.qkv.ws, b.qkv.bias, swiglu=False, rotate=True)
     att = attend_qkv(qkv, b.heads, (b.q_norm, b.k_norm), b.eps, cx.rope, cx.rot, cx.flags)
     o = gemm_s8(att, b.out.w, b.out.ws, b.out.bias, swiglu=False, rotate=True)
-    x = gate_add(x, o, cx.gate_msa, cx.idx)
-    n2 = rms_modulate(x, b.norm2, b.eps, cx.scale_mlp, cx.shift_mlp, cx.idx)
+    x1 = gate_add(x, o, cx.gate_msa, cx.idx)
+    n2 = rms_modulate(x1, b.norm2, b.eps, cx.scale_mlp, cx.shift_mlp, cx.idx)
     h = gemm_s8(n2, b.fc1.w, b.fc1.ws, b.fc1.bias, swiglu=True, rotate=True)
     m = gemm_s8(h, b.fc2.w, b.fc2.ws, b.fc2.bias, swiglu=False, rotate=True)
-    return gate_add(x, m, cx.gate_mlp, cx.idx)
+    y = gate_add(x1, m, cx.gate_mlp, cx.idx)
+    if trace is not None:
+        trace.update(n1=n1, qkv=qkv, att=att, o=o, x1=x1, n2=n2, h=h, m=m, y=y)
+    return y
 
 
 def run_block(x, b: Block, cx: StepCtx):
