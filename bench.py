@@ -124,10 +124,11 @@ def dist_env():
 
 # --------------------------------------------------------------------------------------------- CPU baseline
 
-def cpu_baseline(rows: int = 256) -> dict:
+def cpu_baseline(rows: int = 4096) -> dict:
     """The reference's CPU path (oracle port of portable/kernels.rs:220-242) for every linear of the workload:
     each call dequantises the whole weight (timed in full, once per linear, as the reference does per call), then
-    rotates and multiplies the activations (timed on a `rows`-token sample and scaled to 32760 tokens).
+    rotates and multiplies the activations (timed on a `rows`-token sample and scaled to 32760 tokens).  The
+    default sample is about 10 s of host work on a 16-thread host.
     TOPS = algorithmic ops of the full workload / that extrapolated time.  numpy BLAS uses every host core."""
     import numpy as np
     from oracle import oracle as O
