@@ -34,6 +34,7 @@ WORKLOAD = ("BASELINE c1: DiT-scale int8 ConvRot linears, M=32760 tokens; qkv 51
             "out 5120->5120, fc2 13824->5120; bf16 in/out, per-token int8 activations, int8 weights")
 NOMINAL_INT8_TOPS = 4500.0
 E2E_CHUNK = int(os.environ.get("H3Q_E2E_CHUNK", "2048"))  # rows per chunk of the host-memory path (e2e)
+E2E_IN_SLOTS = int(os.environ.get("H3Q_E2E_IN_SLOTS", "32"))  # input chunk buffers of the host-memory path
 
 
 def ops_per_step(m: int) -> float:
@@ -747,20 +748,24 @@ def main() -> None:
             traffic = json.load(f).get("dram_bytes_per_launch")
 
     # end to end through the C ABI with host buffers: every linear's input comes from pinned host memory and its
-    # output goes back to it (h3q_host_pipeline_gemm_s8: chunked copies in and out overlapped with the GEMMs)
+    # output goes back to it.  The step's four linears go to h3q_host_pipeline_run as one batch: chunked copies in
+    # and out overlap the GEMMs, and each linear's copies in overlap the previous linear's last GEMMs and copies out.
     e2e = None
     if rank == 0 or True:
         host_x = [ly["x"].cpu().pin_memory() for ly in layers]
         host_o = [torch.empty((M, ly["n"]), dtype=torch.bfloat16).pin_memory() for ly in layers]
         pipe = ctypes.c_void_p()
-        h3q.check(L.h3q_host_pipeline_create(E2E_CHUNK, max(ly["k"] for ly in layers), max(ly["n"] for ly in layers),
-                                             ctypes.byref(pipe)))
+        # 32 input chunk buffers (1.8 GB): fc2's wide inputs cross PCIe while qkv and fc1 are bound by their copies out
+        h3q.check(L.h3q_host_pipeline_create_ex(E2E_CHUNK, max(ly["k"] for ly in layers),
+                                                max(ly["n"] for ly in layers), E2E_IN_SLOTS, 2, ctypes.byref(pipe)))
+
+        items = (h3q.HostLinear * len(layers))()
+        for i, ly in enumerate(layers):
+            items[i] = h3q.HostLinear(host_x[i].data_ptr(), ly["w"].data_ptr(), ly["ws"].data_ptr(), ly["n"],
+                                      ly["b"].data_ptr(), host_o[i].data_ptr(), M, ly["n"], ly["k"], 0, 1)
 
         def e2e_step():
-            for i, ly in enumerate(layers):
-                h3q.check(L.h3q_host_pipeline_gemm_s8(pipe, host_x[i].data_ptr(), ly["w"].data_ptr(),
-                                                      ly["ws"].data_ptr(), ly["n"], ly["b"].data_ptr(),
-                                                      host_o[i].data_ptr(), M, ly["n"], ly["k"], 0, 1, sp))
+            h3q.check(L.h3q_host_pipeline_run(pipe, items, len(layers), sp))
 
         e2e_step()
         torch.cuda.synchronize()
@@ -779,7 +784,8 @@ def main() -> None:
         e2e = {"value": ws_n * ops_per_step(M) / (e_ms * 1e-3) / 1e12, "unit": "TOPS",
                "h2d_bytes_per_step": int(sum(h.numel() * 2 for h in host_x)),
                "d2h_bytes_per_step": int(sum(h.numel() * 2 for h in host_o)), "ms_per_step": e_ms,
-               "path": f"h3q_host_pipeline_gemm_s8 (C ABI): pinned host input and output, {E2E_CHUNK}-row chunks "
+               "path": f"h3q_host_pipeline_run (C ABI), the four linears as one batch: pinned host input and output, "
+                       f"{E2E_CHUNK}-row chunks, {E2E_IN_SLOTS} input chunk buffers, "
                        "whose copies in and out overlap the GEMMs, copies inside the timed region"}
         L.h3q_host_pipeline_destroy(pipe)
 

@@ -38,6 +38,13 @@ class LoraDesc(ctypes.Structure):
                 ("scale", ctypes.c_double)]
 
 
+class HostLinear(ctypes.Structure):
+    """h3q_host_linear: one linear of a host-pipeline batch (the arguments of h3q_host_pipeline_gemm_s8)."""
+    _fields_ = [("x_host", ctypes.c_void_p), ("w", ctypes.c_void_p), ("ws", ctypes.c_void_p), ("ws_numel", ctypes.c_int64),
+                ("bias", ctypes.c_void_p), ("out_host", ctypes.c_void_p), ("m", ctypes.c_int64), ("n", ctypes.c_int64),
+                ("k", ctypes.c_int64), ("swiglu", ctypes.c_int), ("rotate", ctypes.c_int)]
+
+
 FMT_DENSE, FMT_INT8, FMT_NVFP4 = 0, 1, 2
 ATTN_SCALE_TOKEN, ATTN_SCALE_BLOCK128, ATTN_PV_F16, ATTN_PV_BF16 = 0, 1, 0, 2
 PATH_GEMM_S8, PATH_INT8_LINEAR, PATH_ROTATE_FUSED, PATH_ROTATE_SEPARATE, PATH_SWIGLU_FUSED, PATH_SWIGLU_AFTER = (
@@ -48,8 +55,10 @@ PATH_GEMM_S8, PATH_INT8_LINEAR, PATH_ROTATE_FUSED, PATH_ROTATE_SEPARATE, PATH_SW
 SIGNATURES = {
     "h3q_last_error": (ctypes.c_char_p, []),
     "h3q_host_pipeline_create": (_int, [_i64, _i64, _i64, ctypes.POINTER(_vp)]),
+    "h3q_host_pipeline_create_ex": (_int, [_i64, _i64, _i64, _int, _int, ctypes.POINTER(_vp)]),
     "h3q_host_pipeline_destroy": (None, [_vp]),
     "h3q_host_pipeline_gemm_s8": (_int, [_vp, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _int, _int, _vp]),
+    "h3q_host_pipeline_run": (_int, [_vp, _vp, _int, _vp]),
     "h3q_streamer_create": (_int, [_sz, _int, ctypes.POINTER(_vp)]),
     "h3q_streamer_destroy": (None, [_vp]),
     "h3q_streamer_slot_bytes": (_sz, [_vp]),
@@ -521,12 +530,12 @@ class HostPipeline:
     """gemm_s8 on pinned host activations with the copies in, the GEMMs and the copies out overlapped
     (h3q_host_pipeline_*)."""
 
-    def __init__(self, chunk_rows: int, max_k: int, max_n: int, device=None):
+    def __init__(self, chunk_rows: int, max_k: int, max_n: int, device=None, in_slots: int = 2, out_slots: int = 2):
         import torch
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         h = ctypes.c_void_p()
         with torch.cuda.device(self.device):
-            check(lib().h3q_host_pipeline_create(chunk_rows, max_k, max_n, ctypes.byref(h)))
+            check(lib().h3q_host_pipeline_create_ex(chunk_rows, max_k, max_n, in_slots, out_slots, ctypes.byref(h)))
         self._h = h
 
     def close(self) -> None:
@@ -552,6 +561,22 @@ class HostPipeline:
         check(lib().h3q_host_pipeline_gemm_s8(self._h, _p(x_host), _p(w), _p(ws), ws.numel(), _p(bias), _p(out), m, n,
                                               k, int(swiglu), int(rotate), _stream(self.device)))
         return out
+
+    def run(self, linears):
+        """Several linears as one pipelined sequence (h3q_host_pipeline_run): each item is
+        (x_host, w, ws, bias, out_host, swiglu, rotate) with pinned host x_host / out_host; an item may read an
+        earlier item's out_host.  Stream-ordered on the current stream, like gemm_s8."""
+        import torch
+        items = (HostLinear * max(len(linears), 1))()
+        keep = []
+        for i, (x_host, w, ws, bias, out_host, swiglu, rotate) in enumerate(linears):
+            ws = ws.to(torch.float32).contiguous()
+            keep.append(ws)
+            m, k = x_host.shape
+            items[i] = HostLinear(_p(x_host), _p(w), _p(ws), ws.numel(), _p(bias), _p(out_host), m, w.shape[0], k,
+                                  int(swiglu), int(rotate))
+        check(lib().h3q_host_pipeline_run(self._h, items, len(linears), _stream(self.device)))
+        del keep
 
 
 def _lora_descs(loras, n: int, k: int, device):

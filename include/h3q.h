@@ -94,6 +94,10 @@ h3q_status h3q_gemm_s8(const uint16_t* x, const int8_t* w, const float* ws, int6
  * workspace and the streams. */
 typedef struct h3q_host_pipeline h3q_host_pipeline;
 h3q_status h3q_host_pipeline_create(int64_t chunk_rows, int64_t max_k, int64_t max_n, h3q_host_pipeline** out);
+/* The same with in_slots input and out_slots output chunk buffers (each in [2, 4096]; the plain create uses 2 and 2).
+ * More input buffers let the copies in run further ahead of the GEMMs. */
+h3q_status h3q_host_pipeline_create_ex(int64_t chunk_rows, int64_t max_k, int64_t max_n, int in_slots, int out_slots,
+                                       h3q_host_pipeline** out);
 void h3q_host_pipeline_destroy(h3q_host_pipeline* p);
 /* out_host [m, n] (or [m, n/2] with swiglu) = h3q_gemm_s8(x_host [m, k]) with host buffers (pinned, for the copies
  * to overlap).  Ordered after the work already on `stream`; `stream` waits for the last copy out, so the output
@@ -101,6 +105,23 @@ void h3q_host_pipeline_destroy(h3q_host_pipeline* p);
 h3q_status h3q_host_pipeline_gemm_s8(h3q_host_pipeline* p, const uint16_t* x_host, const int8_t* w, const float* ws,
                                      int64_t ws_numel, const float* bias, uint16_t* out_host, int64_t m, int64_t n,
                                      int64_t k, int swiglu, int rotate, void* stream);
+/* One linear of a batch: the arguments of h3q_host_pipeline_gemm_s8. */
+typedef struct h3q_host_linear {
+  const uint16_t* x_host;
+  const int8_t* w;
+  const float* ws;
+  int64_t ws_numel;
+  const float* bias;
+  uint16_t* out_host;
+  int64_t m, n, k;
+  int swiglu, rotate;
+} h3q_host_linear;
+/* The `count` linears of `items` as one pipelined sequence (a DiT block's linears on host activations): linear
+ * i + 1 copies in while linear i still computes and copies out, where separate calls would wait for each call's
+ * last copy out.  A linear whose host input overlaps the host output of an earlier linear of the batch starts its
+ * copies in after every copy out enqueued before it.  Every item is checked before anything is enqueued; the batch
+ * as a whole keeps the stream contract of h3q_host_pipeline_gemm_s8 (which is this call with one item). */
+h3q_status h3q_host_pipeline_run(h3q_host_pipeline* p, const h3q_host_linear* items, int count, void* stream);
 
 /* Workspace bytes h3q_int8_linear_ex needs. */
 size_t h3q_int8_linear_workspace_size(int64_t m, int64_t k);

@@ -95,3 +95,12 @@ def test_init_rejects_a_missing_or_unsupported_device():
     import h3q
     assert h3q.lib().h3q_init(4096) == h3q.ERR_UNSUPPORTED
     assert "not an sm_100 GPU" in h3q.last_error()
+
+
+def test_host_pipeline_slot_counts_are_checked():
+    """h3q_host_pipeline_create_ex rejects fewer than two buffers per direction before touching the device."""
+    L = h3q.lib()
+    h = ctypes.c_void_p()
+    for ins, outs in ((1, 2), (2, 1), (2, 5000)):
+        assert L.h3q_host_pipeline_create_ex(256, 1024, 1024, ins, outs, ctypes.byref(h)) == h3q.ERR_ARG
+        assert not h.value
