@@ -781,9 +781,42 @@ def main() -> None:
             t = torch.tensor([e_ms], device=dev, dtype=torch.float64)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e_ms = float(t.item())
+        # the link bound of the same step: its copies alone, in the same chunks, both directions at once
+        cin, cout = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+        dx = torch.empty(E2E_CHUNK * max(ly["k"] for ly in layers), dtype=torch.bfloat16, device=dev)
+        do = torch.empty(E2E_CHUNK * max(ly["n"] for ly in layers), dtype=torch.bfloat16, device=dev)
+
+        def copies_only():
+            cin.wait_stream(stream)
+            cout.wait_stream(stream)
+            for h, ly in zip(host_x, layers):
+                flat = h.view(-1)
+                with torch.cuda.stream(cin):
+                    for r0 in range(0, M, E2E_CHUNK):
+                        n_el = (min(M, r0 + E2E_CHUNK) - r0) * ly["k"]
+                        dx[:n_el].copy_(flat[r0 * ly["k"]:r0 * ly["k"] + n_el], non_blocking=True)
+            for h, ly in zip(host_o, layers):
+                flat = h.view(-1)
+                with torch.cuda.stream(cout):
+                    for r0 in range(0, M, E2E_CHUNK):
+                        n_el = (min(M, r0 + E2E_CHUNK) - r0) * ly["n"]
+                        flat[r0 * ly["n"]:r0 * ly["n"] + n_el].copy_(do[:n_el], non_blocking=True)
+            stream.wait_stream(cin)
+            stream.wait_stream(cout)
+
+        copies_only()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(e_steps):
+            copies_only()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        link_ms = e0.elapsed_time(e1) / e_steps
         e2e = {"value": ws_n * ops_per_step(M) / (e_ms * 1e-3) / 1e12, "unit": "TOPS",
                "h2d_bytes_per_step": int(sum(h.numel() * 2 for h in host_x)),
                "d2h_bytes_per_step": int(sum(h.numel() * 2 for h in host_o)), "ms_per_step": e_ms,
+               "link_bound": {"copies_only_ms": link_ms, "frac": link_ms / e_ms,
+                              "note": "the step's copies alone, same chunks, both PCIe directions at once"},
                "path": f"h3q_host_pipeline_run (C ABI), the four linears as one batch: pinned host input and output, "
                        f"{E2E_CHUNK}-row chunks, {E2E_IN_SLOTS} input chunk buffers, "
                        "whose copies in and out overlap the GEMMs, copies inside the timed region"}
