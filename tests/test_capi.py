@@ -104,3 +104,13 @@ def test_host_pipeline_slot_counts_are_checked():
     for ins, outs in ((1, 2), (2, 1), (2, 5000)):
         assert L.h3q_host_pipeline_create_ex(256, 1024, 1024, ins, outs, ctypes.byref(h)) == h3q.ERR_ARG
         assert not h.value
+
+
+def test_host_pipeline_run_argument_checks():
+    """h3q_host_pipeline_run rejects a null pipeline before touching the device, and its item layout matches
+    include/h3q.h (eleven fields, 8-byte aligned, two trailing ints)."""
+    L = h3q.lib()
+    item = h3q.HostLinear()
+    assert L.h3q_host_pipeline_run(None, ctypes.byref(item), 1, None) == h3q.ERR_ARG
+    assert ctypes.sizeof(h3q.HostLinear) == 9 * 8 + 2 * 4
+    assert h3q.HostLinear.rotate.offset == 9 * 8 + 4
