@@ -24,8 +24,10 @@ from __future__ import annotations
 
 from dataclasses import dataclass
 
-from . import (EPI_GATE_RESID, EPI_LINEAR, EPI_SWIGLU_PAIRS, attend_qkv, gate_add, gemm_s8, gemm_s8_quantized,
-               quant_rows, rms_modulate, rms_modulate_quant)
+from . import (EPI_GATE_RESID, EPI_LINEAR, EPI_SWIGLU_PAIRS, attend_qkv, attention_qkv, gate_add, gemm_s8,
+               gemm_s8_quantized, qk_norm_rope, quant_rows, rms_modulate, rms_modulate_quant)
+
+ATTN_QKV_BUDGET = 1_500_000_000   # bytes of bf16 qkv above which the reference splits the attention (dit.rs:361)
 
 
 @dataclass
@@ -67,12 +69,61 @@ class StepCtx:
     flags: int = 0
 
 
-def run_block_ops(x, b: Block, cx: StepCtx, trace: dict | None = None):
+def attn_groups(tokens: int, heads: int, hidden: int, override: int | None = None) -> int:
+    """Dit::attn_groups (dit.rs:762-773): 1 while the bf16 qkv (3 * tokens * hidden * 2 bytes) fits the budget,
+    else the smallest divisor of heads that is at least the number of budgets it needs.  override plays the
+    H3_ATTN_GROUPS variable: a divisor of heads is taken as is, anything else gives 1."""
+    if override is not None:
+        return override if override >= 1 and heads % override == 0 else 1
+    qkv_bytes = 3 * tokens * hidden * 2
+    if qkv_bytes <= ATTN_QKV_BUDGET:
+        return 1
+    want = -(-qkv_bytes // ATTN_QKV_BUDGET)
+    return next((g for g in range(want, heads + 1) if heads % g == 0), heads)
+
+
+def attend_grouped(n1, b: Block, cx: StepCtx, groups: int):
+    """Dit::attend_grouped (dit.rs:778-801): the qkv projection and the attention `groups` head groups at a time,
+    so that no more than a group's q, k and v exist at once.  Per group g: the q, k and v row blocks of the qkv
+    weight (rows g w .. (g + 1) w of each third, w = heads / groups * 128) through gemm_s8, q / k RMSNorm + RoPE,
+    then attention_qkv with V at column 0 of its own block; the groups' outputs side by side.  Every output column
+    of the GEMM and every head of the attention is computed on its own here, so the result has the bits of the
+    ungrouped qkv GEMM + attend_qkv."""
+    import torch
+    h, d = b.heads, 128
+    inner = h * d
+    hg = h // groups
+    w = hg * d
+
+    def proj(base: int, g: int):
+        r0 = base + g * w
+        ws = b.qkv.ws if b.qkv.ws.numel() == 1 else b.qkv.ws[r0:r0 + w]
+        bias = None if b.qkv.bias is None else b.qkv.bias[r0:r0 + w]
+        return gemm_s8(n1, b.qkv.w[r0:r0 + w], ws, bias, swiglu=False, rotate=True)
+
+    outs = []
+    for g in range(groups):
+        q = qk_norm_rope(proj(0, g), 0, hg, d, (b.q_norm, b.eps), cx.rope, cx.rot)
+        k = qk_norm_rope(proj(inner, g), 0, hg, d, (b.k_norm, b.eps), cx.rope, cx.rot)
+        vt = proj(2 * inner, g)
+        outs.append(attention_qkv(q, k, vt, 0, cx.flags).reshape(n1.shape[0], w))
+    return outs[0] if groups == 1 else torch.cat(outs, dim=1)
+
+
+def run_block_ops(x, b: Block, cx: StepCtx, trace: dict | None = None, groups: int | None = None):
     """The block as the reference issues it (dit.rs:981-1017), one library call per reference call.  With a dict
-    as trace, each intermediate is kept in it under the reference's name (n1, qkv, att, o, x1, n2, h, m, y)."""
+    as trace, each intermediate is kept in it under the reference's name (n1, qkv, att, o, x1, n2, h, m, y).
+    groups: the attention's head groups (attn_groups of the token count when None); above 1 the qkv projection
+    and the attention run group by group (attend_grouped) and trace holds no qkv."""
     n1 = rms_modulate(x, b.norm1, b.eps, cx.scale_msa, cx.shift_msa, cx.idx)
-    qkv = gemm_s8(n1, b.qkv.w, b.qkv.ws, b.qkv.bias, swiglu=False, rotate=True)
-    att = attend_qkv(qkv, b.heads, (b.q_norm, b.k_norm), b.eps, cx.rope, cx.rot, cx.flags)
+    if groups is None:
+        groups = attn_groups(x.shape[0], b.heads, x.shape[1])
+    if groups > 1:
+        qkv = None
+        att = attend_grouped(n1, b, cx, groups)
+    else:
+        qkv = gemm_s8(n1, b.qkv.w, b.qkv.ws, b.qkv.bias, swiglu=False, rotate=True)
+        att = attend_qkv(qkv, b.heads, (b.q_norm, b.k_norm), b.eps, cx.rope, cx.rot, cx.flags)
     o = gemm_s8(att, b.out.w, b.out.ws, b.out.bias, swiglu=False, rotate=True)
     x1 = gate_add(x, o, cx.gate_msa, cx.idx)
     n2 = rms_modulate(x1, b.norm2, b.eps, cx.scale_mlp, cx.shift_mlp, cx.idx)
@@ -99,4 +150,4 @@ def run_block(x, b: Block, cx: StepCtx):
                              gate_idx=cx.idx, resid=x)
 
 
-__all__ = ["Linear", "Block", "StepCtx", "run_block", "run_block_ops"]
+__all__ = ["Linear", "Block", "StepCtx", "attn_groups", "attend_grouped", "run_block", "run_block_ops"]

@@ -125,3 +125,19 @@ def test_block_chain_is_deterministic(cuda):
     y2 = D.run_block(D.run_block(x, blk, cx), blk, cx)
     assert torch.equal(y1.view(torch.int16), y2.view(torch.int16))
     assert bool(torch.isfinite(y1.float()).all())
+
+
+@pytest.mark.parametrize("groups", [2, 4])
+def test_grouped_attention_equals_ungrouped(cuda, groups):
+    """Dit::attend_grouped (dit.rs:778-801): the qkv projection and attention head group by head group give the
+    bits of the whole qkv GEMM + attend_qkv, and the block run that way the bits of the fused block."""
+    S, H, F = 300, 4, 512
+    x, blk, cx = _device(_inputs(7 + groups, S, H, F), H, cuda)
+    n1 = h3q.rms_modulate(x, blk.norm1, blk.eps, cx.scale_msa, cx.shift_msa, cx.idx)
+    qkv = h3q.gemm_s8(n1, blk.qkv.w, blk.qkv.ws, blk.qkv.bias, swiglu=False, rotate=True)
+    whole = h3q.attend_qkv(qkv, H, (blk.q_norm, blk.k_norm), blk.eps, cx.rope, cx.rot, cx.flags).reshape(S, -1)
+    grouped = D.attend_grouped(n1, blk, cx, groups)
+    assert torch.equal(grouped.view(torch.int16), whole.view(torch.int16))
+    y = D.run_block_ops(x, blk, cx, groups=groups)
+    assert torch.equal(y.view(torch.int16), D.run_block(x, blk, cx).view(torch.int16))
+    assert h3q.device_status() == 0
