@@ -18,7 +18,8 @@ per token by idx [S]):
 library offers: the modulation feeds the quantizer directly (h3q_rms_modulate_quant: no bf16 round trip of n1 / n2),
 the SwiGLU runs in the fc1 GEMM's epilogue, and each gate_add runs in the out / fc2 GEMM's epilogue (the gated
 residual epilogue).  Both give the same bits.  The adaLN projection that produces the tables (dit.rs:976) and the
-block's LoRA handling stay with the caller.
+block's LoRA handling stay with the caller.  ControlNet blocks run the same block (control.rs:180).  Above a 1.5 GB
+qkv the reference projects and attends head group by head group (attn_groups / attend_grouped, dit.rs:762-801).
 """
 from __future__ import annotations
 
