@@ -137,10 +137,14 @@ h3q_status h3q_init(int device) {
   if (cudaGetDevice(&prev) != cudaSuccess) return fail(H3Q_ERR_CUDA, "%s: no device", what);
   if (cudaSetDevice(device) != cudaSuccess) return fail(H3Q_ERR_ARG, "%s: bad device %d", what, device);
   // the per-device state the entry points otherwise create on their first call: the device error word (a 4-byte
-  // allocation) and the SM count the persistent kernels size their grids by
+  // allocation), the SM count the persistent kernels size their grids by, and the fixed scratch array of
+  // h3q_gemm_s8_static (its module loads lazily, so the array is reserved here rather than at that entry
+  // point's first call, when the caller may already have taken the rest of the GPU's memory)
   h3q_status st = H3Q_OK;
   if (!h3q::error_word_current()) st = fail(H3Q_ERR_CUDA, "%s: could not set up the device error word", what);
   h3q::sm_count(device);
+  if (st == H3Q_OK && !h3q::static_status_word_current())
+    st = fail(H3Q_ERR_CUDA, "%s: could not reserve the static scratch array on device %d", what, device);
   cudaSetDevice(prev);
   return st;
 }

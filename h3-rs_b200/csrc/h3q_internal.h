@@ -50,5 +50,8 @@ cudaError_t launch_gemm_i8_allgather(const int8_t* A, const int8_t* B, const Gem
 int sm_count(int device);
 // the per-device error word kernels latch bounded-wait time-outs into (allocated once per device)
 int* error_word_current();
+// the status word of h3q_gemm_s8_static's fixed scratch array on the current device (reserving the array there on
+// the first look-up), or null
+int* static_status_word_current();
 
 }  // namespace h3q

@@ -23,6 +23,7 @@ enum DeviceError : int {
   kDevTimeoutProbs = 7,    // attention: MMA warp waited too long for a probability tile
   kDevTimeoutScale = 8,    // attention: softmax warps waited too long for the key scales
   kDevTimeoutPV = 9,       // attention: softmax warps waited too long for the P.V product
+  kDevTimeoutSelftest = 10, // h3q_selftest_wait_timeout: the wait that is made to run out
 };
 
 // ------------------------------------------------------------------------------------------------ numbers

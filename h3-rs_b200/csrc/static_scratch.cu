@@ -4,18 +4,25 @@
 // Some callers cannot allocate device memory at all: a plugin inside a host process that has already reserved
 // the GPU's whole memory for its own pool, or code on a path where cudaMalloc's implicit device synchronisation
 // and possible failure under memory pressure are not acceptable.  For them this file keeps that scratch in one
-// fixed, file-scope device array (kStaticScratchBytes, allocated by the driver when the library's module is
-// loaded and held on every GPU that loads the library until the process exits).  The entry point itself calls no
-// cudaMalloc, cudaFree or allocating library routine.
+// fixed, file-scope device array of kStaticScratchBytes.  The CUDA runtime loads this file's module lazily, so
+// the array is reserved on a device the first time its address is looked up there: by h3q_init(device) or by the
+// first h3q_gemm_s8_static call on that device.  It is then held until the process exits.  The entry point
+// itself calls no cudaMalloc, cudaFree or allocating library routine.
 //
 // Rules for callers:
-//   * The first call on a device looks up the array's device address (cudaGetSymbolAddress, once per device,
-//     with that device current).  Make that first call before any stream capture.
+//   * Call h3q_init(device) before taking the GPU's memory for another pool, so the array is reserved while
+//     there is room for it.  Without it, the first h3q_gemm_s8_static call on a device reserves it.  Either
+//     call looks the array's device address up (cudaGetSymbolAddress, once per device, with that device
+//     current); make it before any stream capture.
+//   * The looked-up address is kept for the life of the process: a device reset (cudaDeviceReset) after it is
+//     not supported.
 //   * Every call on a device shares the one array and leaves its contents behind; calls whose work overlaps
 //     on the GPU (different streams without ordering between them) race on it.
 //   * A problem whose codes and scales need more than the array holds is rejected with H3Q_ERR_ARG.
-//   * A kernel that gives up a bounded wait latches its code into the array's status word (cleared at the start
-//     of each call), not into the word h3q_device_status reads.
+//   * A kernel that gives up a bounded wait latches its code into the array's own status word, not into the
+//     word h3q_device_status reads.  The word is sticky: calls never clear it.
+//     h3q_gemm_s8_static_status(device, &code) synchronises the device, reads it, clears it and returns
+//     H3Q_ERR_TIMEOUT when it was set.
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
@@ -73,6 +80,37 @@ h3q_status scratch_on_current_device(uint8_t** out) {
 
 }  // namespace
 
+namespace h3q {
+// The static-scratch status word on the current device (the array's first 4 bytes), reserving the array there if
+// this is the first look-up; null when the look-up fails.
+int* static_status_word_current() {
+  uint8_t* base = nullptr;
+  if (scratch_on_current_device(&base) != H3Q_OK) return nullptr;
+  return reinterpret_cast<int*>(base);
+}
+}  // namespace h3q
+
+extern "C" h3q_status h3q_gemm_s8_static_status(int device, int* code) {
+  using namespace h3q;
+  const char* what = "h3q_gemm_s8_static_status";
+  if (code) *code = 0;
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess) return fail(H3Q_ERR_CUDA, "%s: no device", what);
+  if (cudaSetDevice(device) != cudaSuccess) return fail(H3Q_ERR_ARG, "%s: bad device %d", what, device);
+  int v = 0;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(&v, g_static_scratch, sizeof(int), 0, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && v) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_static_scratch, &zero, sizeof(int), 0, cudaMemcpyHostToDevice);
+  }
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) return fail(H3Q_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  if (code) *code = v;
+  if (v) return fail(H3Q_ERR_TIMEOUT, "a kernel of h3q_gemm_s8_static on device %d gave up waiting (code %d)", device, v);
+  return H3Q_OK;
+}
+
 extern "C" h3q_status h3q_gemm_s8_static(const uint16_t* x, const int8_t* w, const float* ws, int64_t ws_numel,
                                          const float* bias, uint16_t* out, int64_t m, int64_t n, int64_t k,
                                          int swiglu, int rotate, void* stream) {
@@ -85,6 +123,10 @@ extern "C" h3q_status h3q_gemm_s8_static(const uint16_t* x, const int8_t* w, con
   if (rotate && k / 256 > 64)
     return fail(H3Q_ERR_UNSUPPORTED, "%s: the rotated quantizer handles k <= 16384 (k = %lld)", what, (long long)k);
   if (m == 0 || n == 0) return H3Q_OK;
+  // m * k cannot wrap below: m is bounded by the array's size over k first
+  if (k > 0 && m > (int64_t)(kStaticScratchBytes / (size_t)k))
+    return fail(H3Q_ERR_ARG, "%s: m = %lld rows of k = %lld do not fit the fixed %zu-byte device scratch; use h3q_gemm_s8",
+                what, (long long)m, (long long)k, kStaticScratchBytes);
   const size_t codes = align256((size_t)m * (size_t)k);
   const size_t need = kStatusBytes + codes + 4 * (size_t)m;
   if (need > kStaticScratchBytes)
@@ -104,13 +146,11 @@ extern "C" h3q_status h3q_gemm_s8_static(const uint16_t* x, const int8_t* w, con
   float* xs = reinterpret_cast<float*>(base + kStatusBytes + codes);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
-  // the status word must start at zero; the codes and scales are fully rewritten below
-  cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int), st);
-  if (e == cudaSuccess) {
-    // the quantizer h3q_gemm_s8 selects (kernels.rs:1139): rot2 order for bf16 with k/256 <= 56, else rot order
-    const int order = !rotate ? 0 : (k % 256 == 0 && k / 256 <= 56 ? 2 : 1);
-    e = launch_quant_rows(x, 2, qa, xs, m, k, order, status, st);
-  }
+  // The codes and scales are fully rewritten below.  The status word starts at zero (static storage) and only
+  // h3q_gemm_s8_static_status clears it, so a time-out stays visible until the caller reads it.
+  // The quantizer h3q_gemm_s8 selects (kernels.rs:1139): rot2 order for bf16 with k/256 <= 56, else rot order.
+  const int order = !rotate ? 0 : (k % 256 == 0 && k / 256 <= 56 ? 2 : 1);
+  cudaError_t e = launch_quant_rows(x, 2, qa, xs, m, k, order, status, st);
   if (e == cudaSuccess) {
     GemmArgs g{};
     g.M = m; g.N = n; g.K = k;

@@ -100,6 +100,8 @@ SIGNATURES = {
     "h3q_dequant_nvfp4": (_int, [_vp, _vp, _vp, _vp, _int, _i64, _i64, _vp]),
     "h3q_gate_add": (_int, [_vp, _vp, _int, _vp, _vp, _vp, _i64, _i64, _vp]),
     "h3q_gemm_s8_static": (_int, [_vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _int, _int, _vp]),
+    "h3q_gemm_s8_static_status": (_int, [_int, ctypes.POINTER(_int)]),
+    "h3q_selftest_wait_timeout": (_int, [_int, ctypes.c_uint64, _vp, _vp]),
     "h3q_nvfp4_linear_workspace_size": (_sz, [_i64, _i64, _i64, _int]),
     "h3q_nvfp4_linear": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),
     "h3q_default_switches": (Switches, []),

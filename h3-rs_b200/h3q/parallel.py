@@ -216,5 +216,92 @@ def sharded_attention(q_local, k_local, v_local, total: int, group=None, flags: 
     return rows_op(q_local, k_full, v_full, flags)
 
 
+class RankLeft(RuntimeError):
+    """A rank announced that it left the job (RankMonitor.leave)."""
+
+    def __init__(self, rank: int, reason: str):
+        super().__init__(f"rank {rank} left the job: {reason}")
+        self.rank = rank
+
+
+class RankLost(RuntimeError):
+    """A rank did not reach a step within the monitor's time limit and did not say why."""
+
+    def __init__(self, ranks, step: int, timeout: float):
+        super().__init__(f"rank(s) {list(ranks)} did not reach step {step} within {timeout:.1f} s")
+        self.ranks = list(ranks)
+
+
+class JobCancelled(RuntimeError):
+    """Some rank cancelled the job (RankMonitor.cancel_all)."""
+
+
+class RankMonitor:
+    """Between-step failure detection for one multi-GPU job, on the host only.
+
+    The reference runs on one GPU and checks for cancellation between steps and blocks (progress::check,
+    progress.rs:102-107, called per block at dit.rs:1164; cancel_all bumps a generation, progress.rs:87-89).  With
+    several ranks a step's collectives would wait for a rank that has gone, so before issuing a step's kernels and
+    collectives every rank calls ready(step):
+
+      * it publishes its own heartbeat (the step number) in the job's key-value store (torch.distributed's store:
+        TCPStore between processes);
+      * it raises JobCancelled if any rank called cancel_all() since this monitor was made;
+      * it raises RankLeft if a rank called leave();
+      * it waits until every rank has published a heartbeat of at least `step`, and raises RankLost for the ranks
+        still missing after `timeout` seconds.
+
+    cancel_all() and leave() are called between steps, before the caller's next ready(); since every rank waits
+    for every heartbeat of a step and then looks once more, all ranks raise at the same step.
+
+    Every surviving rank therefore learns of a departure before its next launch, with no kernel or collective of
+    that step in flight.  A rank leaves only between steps.  A rank that dies inside a step is caught by the
+    process group's own (short) timeout in the collective it left behind."""
+
+    def __init__(self, store, rank: int, world: int, prefix: str = "h3q/monitor", timeout: float = 10.0,
+                 poll: float = 0.01):
+        self.store, self.rank, self.world = store, rank, world
+        self.prefix, self.timeout, self.poll = prefix, float(timeout), float(poll)
+        self.gen = int(self.store.add(f"{prefix}/gen", 0))
+
+    def _beat_key(self, r: int) -> str:
+        return f"{self.prefix}/beat/{r}"
+
+    def _left_key(self, r: int) -> str:
+        return f"{self.prefix}/left/{r}"
+
+    def _raise_if_stopped(self) -> None:
+        if int(self.store.add(f"{self.prefix}/gen", 0)) != self.gen:
+            raise JobCancelled("the job was cancelled")
+        for r in range(self.world):
+            if r != self.rank and self.store.check([self._left_key(r)]):
+                raise RankLeft(r, self.store.get(self._left_key(r)).decode(errors="replace"))
+
+    def ready(self, step: int) -> None:
+        import time
+        self.store.set(self._beat_key(self.rank), str(int(step)))
+        deadline = time.monotonic() + self.timeout
+        missing = [r for r in range(self.world) if r != self.rank]
+        while True:
+            self._raise_if_stopped()
+            missing = [r for r in missing
+                       if not (self.store.check([self._beat_key(r)]) and
+                               int(self.store.get(self._beat_key(r))) >= step)]
+            if not missing:
+                # a rank cancels or leaves before it publishes its next heartbeat, so once every heartbeat of this
+                # step is visible, one more look sees any cancellation made ahead of it: all ranks agree
+                self._raise_if_stopped()
+                return
+            if time.monotonic() > deadline:
+                raise RankLost(missing, step, self.timeout)
+            time.sleep(self.poll)
+
+    def leave(self, reason: str = "left") -> None:
+        self.store.set(self._left_key(self.rank), reason)
+
+    def cancel_all(self) -> None:
+        self.store.add(f"{self.prefix}/gen", 1)
+
+
 __all__ = ["row_range", "nsplit_range", "gather_rows", "gather_full", "gather_columns", "PeerBuffers", "NSplitLinear",
-           "sharded_attention", "H3QError"]
+           "sharded_attention", "H3QError", "RankMonitor", "RankLeft", "RankLost", "JobCancelled"]

@@ -54,9 +54,19 @@ int h3q_available_arch(int device);
 
 /* Per-device set-up, once per device and optional: creates the state the entry points otherwise create on their
  * first call on a device (the device error word, a 4-byte allocation, and the SM count), so that the first call
- * of an entry point does not allocate it.  H3Q_ERR_UNSUPPORTED on a device that is not an sm_100 GPU.  Safe to
- * call again. */
+ * of an entry point does not allocate it, and reserves the fixed 64 MiB scratch array of h3q_gemm_s8_static on
+ * the device (the array's module loads lazily; call h3q_init before another pool takes the GPU's memory).
+ * H3Q_ERR_UNSUPPORTED on a device that is not an sm_100 GPU.  Safe to call again. */
 h3q_status h3q_init(int device);
+
+/* Failure-path self-test (no counterpart in the reference; the reference's kernels have no device-side error
+ * reporting).  Launches one CTA with the roles of a pipeline kernel that waits on a barrier nothing completes:
+ * its producer's wait gives up after `limit_ns` (0 < limit_ns <= 1e9) through the same bounded-wait code every
+ * kernel of the library uses, the other roles leave on the CTA's abort flag, TMEM is freed and the kernel
+ * returns.  The time-out is latched into the device error word (target 0, read by h3q_device_status) or the
+ * static-scratch status word (target 1, read by h3q_gemm_s8_static_status).  `done` (device int, zeroed by the
+ * caller, or NULL) receives 1 when the CTA reached its exit path plus 2 when the producer's wait gave up. */
+h3q_status h3q_selftest_wait_timeout(int target, uint64_t limit_ns, int* done, void* stream);
 
 /* kernels::can_fuse_rotation (kernels.rs:1081-1085): whether the rotation fuses into the quantizer for an
  * input width k and ConvRot group size.  Always on here (group 256, k % 256 == 0, k / 256 <= 64); the
@@ -478,14 +488,22 @@ h3q_status h3q_gemm_s8_allgather(const int8_t* a, const float* xs, const int8_t*
  * cannot call cudaMalloc: a plugin inside a host that has already reserved the GPU's whole memory for its own
  * pool, or code where cudaMalloc's implicit synchronisation or failure under memory pressure is not acceptable.
  * This entry point takes no workspace: the quantized activations live in a fixed 64 MiB device array inside the
- * library, held on every GPU that loads the library until the process exits, and the call allocates nothing.
- * Same arguments and results as h3q_gemm_s8 (bit-identical outputs).  Limits: 256 + roundup(m*k, 256) + 4*m
- * bytes must fit in the 64 MiB (else H3Q_ERR_ARG); the first call on a device looks up the array's address and
- * should come before any stream capture; all calls on a device share the array, so calls that overlap on the GPU
- * race; kernel time-outs are latched in the array's own status word, not the one h3q_device_status reads. */
+ * library, and the call allocates nothing.  The array is reserved on a device by h3q_init(device) or, without
+ * it, by the first h3q_gemm_s8_static call there (the array's module loads lazily), and held until the process
+ * exits; call h3q_init first when another pool will take the GPU's memory.  Same arguments and results as
+ * h3q_gemm_s8 (bit-identical outputs).  Limits: 256 + roundup(m*k, 256) + 4*m bytes must fit in the 64 MiB
+ * (else H3Q_ERR_ARG); the array's address is looked up once per device (by h3q_init or the first call), which
+ * should come before any stream capture, and a device reset after it is not supported; all calls on a device
+ * share the array, so calls that overlap on the GPU race.  Kernel time-outs are latched in the array's own
+ * status word (sticky: no call clears it), read with h3q_gemm_s8_static_status. */
 h3q_status h3q_gemm_s8_static(const uint16_t* x, const int8_t* w, const float* ws, int64_t ws_numel,
                               const float* bias, uint16_t* out, int64_t m, int64_t n, int64_t k, int swiglu,
                               int rotate, void* stream);
+
+/* Reads and clears the status word of h3q_gemm_s8_static's scratch array on `device` (no counterpart in the
+ * reference).  Synchronises the device first, allocates nothing.  H3Q_ERR_TIMEOUT (with the kernel's code in
+ * *code) when a kernel of an h3q_gemm_s8_static call gave up a bounded wait since the last read, else H3Q_OK. */
+h3q_status h3q_gemm_s8_static_status(int device, int* code);
 
 #ifdef __cplusplus
 }

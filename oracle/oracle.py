@@ -269,6 +269,60 @@ def nvfp4_linear(x_bf16, q, bs, g, pqs_bf16=None, bias=None, rows=None) -> np.nd
     return f32_to_bf16_bits(y)
 
 
+_E2M1_VALUES = np.array([0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0])
+
+
+def _e4m3_values() -> np.ndarray:
+    """The 127 non-negative finite e4m3 values (bias 7, 3 mantissa bits, subnormals, max 448), in code order."""
+    return np.array([fp8e4m3(c) for c in range(127)], dtype=np.float64)
+
+
+def _round_to_table(a: np.ndarray, table: np.ndarray) -> np.ndarray:
+    """|a| rounded to the nearest entry of an ascending table (ties to the even index, as RNE picks the even
+    mantissa), saturating at the last entry; the sign of a is kept."""
+    m = np.minimum(np.abs(a), table[-1])
+    hi = np.clip(np.searchsorted(table, m), 1, len(table) - 1)
+    lo = hi - 1
+    dlo, dhi = m - table[lo], table[hi] - m
+    pick = np.where(dhi < dlo, hi, np.where(dlo < dhi, lo, np.where(lo % 2 == 0, lo, hi)))
+    return np.sign(a) * table[pick]
+
+
+def nvfp4_quantize_activation(x: np.ndarray, block: int = 16):
+    """NVFP4 quantization of activations [M, K] as the published two-level NVFP4 recipe defines it: one f32
+    global scale gs = amax(x) / (448 * 6), one e4m3 scale per 16 consecutive elements along K,
+    sb = e4m3(amax_block / 6 / gs) (RNE, saturating), and e2m1 values q = e2m1(x / (sb * gs)) (RNE, saturating
+    at +-6).  The reference has no activation quantizer for this layer (weights.rs:612-635 multiplies bf16
+    activations); this is what a W4A4 kernel (tcgen05 kind::mxf4nvf4) would need.  Returns the dequantized
+    activations q * sb * gs (f64)."""
+    x = np.asarray(x, dtype=np.float64)
+    M, K = x.shape
+    amax = float(np.max(np.abs(x)))
+    if amax == 0.0:
+        return np.zeros_like(x)
+    gs = amax / (448.0 * 6.0)
+    xb = x.reshape(M, K // block, block)
+    sb = _round_to_table(np.max(np.abs(xb), axis=2) / 6.0 / gs, _e4m3_values())
+    den = (sb * gs)[:, :, None]
+    q = _round_to_table(np.divide(xb, den, out=np.zeros_like(xb), where=den > 0), _E2M1_VALUES)
+    return (q * den).reshape(M, K)
+
+
+def nvfp4_linear_w4a4(x_bf16, q, bs, g, pqs_bf16=None, bias=None, rows=None) -> np.ndarray:
+    """The NVFP4 linear with the AWQ-scaled activations also quantized to NVFP4 (nvfp4_quantize_activation):
+    y = bf16(Q(bf16(x * pqs)) W^T) + bias, with the same weight decode and roundings as nvfp4_linear.  Used to
+    measure how far W4A4 moves the layer from the reference's W4A16 result.  bf16 bits out."""
+    x = bf16_bits_to_f32(x_bf16 if rows is None else x_bf16[rows])
+    if pqs_bf16 is not None:
+        x = bf16_round(x * bf16_bits_to_f32(pqs_bf16)[None, :])
+    xq = nvfp4_quantize_activation(x)
+    w = bf16_bits_to_f32(dequant_nvfp4(q, bs, float(g), 2))
+    y = bf16_round((xq @ w.astype(np.float64).T).astype(np.float32))
+    if bias is not None:
+        y = bf16_round(y + bf16_round(np.asarray(bias, dtype=np.float32))[None, :])
+    return f32_to_bf16_bits(y)
+
+
 def gate_add(x, y, kind: int, gate, idx) -> np.ndarray:
     """kernels.rs:418-428."""
     x = np.ascontiguousarray(x)
