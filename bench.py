@@ -7,9 +7,13 @@ quantization kernel, then the tcgen05 int8 GEMM with its fused scale/bias epilog
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
---impl reference times the reference's CPU path for the same linears (rotate -> dequantise -> float matmul,
-portable/kernels.rs:220-242) on the host cores, on a bounded row sample.  Under torchrun every rank runs its own
-32760-token shard (weak scaling, no collective on the data path); times are CUDA events, max over ranks.
+Under torchrun the step's 32760 tokens are split over the ranks (BASELINE config 4's M sharding, 4095 tokens per
+GPU at 8 GPUs; strong scaling, weights replicated, no collective on the data path); times are CUDA events, max
+over ranks.  The same line carries, at N > 1, the weak-scaling run (32760 tokens per GPU), the N-split linears and
+the query-sharded attention, each checked against the single-GPU result; at N = 1, the other configs (c2, c3, c4's
+attention), the DiT call sites and the cuBLASLt comparator.  --impl reference times the reference's CPU path for
+the same linears (rotate -> dequantise -> float matmul, portable/kernels.rs:220-242) on the host cores over the
+whole 32760-token workload.
 """
 from __future__ import annotations
 
@@ -134,7 +138,7 @@ def cpu_baseline(rows: int = 4096) -> dict:
     import numpy as np
     from oracle import oracle as O
     rng = np.random.default_rng(0)
-    cores = os.cpu_count() or 1
+    cores = _blas_threads()
     t_full, t_deq, t_rows_s = 0.0, 0.0, 0.0
     for _, k, n in LINEARS:
         w = rng.integers(-127, 128, size=(n, k), dtype=np.int8)
@@ -158,32 +162,91 @@ def cpu_baseline(rows: int = 4096) -> dict:
             "seconds": t_deq + t_rows_s}
 
 
+def _blas_threads() -> int:
+    """Every host core for numpy's BLAS, whatever OMP_NUM_THREADS the launcher set (torchrun sets 1)."""
+    cores = os.cpu_count() or 1
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(cores)
+    except ImportError:
+        pass
+    return cores
+
+
 def run_reference(args) -> None:
-    """--impl reference: the reference's CPU implementation of the path (oracle port; the Rust crate cannot be
-    built here) on this host's cores, same metric, unit and workload; rank 0 only."""
+    """--impl reference: the reference's CPU implementation of the path (oracle port of portable/kernels.rs:220-242,
+    the Rust crate cannot be built here) on this host's cores, same metric, unit and workload; rank 0 only.
+
+    The timed region is one whole reference call per linear over all 32760 tokens, nothing extrapolated: each
+    linear's weight is dequantised once (as one call over the batch does), then the rows are rotated and
+    multiplied.  The K timed steps split the rows into K consecutive slices of every linear (the dequantisation
+    falls in the first step), so ms_per_step x K is the measured time of the full pass.  The W warm-up steps run
+    64-row slices and are not timed."""
+    import numpy as np
+    from oracle import oracle as O
     ws, rank, _ = dist_env()
     if rank != 0:
         return
-    samples = [cpu_baseline() for _ in range(max(1, min(args.steps, 3)))]
-    value = statistics.median(s["value"] for s in samples)
-    cb = dict(samples[0])
-    cb["value"] = value
-    cb.pop("seconds", None)
+    cores = _blas_threads()
+    rng = np.random.default_rng(0)
+    layers = []
+    for _, k, n in LINEARS:
+        w = rng.integers(-127, 128, size=(n, k), dtype=np.int8)
+        wsc = (rng.random(n, dtype=np.float32) * 9e-3 + 1e-3).astype(np.float32)
+        b = O.bf16_round((rng.standard_normal(n) * 0.02).astype(np.float32))
+        x = rng.standard_normal((M_TOKENS, k), dtype=np.float32)
+        x[:, rng.choice(k, 8, replace=False)] *= 20.0
+        layers.append((w, wsc, b, O.f32_to_bf16_bits(x)))
+        del x
+    for _ in range(args.warmup):
+        for w, wsc, b, x in layers:
+            O.cpu_linear_rows(x[:64], O.cpu_dequant_weight(w[:256], wsc[:256]), b[:256], rotate=True)
+    steps = max(1, args.steps)
+    bounds = [M_TOKENS * s // steps for s in range(steps + 1)]
+    deq = [None] * len(layers)
+    t_deq = 0.0
+    t0 = time.perf_counter()
+    for s in range(steps):
+        for i, (w, wsc, b, x) in enumerate(layers):
+            if deq[i] is None:
+                t1 = time.perf_counter()
+                deq[i] = O.cpu_dequant_weight(w, wsc)
+                t_deq += time.perf_counter() - t1
+            O.cpu_linear_rows(x[bounds[s]:bounds[s + 1]], deq[i], b, rotate=True)
+    total = time.perf_counter() - t0
+    value = ops_per_step(M_TOKENS) / total / 1e12
+    cb = {"value": value, "unit": "TOPS", "cores": cores, "kind": "port",
+          "sample": f"the whole workload, unextrapolated: one reference call per linear over all {M_TOKENS} tokens "
+                    f"(weight dequantisation {t_deq:.1f} s, single-threaded like portable/kernels.rs:14-27; rotate + "
+                    f"matmul with numpy BLAS on {cores} threads), split into {steps} row slices, {total:.1f} s "
+                    f"in total"}
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": ws, "steps": len(samples),
-        "warmup": 0, "ms_per_step": 1e3 * ops_per_step(M_TOKENS) / (value * 1e12), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config_block(ws),
-        "cpu_baseline": cb,
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": ws, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * total / steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_block(ws), "cpu_baseline": cb,
         "e2e": {"value": value, "unit": "TOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
 def config_block(n_gpus: int) -> dict:
-    return {"workload": WORKLOAD, "M_per_gpu": M_TOKENS, "linears": [f"{nm}:{k}x{n}" for nm, k, n in LINEARS],
+    m_r = [hi - lo for lo, hi in (row_range(M_TOKENS, n_gpus, r) for r in range(n_gpus))]
+    par = ("x1: all 32760 tokens on one GPU" if n_gpus == 1 else
+           f"token-sharded x{n_gpus} (strong: the 32760 tokens split over the GPUs, {min(m_r)}-{max(m_r)} per GPU, "
+           "weights replicated, no collective)")
+    return {"workload": WORKLOAD, "M_total": M_TOKENS, "M_per_gpu": max(m_r),
+            "linears": [f"{nm}:{k}x{n}" for nm, k, n in LINEARS],
             "rotate": "ConvRot Hadamard-256, fused into the quantizer", "epilogue": "xs*ws*acc + bias -> bf16",
-            "l2": "no flush: every activation (335-905 MB) and output is larger than the 126 MB L2",
-            "parallelism": f"token-sharded x{n_gpus} (weak: 32760 tokens per GPU, weights replicated, no collective)"}
+            "l2": "no flush: at 32760 tokens every activation (335-905 MB) and output is larger than the 126 MB L2; "
+                  "at 4095 tokens per GPU a step's inputs (247 MB of weights plus 240 MB of activations) and "
+                  "outputs (323 MB) are over six times L2, so nothing a linear reads survives to its next run",
+            "parallelism": par}
+
+
+def row_range(total: int, world: int, rank: int) -> tuple[int, int]:
+    """Rows of rank r: [floor(r total / g), floor((r + 1) total / g)) (h3q.parallel.row_range)."""
+    return total * rank // world, total * (rank + 1) // world
 
 
 # --------------------------------------------------------------------------------------------- our arm
@@ -479,6 +542,128 @@ def dit_block_c4(dev, reps: int = 3, S: int = 32760, H: int = 40, F: int = 13824
     return res
 
 
+def make_layers(M: int, dev, rank: int = 0) -> list:
+    """The four c1 linears with M activation rows: weights from one seed shared by every rank (replicated),
+    activations ~N(0, 1) with 8 outlier channels x20 from a per-rank seed."""
+    import torch
+    gw = torch.Generator(device=dev).manual_seed(1234)
+    gx = torch.Generator(device=dev).manual_seed(4321 + rank)
+    layers = []
+    for name, k, n in LINEARS:
+        x = torch.randn((M, k), generator=gx, device=dev)
+        oc = torch.randperm(k, generator=gx, device=dev)[:8]
+        x[:, oc] *= 20.0
+        x = x.to(torch.bfloat16)
+        w = torch.randint(-127, 128, (n, k), generator=gw, device=dev, dtype=torch.int8)
+        wsc = torch.rand(n, generator=gw, device=dev) * 9e-3 + 1e-3
+        b = (torch.randn(n, generator=gw, device=dev) * 0.02).to(torch.bfloat16).float()
+        layers.append(dict(name=name, k=k, n=n, m=M, x=x, w=w, ws=wsc, b=b,
+                           q=torch.empty((M, k), dtype=torch.int8, device=dev),
+                           xs=torch.empty(M, dtype=torch.float32, device=dev),
+                           out=torch.empty((M, n), dtype=torch.bfloat16, device=dev)))
+    return layers
+
+
+def run_linear(L, ly, sp) -> None:
+    """One c1 linear through the C ABI: the rotated quantizer, then the GEMM with the linear epilogue."""
+    import h3q
+    h3q.check(L.h3q_quant_rows_i8(ly["x"].data_ptr(), 2, ly["q"].data_ptr(), ly["xs"].data_ptr(), ly["m"], ly["k"],
+                                  1, sp))
+    h3q.check(L.h3q_gemm_s8_quantized(ly["q"].data_ptr(), ly["xs"].data_ptr(), ly["w"].data_ptr(),
+                                      ly["ws"].data_ptr(), ly["n"], ly["b"].data_ptr(), ly["out"].data_ptr(),
+                                      2, ly["m"], ly["n"], ly["k"], h3q.EPI_LINEAR, None, None, None, sp))
+
+
+def tile_waves(M: int, N: int, units: int = 74) -> dict:
+    """How a linear's 256 x 256 GEMM tiles fill the persistent grid (one CTA pair per tile, `units` pairs)."""
+    tiles = -(-M // 256) * -(-N // 256)
+    waves = -(-tiles // units)
+    return {"tiles": tiles, "waves": round(tiles / units, 2), "wave_efficiency": round(tiles / (waves * units), 3)}
+
+
+def time_steps(fn, reps: int, dev) -> float:
+    """CUDA-event ms per call of fn (after two untimed calls)."""
+    import torch
+    for _ in range(2):
+        fn()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    return e0.elapsed_time(e1) / reps
+
+
+def c2_block(dev, peaks: dict, reps: int = 5) -> dict:
+    """the fused-epilogue DiT linears at M = 65520 (a CFG pair of 32760-token halves sharing the
+    weights).  up-proj 5120 -> 13824 with the GELU-tanh epilogue, whose output is the down-proj's input,
+    13824 -> 5120 with the residual + gate epilogue (gate bf16 per channel ~U(0,1), residual bf16 ~N(0,1)).  Each
+    linear is the rotated quantizer then the GEMM; CUDA-event time per linear."""
+    import torch
+    import h3q
+    M, C, F = 65520, 5120, 13824
+    g = torch.Generator(device=dev).manual_seed(2)
+    x = torch.randn((M, C), generator=g, device=dev)
+    x[:, torch.randperm(C, generator=g, device=dev)[:8]] *= 20.0
+    x = x.to(torch.bfloat16)
+    w1 = torch.randint(-127, 128, (F, C), generator=g, device=dev, dtype=torch.int8)
+    w2 = torch.randint(-127, 128, (C, F), generator=g, device=dev, dtype=torch.int8)
+    ws1, ws2 = (torch.rand(n, generator=g, device=dev) * 9e-3 + 1e-3 for n in (F, C))
+    b1, b2 = ((torch.randn(n, generator=g, device=dev) * 0.02).to(torch.bfloat16).float() for n in (F, C))
+    gate = torch.rand((1, C), generator=g, device=dev).to(torch.bfloat16).float()
+    resid = torch.randn((M, C), generator=g, device=dev).to(torch.bfloat16)
+    up = torch.empty((M, F), dtype=torch.bfloat16, device=dev)
+    down = torch.empty((M, C), dtype=torch.bfloat16, device=dev)
+
+    def up_proj():
+        q, xs = h3q.quant_rows(x, True)
+        h3q.gemm_s8_quantized(q, xs, w1, ws1, b1, h3q.EPI_GELU_TANH, out=up)
+
+    def down_proj():
+        q, xs = h3q.quant_rows(up, True)
+        h3q.gemm_s8_quantized(q, xs, w2, ws2, b2, h3q.EPI_GATE_RESID, gate=gate, resid=resid, out=down)
+
+    res = {}
+    for name, fn, k, n in (("up_gelu", up_proj, C, F), ("down_gate_resid", down_proj, F, C)):
+        ms = time_steps(fn, reps, dev)
+        tops = 2.0 * M * k * n / (ms * 1e-3) / 1e12
+        res[name] = {"linear": f"{k}->{n}", "ms": round(ms, 3), "tops": round(tops, 1),
+                     "frac_of_2x_bf16_burst": round(tops / (2 * peaks["bf16_tflops"]), 3)}
+    res["workload"] = "BASELINE c2: M=65520 (CFG pair), fc1 GELU-tanh epilogue, fc2 residual + gate epilogue"
+    res["note"] = "time per linear includes its rotated quantizer; workspace allocations by torch's caching allocator"
+    res["device_status"] = h3q.device_status(dev.index or 0)
+    return res
+
+
+def gpu_comparators(layers, dev, per_linear, reps: int = 5) -> dict:
+    """The reference's cuBLASLt path on the same GPU, GEMM part: int8 x int8 -> int32 (the H3_GEMM=cublaslt GEMM of
+    kernels.rs:1008-1044; here through torch._int_mm, which issues the same cuBLASLt IMMA: row-major [M, K] codes
+    times the [N, K] weight transposed) at each c1 shape, against this library's GEMM writing the same int32
+    accumulators (H3Q_EPI_ACC_I32) and its fused bf16 epilogue.  The reference adds a separate epilogue kernel
+    reading the int32 result back (kernels.rs:333-373), not timed here; the fused GEMM needs none."""
+    import torch
+    import h3q
+    res = []
+    for ly, pl in zip(layers, per_linear):
+        acc = torch.empty((ly["m"], ly["n"]), dtype=torch.int32, device=dev)
+        wt = ly["w"].t()
+        lt_ms = time_steps(lambda: torch._int_mm(ly["q"], wt), reps, dev)
+        ours_ms = time_steps(lambda: h3q.gemm_s8_quantized(ly["q"], ly["xs"], ly["w"], ly["ws"], None,
+                                                           h3q.EPI_ACC_I32, out=acc), reps, dev)
+        same = bool(torch.equal(torch._int_mm(ly["q"], wt), acc))
+        ops = 2.0 * ly["m"] * ly["k"] * ly["n"]
+        res.append({"linear": f"{ly['name']}:{ly['k']}x{ly['n']}", "cublaslt_int32_ms": round(lt_ms, 4),
+                    "cublaslt_tops": round(ops / (lt_ms * 1e-3) / 1e12, 1),
+                    "ours_int32_ms": round(ours_ms, 4), "ours_int32_tops": round(ops / (ours_ms * 1e-3) / 1e12, 1),
+                    "ours_fused_bf16_ms": pl["gemm_ms"],
+                    "speedup_int32": round(lt_ms / ours_ms, 3), "speedup_vs_fused": round(lt_ms / pl["gemm_ms"], 3),
+                    "same_int32": same})
+        del acc
+    return {"layers": res, "M": layers[0]["m"],
+            "note": "cuBLASLt via torch._int_mm; time of the GEMM only; same_int32 = identical accumulators"}
+
+
 def _max_over_ranks(ms: float, dist, dev) -> float:
     import torch
     t = torch.tensor([ms], device=dev, dtype=torch.float64)
@@ -486,63 +671,86 @@ def _max_over_ranks(ms: float, dist, dev) -> float:
     return float(t.item())
 
 
-def multi_gpu_extras(layers, M: int, dist, dev, reps: int = 3) -> dict:
-    """BASELINE config 4's other partitionings at N > 1 GPUs (all ranks take part; times are CUDA events, max over
-    ranks):
-      nsplit: the four c1 linears with the weight rows split over the ranks and the activations replicated
-              (M = 32760 in total, strong scaling); "fused" is one GEMM per rank writing its column block into
-              every rank's output over NVLink (h3q_gemm_s8_allgather), "nccl" a local GEMM + NCCL all-gather +
-              relayout;
+def multi_gpu_extras(dist, dev, reps: int = 3) -> dict:
+    """At N > 1 GPUs, besides the strong-scaling headline (all ranks take part; times are CUDA events, max over
+    ranks; every result is checked against the single-GPU result on the same rank and `parity` is the AND over
+    ranks and checks):
+      weak:      every rank runs the four c1 linears on its own 32760 tokens (no collective);
+      nsplit:    the four c1 linears with the weight rows split over the ranks and the activations replicated
+                 (M = 32760 in total, strong scaling); "fused" is one GEMM per rank writing its column block into
+                 every rank's output over NVLink (h3q_gemm_s8_allgather), "nccl" a local GEMM + NCCL all-gather +
+                 relayout; each output must equal, bit for bit, the whole linear computed on one GPU (the weak
+                 run's output of the same activations);
       attention: query-sharded c4 attention (S = 32760, H = 40 in total): K/V rows all-gathered, each rank attends
-              its 32760 / N queries (h3q_attention_rows)."""
+                 its 32760 / N queries (h3q_attention_rows); its rows must equal those of the whole-sequence
+                 attention computed on one GPU."""
     import torch
     import h3q
     from h3q import parallel as P
     world = dist.get_world_size()
     rank = dist.get_rank()
+    M = M_TOKENS
+    L = h3q.lib()
+    sp = torch.cuda.current_stream(dev).cuda_stream
+    layers = make_layers(M, dev, rank=0)  # the same activations on every rank (the N split replicates them)
+    checks = {}
+
+    def step_weak():
+        for ly in layers:
+            run_linear(L, ly, sp)
+    step_weak()
+    torch.cuda.synchronize()
+    dist.barrier()
+    ms = _max_over_ranks(time_steps(step_weak, reps, dev), dist, dev)
+    weak = {"ms_per_step": round(ms, 3), "tops": round(world * ops_per_step(M) / (ms * 1e-3) / 1e12, 1),
+            "note": "32760 tokens per GPU, value = all ranks' ops / max time"}
+    rows = torch.tensor([0, 1, 4095, 16380, 24571, M - 1], device=dev)
     res = {}
     for fused in (True, False):
         lins = [P.NSplitLinear(ly["w"], ly["ws"], ly["b"], fused=fused) for ly in layers]
+        outs = [None] * len(lins)
 
         def step():
-            for lin, ly in zip(lins, layers):
-                lin.forward(ly["x"])
+            for i, (lin, ly) in enumerate(zip(lins, layers)):
+                outs[i] = lin.forward(ly["x"])
         step()
         torch.cuda.synchronize()
+        ok = all(torch.equal(o.index_select(0, rows).view(torch.int16), ly["out"].index_select(0, rows).view(torch.int16))
+                 for o, ly in zip(outs, layers))
+        checks["nsplit_fused" if fused else "nsplit_nccl"] = ok
         dist.barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(reps):
-            step()
-        e1.record()
-        torch.cuda.synchronize()
-        ms = _max_over_ranks(e0.elapsed_time(e1) / reps, dist, dev)
+        ms = _max_over_ranks(time_steps(step, reps, dev), dist, dev)
         res["fused" if fused else "nccl"] = {"ms_per_step": round(ms, 3),
                                              "tops": round(ops_per_step(M) / (ms * 1e-3) / 1e12, 1)}
+        outs = None
         for lin in lins:
             lin.close()
         torch.cuda.synchronize()
         dist.barrier()
+    del layers
     S, H = 32760, 40
     lo, hi = P.row_range(S, world, rank)
-    g = torch.Generator(device=dev).manual_seed(77 + rank)
-    q = torch.randn((hi - lo, H, 128), generator=g, device=dev).to(torch.bfloat16)
-    k = torch.randn((hi - lo, H, 128), generator=g, device=dev).to(torch.bfloat16)
-    v = torch.randn((hi - lo, H, 128), generator=g, device=dev).to(torch.bfloat16)
-    P.sharded_attention(q, k, v, S)
+    g = torch.Generator(device=dev).manual_seed(77)  # the same sequence on every rank; each keeps its rows
+    q = torch.randn((S, H, 128), generator=g, device=dev).to(torch.bfloat16)
+    k = (torch.randn((S, H, 128), generator=g, device=dev) +
+         3.0 * torch.randn((1, H, 128), generator=g, device=dev)).to(torch.bfloat16)
+    v = torch.randn((S, H, 128), generator=g, device=dev).to(torch.bfloat16)
+    ql, kl, vl = (t[lo:hi].contiguous() for t in (q, k, v))
+    got = P.sharded_attention(ql, kl, vl, S)
+    whole = h3q.attention(q, k, v)
     torch.cuda.synchronize()
+    checks["attention_query_sharded"] = bool(torch.equal(got.view(torch.int16), whole[lo:hi].view(torch.int16)))
+    del whole, q, k, v
     dist.barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(reps):
-        P.sharded_attention(q, k, v, S)
-    e1.record()
-    torch.cuda.synchronize()
-    ms = _max_over_ranks(e0.elapsed_time(e1) / reps, dist, dev)
+    ms = _max_over_ranks(time_steps(lambda: P.sharded_attention(ql, kl, vl, S), reps, dev), dist, dev)
     att = {"ms": round(ms, 3), "tops": round(4.0 * S * S * 128 * H / (ms * 1e-3) / 1e12, 1),
            "note": "K/V all-gather + kmean/quant of the full K + attention of this rank's query rows"}
-    return {"nsplit_c1_linears": dict(res, workload="c1 linears, N split, M=32760 in total (strong scaling)"),
-            "attention_c4_query_sharded": att, "device_status": h3q.device_status(dev.index or 0)}
+    flag = torch.tensor([1 if all(checks.values()) else 0], device=dev, dtype=torch.int32)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    return {"weak_c1_linears": weak,
+            "nsplit_c1_linears": dict(res, workload="c1 linears, N split, M=32760 in total (strong scaling)"),
+            "attention_c4_query_sharded": att, "parity": bool(flag.item()), "parity_checks_rank0": checks,
+            "device_status": h3q.device_status(dev.index or 0)}
 
 
 def run_profile_case(args) -> None:
@@ -654,21 +862,10 @@ def main() -> None:
     if not h3q.available_arch(local):
         raise SystemExit("bench.py: this library needs an sm_100 (B200) GPU")
 
-    M = M_TOKENS
-    g = torch.Generator(device=dev).manual_seed(1234 + rank)
-    layers = []
-    for name, k, n in LINEARS:
-        x = torch.randn((M, k), generator=g, device=dev)
-        oc = torch.randperm(k, generator=g, device=dev)[:8]
-        x[:, oc] *= 20.0
-        x = x.to(torch.bfloat16)
-        w = torch.randint(-127, 128, (n, k), generator=g, device=dev, dtype=torch.int8)
-        wsc = torch.rand(n, generator=g, device=dev) * 9e-3 + 1e-3
-        b = (torch.randn(n, generator=g, device=dev) * 0.02).to(torch.bfloat16).float()
-        layers.append(dict(name=name, k=k, n=n, x=x, w=w, ws=wsc, b=b,
-                           q=torch.empty((M, k), dtype=torch.int8, device=dev),
-                           xs=torch.empty(M, dtype=torch.float32, device=dev),
-                           out=torch.empty((M, n), dtype=torch.bfloat16, device=dev)))
+    # strong scaling: the 32760 tokens of the step split over the ranks (row_range), weights replicated
+    lo_r, hi_r = row_range(M_TOKENS, ws_n, rank)
+    M = hi_r - lo_r
+    layers = make_layers(M, dev, rank)
     L = h3q.lib()
     stream = torch.cuda.current_stream(dev)
     sp = stream.cuda_stream
@@ -710,7 +907,8 @@ def main() -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         elapsed_ms = float(t.item())
     ms_step = elapsed_ms / args.steps
-    value = ws_n * ops_per_step(M) / (ms_step * 1e-3) / 1e12
+    # strong scaling: every step of the job processes the 32760 tokens once, split over the ranks
+    value = ops_per_step(M_TOKENS) / (ms_step * 1e-3) / 1e12
     status = h3q.device_status(local)
     if status:
         raise SystemExit(f"bench.py: a kernel reported device error {status}")
@@ -727,9 +925,10 @@ def main() -> None:
     for i, (nm, k, n) in enumerate(LINEARS):
         g_ms = sum(ev[s][i][1].elapsed_time(ev[s][i][2]) for s in range(args.steps)) / args.steps
         q_ms = sum(ev[s][i][0].elapsed_time(ev[s][i][1]) for s in range(args.steps)) / args.steps
-        per_linear.append({"linear": f"{nm}:{k}x{n}", "gemm_ms": round(g_ms, 4),
+        per_linear.append({"linear": f"{nm}:{k}x{n}", "m": M, "gemm_ms": round(g_ms, 4),
                            "gemm_tops": round(2.0 * M * k * n / (g_ms * 1e-3) / 1e12, 1), "quant_ms": round(q_ms, 4),
-                           "quant_gbs": round((3.0 * M * k + 4.0 * M) / (q_ms * 1e-3) / 1e9, 1)})
+                           "quant_gbs": round((3.0 * M * k + 4.0 * M) / (q_ms * 1e-3) / 1e9, 1),
+                           **tile_waves(M, n)})
     peaks = load_peaks()
     # the GEMM runs inside the timed step: when the power cap engaged during it (sw_power_cap among the reasons the
     # clock samples inside the region show), the denominator is the sustained (power-capped) bf16 figure, else the
@@ -812,7 +1011,7 @@ def main() -> None:
         e1.record(stream)
         torch.cuda.synchronize()
         link_ms = e0.elapsed_time(e1) / e_steps
-        e2e = {"value": ws_n * ops_per_step(M) / (e_ms * 1e-3) / 1e12, "unit": "TOPS",
+        e2e = {"value": ops_per_step(M_TOKENS) / (e_ms * 1e-3) / 1e12, "unit": "TOPS",
                "h2d_bytes_per_step": int(sum(h.numel() * 2 for h in host_x)),
                "d2h_bytes_per_step": int(sum(h.numel() * 2 for h in host_o)), "ms_per_step": e_ms,
                "link_bound": {"copies_only_ms": link_ms, "frac": link_ms / e_ms,
@@ -825,18 +1024,22 @@ def main() -> None:
     extras = None
     if dist is not None:
         try:
-            extras = multi_gpu_extras(layers, M, dist, dev)
+            extras = multi_gpu_extras(dist, dev)
         except Exception as e:  # the headline line must still print; the failure is reported in it
             extras = {"error": f"{type(e).__name__}: {e}"}
         torch.cuda.synchronize()
         dist.barrier()
-    nv = nvfp4_c3(dev, load_peaks()) if rank == 0 else None
-    att = attention_c4(dev, load_peaks()) if rank == 0 else None
-    modq = modulate_fused(dev, load_peaks()) if rank == 0 else None
-    lmerge = lora_merge(dev) if rank == 0 else None
-    attend = attend_step_c4(dev) if rank == 0 else None
-    stream_c1 = streaming_c1(layers, M, dev) if rank == 0 else None
-    block = dit_block_c4(dev) if rank == 0 else None
+    # single-GPU measurements of the other configs and call sites: at N = 1 only
+    solo = rank == 0 and ws_n == 1
+    comp = gpu_comparators(layers, dev, per_linear) if solo else None
+    c2 = c2_block(dev, load_peaks()) if solo else None
+    nv = nvfp4_c3(dev, load_peaks()) if solo else None
+    att = attention_c4(dev, load_peaks()) if solo else None
+    modq = modulate_fused(dev, load_peaks()) if solo else None
+    lmerge = lora_merge(dev) if solo else None
+    attend = attend_step_c4(dev) if solo else None
+    stream_c1 = streaming_c1(layers, M, dev) if solo else None
+    block = dit_block_c4(dev) if solo else None
 
     cb = None
     if rank == 0 and ws_n == 1 and not args.no_cpu_baseline:
@@ -850,7 +1053,7 @@ def main() -> None:
         return
     line = {
         "metric": METRIC, "value": value, "unit": "TOPS", "n_gpus": ws_n, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "int8", "data": "synthetic", "config": config_block(ws_n),
         "frac_of_int8_peak": value / ws_n / int8_peak,
         "roofline": {"kernel": "gemm_i8_kernel (tcgen05 kind::i8, fused epilogue)", "bound": "tensor",
@@ -866,6 +1069,8 @@ def main() -> None:
                            "frac": q_achieved / peaks["hbm_gbs"], "avg_launch_ms": quant_avg_ms,
                            "bytes_per_launch": quant_bytes_launch},
         "per_linear": per_linear,
+        "gpu_comparators": comp,
+        "c2": c2,
         "nvfp4_c3": nv,
         "attention_c4": att,
         "modulate_quant": modq,
