@@ -44,9 +44,13 @@ struct GemmCfg {
   static constexpr size_t kSmem = 1024 + (size_t)kStages * kStageBytes + EPI_SMEM + 256;
 };
 
+// candle's tanh GELU, 0.5 y (1 + tanh(z)) with z = sqrt(2/pi) (y + 0.044715 y^3), in its logistic form: since
+// 1 + tanh(z) = 2 / (1 + e^(-2z)), it equals y / (1 + e^(-2z)), one exponential and one approximate reciprocal
+// instead of a tanh.  Large negative y: e^(-2z) overflows, the reciprocal is 0 and the result -0, as the limit.
 __device__ __forceinline__ float gelu_tanh(float y) {
-  const float c = 0.7978845608028654f;  // sqrt(2/pi)
-  return 0.5f * y * (1.f + tanhf(c * (y + 0.044715f * y * y * y)));
+  const float m2c = -2.f * 0.7978845608028654f;  // -2 sqrt(2/pi)
+  const float z2 = m2c * __fmaf_rn(0.044715f * y, y * y, y);
+  return __fdividef(y, 1.f + __expf(z2));
 }
 
 // Epilogue of one accumulator tile for the 32 output rows of this warp (TMEM lanes 32q..32q+31 of `tacc`).

@@ -141,11 +141,11 @@ struct ModArgs {
   float eps;
 };
 
-template <int ORDER, typename Tin, bool ROT_ONLY = false, bool MOD = false>
-__global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__ CUtensorMap tmx,
-                                                         int8_t* __restrict__ q, float* __restrict__ scale,
-                                                         int64_t M, int K, int box_rows, int boxes_per_row,
-                                                         int* err, uint16_t* __restrict__ ybf, const ModArgs mod) {
+template <int ORDER, typename Tin, bool ROT_ONLY, bool MOD>
+__device__ __forceinline__ void quant_rows_body(const CUtensorMap& tmx, int8_t* __restrict__ q,
+                                                float* __restrict__ scale, int64_t M, int K, int box_rows,
+                                                int boxes_per_row, int* err, uint16_t* __restrict__ ybf,
+                                                const ModArgs& mod) {
   constexpr int NST = MOD ? kQStagesMod : kQStages;
   extern __shared__ uint8_t qsm_raw[];
   // align by offsetting the __shared__ array itself, so the compiler keeps shared-space (LDS/STS) accesses
@@ -277,7 +277,10 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
     }
     float inv_rms = 0.f;
     if (!MOD) {
-      const bool landed = mbar_wait_bounded(&full[stage], (uint32_t)(it / NST) & 1u, &s_abort, err, kDevTimeoutFull);
+      // one thread waits for the row's bytes (its mbarrier wait acquires them); the barrier then orders that wait
+      // before every other thread's reads, and those threads sleep in the barrier instead of polling the mbarrier
+      bool landed = true;
+      if (t == 0) landed = mbar_wait_bounded(&full[stage], (uint32_t)(it / NST) & 1u, &s_abort, err, kDevTimeoutFull);
       if (!__syncthreads_and(landed)) break;  // the whole CTA gives up together (barriers follow)
     } else {
       if (stop) break;  // the row did not land (the CTA agreed under the previous barrier)
@@ -416,16 +419,20 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
     }
     // Row maximum of |v|, NaN-propagating: rows holding an Inf or NaN (max bits >= the Inf pattern) take the exact
     // slow path below; every other row needs neither the NaN-ignoring max nor per-element NaN / clamp selects.
+    // max|v| = max(max v, -min v): two 3-input operations per pair, no absolute values.
     float m = 0.f;
     if (!ROT_ONLY) {
+      float mx = 0.f, mn = 0.f;
 #pragma unroll
       for (int d3 = 0; d3 < 4; ++d3)
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           float x0, x1;
           upk(u2[d3][i], x0, x1);
-          asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(m), "f"(fabsf(x0)), "f"(fabsf(x1)));
+          asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(mx) : "f"(mx), "f"(x0), "f"(x1));
+          asm("min.NaN.f32 %0, %1, %2, %3;" : "=f"(mn) : "f"(mn), "f"(x0), "f"(x1));
         }
+      asm("max.NaN.f32 %0, %1, %2;" : "=f"(m) : "f"(mx), "f"(-mn));
     }
     const unsigned mw = __reduce_max_sync(0xffffffffu, __float_as_uint(m));
     const int slot = it % 3;
@@ -528,9 +535,10 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
           const f2 tt = fma2(u2[d3][i0 + e], inv2, zero2);
           if (!special) {
             // |t| <= 127 by construction of inv: the nearest-even integer is the code, no clamp or NaN case
+            // the code is the low byte of the sum's bits; the byte permutes below read only that byte
             upk(add2(tt, rnd2), r0, r1);
-            b[2 * e] = __float_as_uint(r0) & 0xffu;
-            b[2 * e + 1] = __float_as_uint(r1) & 0xffu;
+            b[2 * e] = __float_as_uint(r0);
+            b[2 * e + 1] = __float_as_uint(r1);
           } else {
             upk(tt, t0, t1);
             b[2 * e] = code_of<ORDER>(t0);
@@ -563,6 +571,25 @@ __global__ void __launch_bounds__(256) quant_rows_kernel(const __grid_constant__
     }
   }
   __syncthreads();
+}
+
+// The row quantizer without modulation, capped at 96 registers: with the 96-thread team of K = 5120 that is six
+// CTAs (18 warps) per SM, where the compiler's own choice (103 registers) left room for five; no spills.
+template <int ORDER, typename Tin, bool ROT_ONLY = false>
+__global__ void __maxnreg__(96) quant_rows_kernel(const __grid_constant__ CUtensorMap tmx, int8_t* __restrict__ q,
+                                                  float* __restrict__ scale, int64_t M, int K, int box_rows,
+                                                  int boxes_per_row, int* err, uint16_t* __restrict__ ybf,
+                                                  const ModArgs mod) {
+  quant_rows_body<ORDER, Tin, ROT_ONLY, false>(tmx, q, scale, M, K, box_rows, boxes_per_row, err, ybf, mod);
+}
+
+// RMSNorm + modulate, then the quantizer (or the modulated row alone): the register cap above would spill here.
+template <int ORDER, typename Tin, bool ROT_ONLY = false>
+__global__ void __launch_bounds__(256) quant_rows_mod_kernel(const __grid_constant__ CUtensorMap tmx,
+                                                             int8_t* __restrict__ q, float* __restrict__ scale,
+                                                             int64_t M, int K, int box_rows, int boxes_per_row,
+                                                             int* err, uint16_t* __restrict__ ybf, const ModArgs mod) {
+  quant_rows_body<ORDER, Tin, ROT_ONLY, true>(tmx, q, scale, M, K, box_rows, boxes_per_row, err, ybf, mod);
 }
 
 // Unrotated per-row quantization for any K (quant_rows_i8, kernels.rs:296-318): one 256-thread block per row,
@@ -628,8 +655,15 @@ static cudaError_t launch_rows(const void* x, int8_t* q, float* scale, int64_t M
   // MOD adds each owner thread's 64 columns of the current adaLN table row (bf16 scale / shift, 256 bytes); the
   // norm weight, the same for every row, is read through L1
   const size_t smem = 1024 + (MOD ? kQStagesMod : kQStages) * stage_bytes + (MOD ? (size_t)4 * G * 256 : 0);
-  auto kern = quant_rows_kernel<ORDER, Tin, ROT_ONLY, MOD>;
+  auto kern = [] {
+    if constexpr (MOD) return quant_rows_mod_kernel<ORDER, Tin, ROT_ONLY>;
+    else return quant_rows_kernel<ORDER, Tin, ROT_ONLY>;
+  }();
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  // the largest shared-memory carveout of the unified L1 / shared array, so the rings of more CTAs fit on an SM;
+  // what the kernel reads through L1 (MOD's norm weight and table rows, a few KB per CTA) fits in the rest
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
   if (e != cudaSuccess) return e;
   int dev = 0, per_sm = 0;
   cudaGetDevice(&dev);
