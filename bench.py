@@ -677,10 +677,13 @@ def multi_gpu_extras(dist, dev, reps: int = 3) -> dict:
     ranks and checks):
       weak:      every rank runs the four c1 linears on its own 32760 tokens (no collective);
       nsplit:    the four c1 linears with the weight rows split over the ranks and the activations replicated
-                 (M = 32760 in total, strong scaling); "fused" is one GEMM per rank writing its column block into
-                 every rank's output over NVLink (h3q_gemm_s8_allgather), "nccl" a local GEMM + NCCL all-gather +
-                 relayout; each output must equal, bit for bit, the whole linear computed on one GPU (the weak
-                 run's output of the same activations);
+                 (M = 32760 in total, strong scaling), through h3q_gemm_s8_nsplit: "fused" is one GEMM per rank
+                 storing its column block into every rank's output over NVLink, "push" the GEMM in row chunks with
+                 the copy engines forwarding each finished chunk, "nccl" a local GEMM + ncclAllGather + relayout,
+                 "push_shard_quant" push with each rank quantizing only its row block and all-gathering the codes;
+                 exchange_ms = the form's time minus the local work alone (compute_only_ms); each output must
+                 equal, bit for bit, the whole linear computed on one GPU (the weak run's output of the same
+                 activations);
       attention: query-sharded c4 attention (S = 32760, H = 40 in total): K/V rows all-gathered, each rank attends
                  its 32760 / N queries (h3q_attention_rows); its rows must equal those of the whole-sequence
                  attention computed on one GPU."""
@@ -705,9 +708,21 @@ def multi_gpu_extras(dist, dev, reps: int = 3) -> dict:
     weak = {"ms_per_step": round(ms, 3), "tops": round(world * ops_per_step(M) / (ms * 1e-3) / 1e12, 1),
             "note": "32760 tokens per GPU, value = all ranks' ops / max time"}
     rows = torch.tensor([0, 1, 4095, 16380, 24571, M - 1], device=dev)
+    comm = P.Comm(dev)
     res = {}
-    for fused in (True, False):
-        lins = [P.NSplitLinear(ly["w"], ly["ws"], ly["b"], fused=fused) for ly in layers]
+    # the local work alone (quantize all rows, GEMM of this rank's columns), to itemise the exchange
+    lins = [P.NSplitLinear(ly["w"], ly["ws"], ly["b"], comm, mode="nccl") for ly in layers]
+
+    def compute_only():
+        for lin, ly in zip(lins, layers):
+            q, xs = h3q.quant_rows(ly["x"], True)
+            h3q.gemm_s8_quantized(q, xs, lin.w, lin.ws, lin.bias, h3q.EPI_LINEAR)
+    dist.barrier()
+    compute_ms = _max_over_ranks(time_steps(compute_only, reps, dev), dist, dev)
+    del lins
+    for name, mode, shard in (("fused", "fused", False), ("push", "push", False), ("nccl", "nccl", False),
+                              ("push_shard_quant", "push", True)):
+        lins = [P.NSplitLinear(ly["w"], ly["ws"], ly["b"], comm, mode=mode, shard_quant=shard) for ly in layers]
         outs = [None] * len(lins)
 
         def step():
@@ -717,16 +732,18 @@ def multi_gpu_extras(dist, dev, reps: int = 3) -> dict:
         torch.cuda.synchronize()
         ok = all(torch.equal(o.index_select(0, rows).view(torch.int16), ly["out"].index_select(0, rows).view(torch.int16))
                  for o, ly in zip(outs, layers))
-        checks["nsplit_fused" if fused else "nsplit_nccl"] = ok
+        checks["nsplit_" + name] = ok
         dist.barrier()
         ms = _max_over_ranks(time_steps(step, reps, dev), dist, dev)
-        res["fused" if fused else "nccl"] = {"ms_per_step": round(ms, 3),
-                                             "tops": round(ops_per_step(M) / (ms * 1e-3) / 1e12, 1)}
+        res[name] = {"ms_per_step": round(ms, 3), "tops": round(ops_per_step(M) / (ms * 1e-3) / 1e12, 1),
+                     "exchange_ms": round(ms - compute_ms, 3)}
         outs = None
         for lin in lins:
             lin.close()
         torch.cuda.synchronize()
         dist.barrier()
+    res["compute_only_ms"] = round(compute_ms, 3)
+    res["output_bytes_received_per_rank"] = int(sum(M * ly["n"] * 2 for ly in layers) * (world - 1) / world)
     del layers
     S, H = 32760, 40
     lo, hi = P.row_range(S, world, rank)
@@ -736,17 +753,18 @@ def multi_gpu_extras(dist, dev, reps: int = 3) -> dict:
          3.0 * torch.randn((1, H, 128), generator=g, device=dev)).to(torch.bfloat16)
     v = torch.randn((S, H, 128), generator=g, device=dev).to(torch.bfloat16)
     ql, kl, vl = (t[lo:hi].contiguous() for t in (q, k, v))
-    got = P.sharded_attention(ql, kl, vl, S)
+    got = P.sharded_attention(ql, kl, vl, S, comm=comm)
     whole = h3q.attention(q, k, v)
     torch.cuda.synchronize()
     checks["attention_query_sharded"] = bool(torch.equal(got.view(torch.int16), whole[lo:hi].view(torch.int16)))
     del whole, q, k, v
     dist.barrier()
-    ms = _max_over_ranks(time_steps(lambda: P.sharded_attention(ql, kl, vl, S), reps, dev), dist, dev)
+    ms = _max_over_ranks(time_steps(lambda: P.sharded_attention(ql, kl, vl, S, comm=comm), reps, dev), dist, dev)
     att = {"ms": round(ms, 3), "tops": round(4.0 * S * S * 128 * H / (ms * 1e-3) / 1e12, 1),
            "note": "K/V all-gather + kmean/quant of the full K + attention of this rank's query rows"}
     flag = torch.tensor([1 if all(checks.values()) else 0], device=dev, dtype=torch.int32)
     dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+    comm.close()
     return {"weak_c1_linears": weak,
             "nsplit_c1_linears": dict(res, workload="c1 linears, N split, M=32760 in total (strong scaling)"),
             "attention_c4_query_sharded": att, "parity": bool(flag.item()), "parity_checks_rank0": checks,

@@ -101,6 +101,17 @@ SIGNATURES = {
     "h3q_gate_add": (_int, [_vp, _vp, _int, _vp, _vp, _vp, _i64, _i64, _vp]),
     "h3q_gemm_s8_static": (_int, [_vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _int, _int, _vp]),
     "h3q_gemm_s8_static_status": (_int, [_int, ctypes.POINTER(_int)]),
+    "h3q_comm_unique_id": (_int, [_vp]),
+    "h3q_comm_init": (_int, [_int, _int, _vp, ctypes.POINTER(_vp)]),
+    "h3q_comm_destroy": (_int, [_vp]),
+    "h3q_comm_rank": (_int, [_vp]),
+    "h3q_comm_size": (_int, [_vp]),
+    "h3q_comm_allgather": (_int, [_vp, _vp, _vp, _sz, _vp]),
+    "h3q_comm_barrier": (_int, [_vp, _vp]),
+    "h3q_nsplit_range": (None, [_i64, _int, _int, ctypes.POINTER(_i64), ctypes.POINTER(_i64)]),
+    "h3q_gemm_s8_nsplit_workspace_size": (_sz, [_i64, _i64, _int, _int]),
+    "h3q_gemm_s8_nsplit": (_int, [_vp, _int, _vp, _vp, _vp, _vp, _i64, _vp, ctypes.POINTER(_vp), _i64, _i64, _i64, _vp,
+                                  _sz, _vp]),
     "h3q_selftest_wait_timeout": (_int, [_int, ctypes.c_uint64, _vp, _vp]),
     "h3q_nvfp4_linear_workspace_size": (_sz, [_i64, _i64, _i64, _int]),
     "h3q_nvfp4_linear": (_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp, _sz, _vp]),

@@ -6,15 +6,17 @@ The reference runs on a single GPU; partitioning follows the data:
   needs no collective (per-row quantisation, per-row scales); gather_rows() assembles a full [M, ...] tensor on
   every rank when a caller needs one.
 * N-split linear: rank r holds the weight rows (output columns) nsplit_range(N, world, r) and the full activation;
-  NSplitLinear writes each rank's column block into every rank's output inside the GEMM (peer memory over
-  NVLink, h3q_gemm_s8_allgather), or computes locally and all-gathers through NCCL; by default the faster of the
-  two for the number of ranks.
+  NSplitLinear runs h3q_gemm_s8_nsplit (C ABI) in one of its forms: the GEMM storing each output box into every
+  rank's buffer (fused), the GEMM in row chunks with the copy engines pushing finished chunks to the peers (push),
+  or a local GEMM + ncclAllGather + relayout (nccl).
 * Query-sharded attention: rank r owns query rows row_range(S, world, r); K and V rows are gathered from all ranks
-  and each rank attends its queries against every key (h3q_attention_rows).  Its rows equal the single-GPU
-  result's (per-token scales).
+  (h3q_comm_allgather) and each rank attends its queries against every key (h3q_attention_rows).  Its rows equal
+  the single-GPU result's (per-token scales).
 
-Collectives go through torch.distributed: NCCL between GPUs, gloo in the CPU tests.  The operators are parameters
-so the host logic can be exercised on CPU with the oracle; on GPUs they default to this library's kernels.
+On GPUs the data plane is the library's: a Comm is an NCCL communicator created through the C ABI
+(h3q_comm_init), its id handed around over torch.distributed.  torch.distributed also carries the host-side
+set-up (ids, IPC handles) and, in the CPU tests, the gloo collectives; the operators are parameters, so the host
+logic is exercised on CPU with the oracle.
 """
 from __future__ import annotations
 
@@ -129,69 +131,140 @@ class PeerBuffers:
                 self._own = None
 
 
-class NSplitLinear:
-    """attn8::gemm_s8 (linear epilogue, bf16 out) with the weight rows split over the ranks.  Every rank passes the
-    full activation x [M, K] and receives the full output [M, N]; rank r stores the columns nsplit_range(N, g, r).
+NSPLIT_FUSED, NSPLIT_PUSH, NSPLIT_NCCL = 0, 1, 2
+NSPLIT_MODES = {"fused": NSPLIT_FUSED, "push": NSPLIT_PUSH, "nccl": NSPLIT_NCCL}
 
-    fused=True: one kernel per rank computes its columns and writes them into every rank's output buffer over
-    NVLink; a one-element all-reduce after it is the barrier that makes the output complete.  fused=False: local
-    GEMM, then gather_columns (NCCL all-gather + relayout).  fused=None (the default) picks the faster one as
-    measured on B200 for the DiT linears: the fused kernel up to FUSED_MAX_RANKS ranks (2 GPUs: 4.6 ms against
-    8.8 ms for the four c1 linears), NCCL beyond (8 GPUs: 10.2 ms against 27.1 ms, where every output box becomes
-    seven small remote stores)."""
 
-    FUSED_MAX_RANKS = 2
+class Comm:
+    """An h3q communicator (NCCL, created by h3q_comm_init through the C ABI) over the ranks of a torch.distributed
+    group, on `device`.  Rank 0 of the group makes the id; torch.distributed hands it to the others."""
 
-    def __init__(self, w, ws, bias, group=None, fused: bool | None = None, rotate: bool = True):
+    def __init__(self, device, group=None):
         import torch
         dist = _dist()
-        self.group = group
         self.world, self.rank = dist.get_world_size(group), dist.get_rank(group)
+        self.device = torch.device(device)
+        idb = (ctypes.c_uint8 * 128)()
+        if self.rank == 0:
+            check(lib().h3q_comm_unique_id(idb))
+        obj = [bytes(idb) if self.rank == 0 else None]
+        src = dist.get_global_rank(group, 0) if group is not None else 0
+        dist.broadcast_object_list(obj, src=src, group=group, device=self.device)
+        idb = (ctypes.c_uint8 * 128).from_buffer_copy(obj[0])
+        self.ptr = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            check(lib().h3q_comm_init(self.world, self.rank, idb, ctypes.byref(self.ptr)))
+
+    def allgather(self, send, recv) -> None:
+        """recv (world x send's bytes, rank order) = every rank's send; on the current stream."""
+        nbytes = send.numel() * send.element_size()
+        if recv.numel() * recv.element_size() != self.world * nbytes:
+            raise ValueError("Comm.allgather: recv must hold world x send bytes")
+        check(lib().h3q_comm_allgather(self.ptr, _p(send), _p(recv), nbytes, _stream(self.device)))
+
+    def barrier(self) -> None:
+        check(lib().h3q_comm_barrier(self.ptr, _stream(self.device)))
+
+    def close(self) -> None:
+        if self.ptr:
+            import torch
+            torch.cuda.synchronize(self.device)
+            check(lib().h3q_comm_destroy(self.ptr))
+            self.ptr = None
+
+
+class NSplitLinear:
+    """attn8::gemm_s8 (linear epilogue, bf16 out) with the weight rows split over the ranks.  Every rank passes the
+    full activation x [M, K] and receives the full output [M, N]; rank r computes the columns nsplit_range(N, g, r)
+    and h3q_gemm_s8_nsplit all-gathers them in the chosen form:
+
+      "fused"  one GEMM per rank whose epilogue stores every output box into every rank's buffer (peer memory over
+               NVLink), so the transfer runs inside the GEMM;
+      "push"   the GEMM in row chunks into this rank's buffer, the copy engines pushing each finished chunk into
+               the peers' buffers while the next chunk computes;
+      "nccl"   local GEMM, ncclAllGather of the column blocks, relayout kernel.
+
+    mode=None picks the form measured fastest on B200 for the four c1 linears (M = 32760, DEFAULT_MODE): "push"
+    (2 GPUs: 4.28 ms against 4.49 fused and 7.61 nccl).
+    shard_quant=True quantizes only this rank's row_range of x and all-gathers the int8 codes and row scales
+    (M K + 4 M bytes over NVLink) instead of every rank quantizing all rows (needs M % world == 0)."""
+
+    DEFAULT_MODE = "push"
+
+    def __init__(self, w, ws, bias, comm: Comm, mode: str | None = None, rotate: bool = True,
+                 shard_quant: bool = False, group=None):
+        import torch
+        self.comm, self.group = comm, group
+        self.world, self.rank = comm.world, comm.rank
         self.n = w.shape[0]
         self.n0, self.n1 = nsplit_range(self.n, self.world, self.rank)
         self.w = w[self.n0:self.n1].contiguous()
         ws = ws.to(torch.float32).reshape(-1)
         self.ws = (ws[self.n0:self.n1] if ws.numel() == self.n and self.n > 1 else ws[:1]).contiguous()
         self.bias = None if bias is None else bias.to(torch.float32)[self.n0:self.n1].contiguous()
-        self.fused = (self.world <= self.FUSED_MAX_RANKS) if fused is None else bool(fused)
+        mode = mode or self.DEFAULT_MODE
+        if mode not in NSPLIT_MODES:
+            raise ValueError(f"NSplitLinear: unknown mode {mode!r}")
+        self.mode = mode
         self.rotate = rotate
+        self.shard_quant = shard_quant
         self.bufs = None
-        self._flag = None
+        self.out = None
+        self.ws_buf = None
 
-    def _buffers(self, m: int, device):
+    def _outputs(self, m: int, device):
+        import torch
+        if self.mode == "nccl":
+            if self.out is None or self.out.shape[0] != m:
+                self.out = torch.empty((m, self.n), dtype=torch.bfloat16, device=device)
+                nb = lib().h3q_gemm_s8_nsplit_workspace_size(m, self.n, self.world, NSPLIT_NCCL)
+                self.ws_buf = torch.empty(max(nb, 1), dtype=torch.uint8, device=device)
+            ptrs = [None] * self.world
+            ptrs[self.rank] = self.out.data_ptr()
+            return self.out, ptrs
         if self.bufs is None or self.bufs.rows != m:
             if self.bufs is not None:
                 self.bufs.close()
             self.bufs = PeerBuffers(m, self.n, device, self.group)
-        return self.bufs
+        return self.bufs.local, self.bufs.ptrs
 
-    def forward(self, x):
+    def quantize(self, x):
+        """(codes [M, K], scales [M]) of x on every rank: computed whole, or per row block and all-gathered."""
         import torch
-        dist = _dist()
-        q, xs = _quant_rows(x, self.rotate)
-        if not self.fused:
-            y = _gemm_s8_quantized(q, xs, self.w, self.ws, self.bias)
-            return gather_columns(y, self.n, self.group)
+        m, k = x.shape
+        if not self.shard_quant or self.world == 1 or m % self.world:
+            return _quant_rows(x, self.rotate)
+        lo, hi = row_range(m, self.world, self.rank)
+        ql, sl = _quant_rows(x[lo:hi], self.rotate)
+        q = torch.empty((m, k), dtype=torch.int8, device=x.device)
+        s = torch.empty(m, dtype=torch.float32, device=x.device)
+        self.comm.allgather(ql, q)
+        self.comm.allgather(sl, s)
+        return q, s
+
+    def forward(self, x, quantized=None):
+        import torch
+        q, xs = quantized if quantized is not None else self.quantize(x)
         m, k = q.shape
-        bufs = self._buffers(m, x.device)
-        outs = (ctypes.c_void_p * self.world)(*bufs.ptrs)
-        check(lib().h3q_gemm_s8_allgather(_p(q), _p(xs), _p(self.w), _p(self.ws), self.ws.numel(), _p(self.bias),
-                                          outs, self.world, m, self.n, self.n0, self.n1 - self.n0, k,
-                                          _stream(x.device)))
-        if self._flag is None:
-            self._flag = torch.zeros(1, device=x.device)
-        dist.all_reduce(self._flag, group=self.group)  # every rank's stores are complete past this point
-        return bufs.local
+        out, ptrs = self._outputs(m, x.device)
+        outs = (ctypes.c_void_p * self.world)(*ptrs)
+        wsp = self.ws_buf if self.mode == "nccl" else None
+        check(lib().h3q_gemm_s8_nsplit(self.comm.ptr, NSPLIT_MODES[self.mode], _p(q), _p(xs), _p(self.w),
+                                       _p(self.ws), self.ws.numel(), _p(self.bias), outs, m, self.n, k, _p(wsp),
+                                       0 if wsp is None else wsp.numel(), _stream(x.device)))
+        return out
 
     def close(self) -> None:
         if self.bufs is not None:
             self.bufs.close()
             self.bufs = None
+        self.out = self.ws_buf = None
 
 
-def gather_full(local, total: int, group=None):
+def gather_full(local, total: int, group=None, comm: Comm | None = None):
     """gather_rows without the staging copies when every rank holds the same number of rows (total divisible by
-    the world size): one all-gather straight into the full [total, ...] tensor, rank blocks in rank order."""
+    the world size): one all-gather straight into the full [total, ...] tensor, rank blocks in rank order; through
+    the library's communicator when `comm` is given, else torch.distributed."""
     dist = _dist()
     world, rank = dist.get_world_size(group), dist.get_rank(group)
     if total % world != 0:
@@ -200,16 +273,21 @@ def gather_full(local, total: int, group=None):
     if local.shape[0] != hi - lo:
         raise ValueError(f"gather_full: rank {rank} holds {local.shape[0]} rows, expected {(lo, hi)}")
     out = local.new_empty((total,) + tuple(local.shape[1:]))
-    dist.all_gather_into_tensor(out, local.contiguous(), group=group)
+    if comm is not None:
+        comm.allgather(local.contiguous(), out)
+    else:
+        dist.all_gather_into_tensor(out, local.contiguous(), group=group)
     return out
 
 
-def sharded_attention(q_local, k_local, v_local, total: int, group=None, flags: int = 0, rows_op=None):
+def sharded_attention(q_local, k_local, v_local, total: int, group=None, flags: int = 0, rows_op=None,
+                      comm: Comm | None = None):
     """Query-sharded attention: this rank's rows q_local, k_local, v_local ([s_r, H, 128], row_range order) ->
     its output rows [s_r, H, 128], attending over the keys and values of every rank.  K and V are each gathered
-    straight into full tensors (gather_full).  rows_op(q, k, v, flags) defaults to h3q.attention_rows."""
-    k_full = gather_full(k_local, total, group)
-    v_full = gather_full(v_local, total, group)
+    straight into full tensors (gather_full, through `comm` when given).  rows_op(q, k, v, flags) defaults to
+    h3q.attention_rows."""
+    k_full = gather_full(k_local, total, group, comm)
+    v_full = gather_full(v_local, total, group, comm)
     if rows_op is None:
         H = q_local.shape[1]
         return _attention_rows(q_local, k_full, v_full.reshape(total, H * 128), H * 128, 0, flags)
@@ -304,4 +382,5 @@ class RankMonitor:
 
 
 __all__ = ["row_range", "nsplit_range", "gather_rows", "gather_full", "gather_columns", "PeerBuffers", "NSplitLinear",
+           "Comm", "NSPLIT_MODES",
            "sharded_attention", "H3QError", "RankMonitor", "RankLeft", "RankLost", "JobCancelled"]

@@ -27,7 +27,7 @@ typedef enum {
   H3Q_ERR_UNSUPPORTED = 2, /* valid for the reference but outside what this build implements */
   H3Q_ERR_CUDA = 3,        /* a CUDA runtime / driver call failed */
   H3Q_ERR_TIMEOUT = 4,     /* a kernel gave up waiting on one of its own barriers (h3q_device_status) */
-  H3Q_ERR_NCCL = 5,        /* reserved for multi-GPU entry points */
+  H3Q_ERR_NCCL = 5,        /* NCCL missing or a collective failed (multi-GPU entry points) */
   H3Q_ERR_WORKSPACE = 6    /* the caller's workspace is smaller than *_workspace_size */
 } h3q_status;
 
@@ -483,6 +483,52 @@ h3q_status h3q_peer_buffer_free(void* ptr);
 h3q_status h3q_gemm_s8_allgather(const int8_t* a, const float* xs, const int8_t* w_local, const float* ws_local,
                                  int64_t ws_numel, const float* bias_local, void* const* outs, int n_ranks, int64_t m,
                                  int64_t n_total, int64_t n_offset, int64_t n_local, int64_t k, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * Multi-GPU data plane (no counterpart in the reference, which runs on one device: backend.rs:5-23).  One process
+ * per GPU.  Communicators are NCCL's, loaded at run time (a libnccl.so.2 already in the process is preferred);
+ * without NCCL these entry points return H3Q_ERR_NCCL.  Collectives are stream-ordered like every other call. */
+#define H3Q_COMM_ID_BYTES 128
+typedef struct h3q_comm h3q_comm;
+
+/* A new communicator id (H3Q_COMM_ID_BYTES bytes): made by one rank and handed to the others over the caller's
+ * own transport. */
+h3q_status h3q_comm_unique_id(void* id);
+/* Joins rank `rank` of `nranks` on the current device (collective: every rank calls it with the same id).  Also
+ * creates the communicator's barrier operand, copy stream and events (set-up, not the hot path). */
+h3q_status h3q_comm_init(int nranks, int rank, const void* id, h3q_comm** comm);
+h3q_status h3q_comm_destroy(h3q_comm* comm);
+int h3q_comm_rank(const h3q_comm* comm);
+int h3q_comm_size(const h3q_comm* comm);
+/* recv [nranks][bytes_per_rank] = every rank's send buffer, in rank order (ncclAllGather of bytes). */
+h3q_status h3q_comm_allgather(h3q_comm* comm, const void* send, void* recv, size_t bytes_per_rank, void* stream);
+/* Cross-rank barrier on the stream: completes on every rank only after every rank's earlier work on its stream. */
+h3q_status h3q_comm_barrier(h3q_comm* comm, void* stream);
+
+/* Forms of the N-split all-gather (h3q_gemm_s8_nsplit). */
+enum {
+  H3Q_NSPLIT_FUSED = 0, /* the GEMM's epilogue stores every output box into every rank's buffer (peer memory) */
+  H3Q_NSPLIT_PUSH = 1,  /* GEMM in row chunks into this rank's buffer; copy engines push finished chunks to peers */
+  H3Q_NSPLIT_NCCL = 2   /* local GEMM into a packed block, ncclAllGather, relayout kernel into the output */
+};
+
+/* Output columns [lo, hi) of rank `rank` in the N split of n columns: whole 256-column GEMM tiles, spread as evenly
+ * as the tile count allows (h3q.parallel.nsplit_range). */
+void h3q_nsplit_range(int64_t n, int nranks, int rank, int64_t* lo, int64_t* hi);
+/* Workspace bytes of h3q_gemm_s8_nsplit (non-zero for H3Q_NSPLIT_NCCL only). */
+size_t h3q_gemm_s8_nsplit_workspace_size(int64_t m, int64_t n_total, int nranks, int mode);
+/* attn8::gemm_s8's linear (bf16 out) with the weight rows split over the communicator's ranks: quantized
+ * activations a [m, k] with row scales xs [m] (the same on every rank), this rank's weight rows w_local
+ * [n_local, k] for its columns h3q_nsplit_range(n_total, nranks, rank) (scales ws_local per row when
+ * ws_numel == n_local > 1, bias_local [n_local] or NULL).  Every rank receives the whole output [m, n_total] in
+ * outs[rank].  FUSED and PUSH write into peers' buffers: outs[d] is rank d's output mapped into this process
+ * (h3q_peer_buffer_open); NCCL reads only outs[rank].  Barriers inside the call order the peers' writes after every
+ * rank's earlier use of its output and make the output complete when the call's work on the stream is done.
+ * Collective: every rank calls it with the same mode and shape.  n_total % 8 == 0, k % 16 == 0. */
+h3q_status h3q_gemm_s8_nsplit(h3q_comm* comm, int mode, const int8_t* a, const float* xs, const int8_t* w_local,
+                              const float* ws_local, int64_t ws_numel, const float* bias_local, void* const* outs,
+                              int64_t m, int64_t n_total, int64_t k, void* workspace, size_t workspace_bytes,
+                              void* stream);
 
 /* h3q_gemm_s8 for callers that cannot allocate device memory (no counterpart in the reference).  Some callers
  * cannot call cudaMalloc: a plugin inside a host that has already reserved the GPU's whole memory for its own

@@ -114,3 +114,30 @@ def test_host_pipeline_run_argument_checks():
     assert L.h3q_host_pipeline_run(None, ctypes.byref(item), 1, None) == h3q.ERR_ARG
     assert ctypes.sizeof(h3q.HostLinear) == 9 * 8 + 2 * 4
     assert h3q.HostLinear.rotate.offset == 9 * 8 + 4
+
+
+def test_nsplit_range_matches_python_split():
+    from h3q import parallel as P
+    L = h3q.lib()
+    lo, hi = ctypes.c_int64(), ctypes.c_int64()
+    for n, g in ((15360, 8), (5120, 3), (600, 2), (100, 4), (13824, 8), (5120, 8)):
+        for r in range(g):
+            L.h3q_nsplit_range(n, g, r, ctypes.byref(lo), ctypes.byref(hi))
+            assert (lo.value, hi.value) == P.nsplit_range(n, g, r)
+    L.h3q_nsplit_range(100, 4, 7, ctypes.byref(lo), ctypes.byref(hi))
+    assert (lo.value, hi.value) == (0, 0)
+
+
+def test_nsplit_workspace_and_comm_argument_checks():
+    L = h3q.lib()
+    # the NCCL form gathers [g][m][widest block] next to its own packed block; the other forms need none
+    assert L.h3q_gemm_s8_nsplit_workspace_size(1000, 15360, 8, 2) == 1000 * 2048 * 2 * 9
+    assert L.h3q_gemm_s8_nsplit_workspace_size(1000, 15360, 8, 0) == 0
+    assert L.h3q_gemm_s8_nsplit_workspace_size(1000, 15360, 8, 1) == 0
+    comm = ctypes.c_void_p()
+    idb = (ctypes.c_uint8 * 128)()
+    assert L.h3q_comm_init(0, 0, idb, ctypes.byref(comm)) == h3q.ERR_ARG and not comm.value
+    assert L.h3q_comm_init(2, 2, idb, ctypes.byref(comm)) == h3q.ERR_ARG
+    assert L.h3q_gemm_s8_nsplit(None, 0, None, None, None, None, 1, None, None, 1, 8, 16, None, 0, None) == h3q.ERR_ARG
+    assert L.h3q_comm_rank(None) == -1 and L.h3q_comm_size(None) == 0
+    assert L.h3q_comm_destroy(None) == h3q.OK
