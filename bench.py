@@ -268,22 +268,28 @@ def nvfp4_c3(dev, peaks: dict, reps: int = 10) -> dict:
         bs = pool[torch.randint(0, pool.numel(), (nbytes,), generator=g, device=dev)]
         gs = torch.tensor([1.0 / 448.0], device=dev)
         pqs = (torch.rand(K, generator=g, device=dev) * 1.5 + 0.5).to(torch.bfloat16)
-        for _ in range(3):
-            h3q.nvfp4_linear(x, q, bs, gs, pqs)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record()
-        for _ in range(reps):
-            h3q.nvfp4_linear(x, q, bs, gs, pqs)
-        e1.record()
-        torch.cuda.synchronize()
-        ms = e0.elapsed_time(e1) / reps
+        ms = time_steps(lambda: h3q.nvfp4_linear(x, q, bs, gs, pqs), reps, dev)
+        # the reference's GPU path on the same box: dequant_nvfp4 of the whole weight to bf16 (this library's
+        # bit-exact kernel for kernels.rs:65-81), the AWQ multiply (weights.rs:617-620) and a bf16 cuBLAS matmul
+        # (weights.rs:632), as QLinear::apply runs them for every call
+        wbf = torch.empty((N, K), dtype=torch.bfloat16, device=dev)
+
+        def ref_path():
+            wd = h3q.dequant_nvfp4(q, bs, gs, torch.bfloat16)
+            x2 = (x.float() * pqs.float()).to(torch.bfloat16)
+            return torch.matmul(x2, wd.t())
+        ref_ms = time_steps(ref_path, reps, dev)
+        mm_ms = time_steps(lambda: torch.matmul(x, wbf.t()), reps, dev)
         tf = 2.0 * M * N * K / (ms * 1e-3) / 1e12
         wbytes = N * K // 2 + nbytes
         res.append({"linear": f"{K}->{N}", "M": M, "ms": round(ms, 4), "tflops": round(tf, 1),
                     "frac_of_bf16_peak": round(tf / peaks["bf16_tflops"], 3),
-                    "weight_gbs": round(wbytes / (ms * 1e-3) / 1e9, 1)})
+                    "weight_gbs": round(wbytes / (ms * 1e-3) / 1e9, 1),
+                    "reference_gpu_path_ms": round(ref_ms, 4), "speedup_vs_reference_gpu_path": round(ref_ms / ms, 2),
+                    "cublas_bf16_matmul_alone_ms": round(mm_ms, 4)})
     return {"workload": "BASELINE c3: NVFP4+AWQ text-encoder linears, M=512", "layers": res,
-            "note": "time per call includes the AWQ pre-pass and, for 25600->5120, the split-K reduction"}
+            "note": "time per call includes the AWQ pre-pass and, for 25600->5120, the split-K reduction; "
+                    "cublas_bf16_matmul_alone_ms: the bf16 GEMM of the same shape with a resident bf16 weight"}
 
 
 def attention_c4(dev, peaks: dict, reps: int = 5, S: int = 32760, H: int = 40) -> dict:
