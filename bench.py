@@ -797,6 +797,23 @@ def run_profile_case(args) -> None:
                       "device_status": h3q.device_status(0)}))
 
 
+def run_profile_linears(args) -> None:
+    """The four c1 linears (quantizer + GEMM each) at args.profile_linears tokens: warmup + steps passes, for
+    ncu DRAM-traffic captures on a smaller case than the bench's 32760 tokens (8192 tokens hold ~1.5 GB)."""
+    import torch
+    import h3q
+    dev = torch.device("cuda", 0)
+    layers = make_layers(args.profile_linears, dev)
+    L = h3q.lib()
+    sp = torch.cuda.current_stream(dev).cuda_stream
+    for _ in range(args.warmup + args.steps):
+        for ly in layers:
+            run_linear(L, ly, sp)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": f"c1 linears at M={args.profile_linears}",
+                      "launches": 8 * (args.warmup + args.steps), "device_status": h3q.device_status(0)}))
+
+
 def run_profile_rope(args) -> None:
     """qk_norm_rope of the q part of a fused qkv, S=16384, H=40, rot 96: warmup + steps launches of
     qk_norm_rope128_kernel (q heads 168 MB in, 168 MB out)."""
@@ -835,12 +852,17 @@ def main() -> None:
                     help="small case for ncu captures: the LoRA merge of a 4096 x 5120 int8 layer, rank 64")
     ap.add_argument("--profile", action="store_true",
                     help="small case for ncu captures: one 4096-token fc1 linear (quant + GEMM), nothing else")
+    ap.add_argument("--profile-linears", type=int, default=0, metavar="M",
+                    help="small case for ncu captures: the four c1 linears at M tokens, nothing else")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference(args)
         return
     if args.profile:
         run_profile_case(args)
+        return
+    if args.profile_linears:
+        run_profile_linears(args)
         return
     if args.profile_rope:
         run_profile_rope(args)

@@ -1,0 +1,79 @@
+"""The reference's own GPU kernels, compiled from their source for sm_100a (oracle/_ref, test infrastructure), timed
+against this library's kernels on the same inputs and the same B200: the fused int8 GEMM gemm_s8 (attn8.rs:258-344,
+mma.sync m16n8k32) against the tcgen05 GEMM, the rotated quantizer quant_rows_i8_rot2 (kernels.rs:220-293) against
+the row quantizer, and attn_qk8 (attn8.rs:107-246) against the tcgen05 attention.  Each pair is first checked for
+equal results (bit for bit, or within the attention's 1e-2), then timed with CUDA events; the test asserts the
+library is faster by a wide margin and prints the times (run with -s to see them).
+"""
+import json
+
+import numpy as np
+import pytest
+import torch
+
+import h3q
+from oracle import oracle as O
+from oracle import ref as R
+
+pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not R.available(), reason="reference kernels not built")]
+
+
+def _ms(fn, reps: int = 10) -> float:
+    for _ in range(2):
+        fn()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def test_gemm_and_quantizer_vs_reference_kernels(cuda):
+    M, K, N = 8192, 5120, 13824  # the c1 fc1 linear on a quarter of its tokens
+    g = torch.Generator(device=cuda).manual_seed(9)
+    x = torch.randn((M, K), generator=g, device=cuda).to(torch.bfloat16)
+    w = torch.randint(-127, 128, (N, K), generator=g, device=cuda, dtype=torch.int8)
+    ws = torch.rand(N, generator=g, device=cuda) * 9e-3 + 1e-3
+    b = (torch.randn(N, generator=g, device=cuda) * 0.02).to(torch.bfloat16).float()
+    q, xs = h3q.quant_rows(x, True)
+    rq, rs = R.quant_rows(x, 2, True)
+    assert torch.equal(q, rq) and torch.equal(xs, rs)
+    ours = h3q.gemm_s8_quantized(q, xs, w, ws, b, h3q.EPI_LINEAR)
+    ref = R.gemm_s8(q, w, xs, ws, b, False)
+    torch.cuda.synchronize()
+    assert torch.equal(ours.view(torch.int16), ref.view(torch.int16))
+    t = {"gemm_ours_ms": _ms(lambda: h3q.gemm_s8_quantized(q, xs, w, ws, b, h3q.EPI_LINEAR, out=ours)),
+         "gemm_reference_ms": _ms(lambda: R.gemm_s8(q, w, xs, ws, b, False)),
+         "quant_ours_ms": _ms(lambda: h3q.quant_rows(x, True)),
+         "quant_reference_ms": _ms(lambda: R.quant_rows(x, 2, True))}
+    ops = 2.0 * M * N * K
+    t["gemm_ours_tops"] = ops / t["gemm_ours_ms"] / 1e9
+    t["gemm_reference_tops"] = ops / t["gemm_reference_ms"] / 1e9
+    print(json.dumps({"shape": [M, K, N], **{k: round(v, 4) for k, v in t.items()}}))
+    assert t["gemm_ours_ms"] * 2 < t["gemm_reference_ms"]
+    assert t["quant_ours_ms"] < t["quant_reference_ms"]
+
+
+def test_attention_vs_reference_kernel(cuda):
+    S, H = 8192, 4
+    g = torch.Generator(device=cuda).manual_seed(10)
+    q = torch.randn((S, H, 128), generator=g, device=cuda).to(torch.bfloat16)
+    k = (torch.randn((S, H, 128), generator=g, device=cuda) +
+         3.0 * torch.randn((1, H, 128), generator=g, device=cuda)).to(torch.bfloat16)
+    v = torch.randn((S, H, 128), generator=g, device=cuda).to(torch.bfloat16)
+    km = h3q.attn_kmean(k)
+    q8, qs = h3q.attn_quant_heads(q)
+    k8, ks = h3q.attn_quant_heads(k, km)
+    vt = h3q.attn_v_layout(v.reshape(S, H * 128), H * 128, 0, S, H)
+    v16 = R.v_to_f16(v.reshape(S, H * 128), H * 128, 0, S, H)
+    qsr, ksr = qs[:, :S].contiguous(), ks[:, :S].contiguous()
+    ours = h3q.attention_core(q8, qs, k8, ks, vt)
+    ref = R.attn_qk8(q8, qsr, k8, ksr, v16, O.attn_scale_log2())
+    torch.cuda.synchronize()
+    assert O.max_abs_rel(ours.float().cpu().numpy(), ref.float().cpu().numpy()) <= 1e-2
+    t = {"attention_ours_ms": _ms(lambda: h3q.attention_core(q8, qs, k8, ks, vt)),
+         "attention_reference_ms": _ms(lambda: R.attn_qk8(q8, qsr, k8, ksr, v16, O.attn_scale_log2()))}
+    print(json.dumps({"S": S, "H": H, **{k2: round(v2, 4) for k2, v2 in t.items()}}))
+    assert t["attention_ours_ms"] * 2 < t["attention_reference_ms"]
