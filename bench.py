@@ -288,7 +288,7 @@ def nvfp4_c3(dev, peaks: dict, reps: int = 10) -> dict:
                     "reference_gpu_path_ms": round(ref_ms, 4), "speedup_vs_reference_gpu_path": round(ref_ms / ms, 2),
                     "cublas_bf16_matmul_alone_ms": round(mm_ms, 4)})
     return {"workload": "BASELINE c3: NVFP4+AWQ text-encoder linears, M=512", "layers": res,
-            "note": "time per call includes the AWQ pre-pass and, for 25600->5120, the split-K reduction; "
+            "note": "time per call includes the AWQ pre-pass and, for 25600->5120, the stream-K fix-up; "
                     "cublas_bf16_matmul_alone_ms: the bf16 GEMM of the same shape with a resident bf16 weight"}
 
 
