@@ -1077,6 +1077,18 @@ def main() -> None:
         dist.barrier()
     # single-GPU measurements of the other configs and call sites: at N = 1 only
     solo = rank == 0 and ws_n == 1
+    q_alone = None
+    if solo:
+        # the same four quantizer launches back to back, no GEMM between them: inside the step the quantizer runs
+        # at the SM clock the power-capped GEMMs leave behind, and it is issue-bound
+        def quants():
+            for ly in layers:
+                h3q.check(L.h3q_quant_rows_i8(ly["x"].data_ptr(), 2, ly["q"].data_ptr(), ly["xs"].data_ptr(), M,
+                                              ly["k"], 1, sp))
+        qa_ms = time_steps(quants, 10, dev) / len(LINEARS)
+        q_alone = {"avg_launch_ms": qa_ms, "achieved": quant_bytes_launch / (qa_ms * 1e-3) / 1e9,
+                   "frac": quant_bytes_launch / (qa_ms * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                   "note": "the four quantizer launches alone, back to back (CUDA events)"}
     comp = gpu_comparators(layers, dev, per_linear) if solo else None
     c2 = c2_block(dev, load_peaks()) if solo else None
     nv = nvfp4_c3(dev, load_peaks()) if solo else None
@@ -1113,7 +1125,7 @@ def main() -> None:
         "roofline_quant": {"kernel": "quant_rows_kernel<2> (rotate + per-token int8)", "bound": "hbm",
                            "achieved": q_achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
                            "frac": q_achieved / peaks["hbm_gbs"], "avg_launch_ms": quant_avg_ms,
-                           "bytes_per_launch": quant_bytes_launch},
+                           "bytes_per_launch": quant_bytes_launch, "alone": q_alone},
         "per_linear": per_linear,
         "gpu_comparators": comp,
         "c2": c2,
