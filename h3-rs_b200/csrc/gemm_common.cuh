@@ -42,16 +42,30 @@ __device__ __forceinline__ void load_vec32(const float* p, int64_t col0, int val
 }
 
 // 32 f32 values -> packed words of the output kind (0 f32, 1 f16, 2 bf16); returns the row-chunk width in bytes.
+// bf16: the hardware's paired round-to-nearest-even conversion (one instruction per two values, the same bits as
+// f2bf for every non-NaN value, subnormals, infinities and overflow to infinity included), then, only when the
+// chunk holds a NaN, f2bf for the chunk so every NaN becomes the reference's 0x7fc0.
 __device__ __forceinline__ int pack_out(const float (&v)[32], int kind, uint32_t (&w)[32]) {
   if (kind == 0) {
 #pragma unroll
     for (int i = 0; i < 32; ++i) w[i] = __float_as_uint(v[i]);
     return 128;
   }
+  if (kind == 2) {
+    float m = 0.f;
 #pragma unroll
-  for (int i = 0; i < 16; ++i)
-    w[i] = kind == 2 ? pack_bf2(v[2 * i], v[2 * i + 1])
-                     : ((uint32_t)f2h(v[2 * i]) | ((uint32_t)f2h(v[2 * i + 1]) << 16));
+    for (int i = 0; i < 16; ++i) {
+      asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(w[i]) : "f"(v[2 * i + 1]), "f"(v[2 * i]));
+      asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(m), "f"(v[2 * i]), "f"(v[2 * i + 1]));
+    }
+    if (m != m) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) w[i] = pack_bf2(v[2 * i], v[2 * i + 1]);
+    }
+    return 64;
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) w[i] = (uint32_t)f2h(v[2 * i]) | ((uint32_t)f2h(v[2 * i + 1]) << 16);
   return 64;
 }
 

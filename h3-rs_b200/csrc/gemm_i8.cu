@@ -133,9 +133,15 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& p, EpiWarp& ew, ui
 #pragma unroll
       for (int i = 0; i < 32; ++i) b[i] = 0.f;
     }
+    // v = fma(acc * xs, ws, bias) two columns per instruction (paired f32 multiply and fma: each lane rounds
+    // exactly as the scalar instruction, so the bits are the reference's `acc * x * w + b`)
     float v[32];
+    const f2 xs2 = pk(xs, xs);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __fmaf_rn(__fmul_rn((float)(int)r[i], xs), w[i], b[i]);
+    for (int i = 0; i < 16; ++i) {
+      const f2 t = mul2(pk((float)(int)r[2 * i], (float)(int)r[2 * i + 1]), xs2);
+      upk(fma2(t, pk(w[2 * i], w[2 * i + 1]), pk(b[2 * i], b[2 * i + 1])), v[2 * i], v[2 * i + 1]);
+    }
     uint32_t o[32];
     if (EPI == kEpiSwigluPairs) {
 #pragma unroll
