@@ -37,7 +37,14 @@ __device__ __forceinline__ uint32_t f2bf(float f) {
   u += 0x7fffu + ((u >> 16) & 1u);
   return u >> 16;
 }
-__device__ __forceinline__ float bf16r(float f) { return __uint_as_float(f2bf(f) << 16); }
+// f rounded to bf16 and widened back, for intermediate roundings: the hardware's round-to-nearest-even conversion,
+// the same value as f2bf for every non-NaN input; a NaN stays a NaN (its bit pattern differs from f2bf's 0x7fc0,
+// so values that are stored go through f2bf / pack_bf2, or pack_out's NaN fallback)
+__device__ __forceinline__ float bf16r(float f) {
+  uint16_t h;
+  asm("cvt.rn.bf16.f32 %0, %1;" : "=h"(h) : "f"(f));
+  return __uint_as_float((uint32_t)h << 16);
+}
 __device__ __forceinline__ uint32_t pack_bf2(float lo, float hi) { return f2bf(lo) | (f2bf(hi) << 16); }
 
 __device__ __forceinline__ float h2f(uint16_t v) {
