@@ -101,7 +101,9 @@ __device__ __forceinline__ void decode_block(uint32_t w0, uint32_t w1, uint32_t 
       const uint32_t h = hmul2(d[b], sc2);  // exact: at most 5 significant bits, inside the f16 range
       const float odd = __half2float(__ushort_as_half((unsigned short)(h & 0xffffu)));   // low nibble
       const float even = __half2float(__ushort_as_half((unsigned short)(h >> 16)));     // high nibble
-      o[4 * wi + b] = cvt_bf16x2(__fmul_rn(even, g), __fmul_rn(odd, g));
+      float e2, o2;  // both products with the global scale in one paired multiply (each lane rounded as FMUL)
+      upk(mul2(pk(even, odd), pk(g, g)), e2, o2);
+      o[4 * wi + b] = cvt_bf16x2(e2, o2);
     }
   }
 }
