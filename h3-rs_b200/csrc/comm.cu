@@ -98,6 +98,7 @@ h3q_status need_nccl(const char* what) {
 }
 
 constexpr int kPushChunks = 4;     // row chunks of the PUSH form: chunk c's copies overlap chunk c+1's GEMM
+constexpr int kMaxPeers = 15;      // copy streams of the PUSH form (one per peer)
 constexpr int64_t kNsplitAlign = 256;  // the GEMM's tile width: every column block but the last is whole tiles
 
 // Columns of rank r: whole 256-column tiles, spread as evenly as the tile count allows.
@@ -146,8 +147,11 @@ struct h3q_comm {
   ncclComm_t nc = nullptr;
   int rank = 0, nranks = 0, device = 0;
   float* flag = nullptr;                // one device float: the barrier's all-reduce operand
-  cudaStream_t copy = nullptr;          // PUSH: the copy-engine stream
-  cudaEvent_t ev[kPushChunks + 2] = {};  // PUSH: chunk done, call start, copies done
+  // PUSH: one copy stream per peer (its copies run on their own copy engine, in parallel with the other peers'),
+  // the chunk-done and call-start events every copy stream waits on, and one copies-done event per copy stream
+  cudaStream_t copy[kMaxPeers] = {};
+  cudaEvent_t ev[kPushChunks + 1] = {};
+  cudaEvent_t done[kMaxPeers] = {};
 };
 
 extern "C" {
@@ -175,8 +179,11 @@ h3q_status h3q_comm_init(int nranks, int rank, const void* id, h3q_comm** comm) 
   cudaError_t e = cudaGetDevice(&c->device);
   if (e == cudaSuccess) e = cudaMalloc(&c->flag, sizeof(float));
   if (e == cudaSuccess) e = cudaMemset(c->flag, 0, sizeof(float));
-  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c->copy, cudaStreamNonBlocking);
-  for (int i = 0; i < kPushChunks + 2 && e == cudaSuccess; ++i)
+  for (int i = 0; i + 1 < nranks && i < kMaxPeers && e == cudaSuccess; ++i) {
+    e = cudaStreamCreateWithFlags(&c->copy[i], cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c->done[i], cudaEventDisableTiming);
+  }
+  for (int i = 0; i < kPushChunks + 1 && e == cudaSuccess; ++i)
     e = cudaEventCreateWithFlags(&c->ev[i], cudaEventDisableTiming);
   h3q_status st = cuda_status(e, what);
   if (st == H3Q_OK) {
@@ -201,7 +208,10 @@ h3q_status h3q_comm_destroy(h3q_comm* c) {
   if (c->nc) st = nccl_status(nccl().comm_destroy(c->nc), "h3q_comm_destroy");
   for (cudaEvent_t& ev : c->ev)
     if (ev) cudaEventDestroy(ev);
-  if (c->copy) cudaStreamDestroy(c->copy);
+  for (int i = 0; i < kMaxPeers; ++i) {
+    if (c->done[i]) cudaEventDestroy(c->done[i]);
+    if (c->copy[i]) cudaStreamDestroy(c->copy[i]);
+  }
   if (c->flag) cudaFree(c->flag);
   cudaSetDevice(prev);
   delete c;
@@ -317,12 +327,14 @@ h3q_status h3q_gemm_s8_nsplit(h3q_comm* c, int mode, const int8_t* a, const floa
     return h3q_comm_barrier(c, stream);
   }
 
-  // PUSH: row chunks of whole 256-row GEMM tiles; the copy stream forwards chunk j while the GEMM computes j+1
+  // PUSH: row chunks of whole 256-row GEMM tiles; while the GEMM computes chunk j+1, the copy streams (one per peer,
+  // so the peers' copies run on separate copy engines at once) forward chunk j
   if (nl > 0) {
+    if (g - 1 > kMaxPeers) return fail(H3Q_ERR_UNSUPPORTED, "%s: the push form serves at most %d peers", what, kMaxPeers);
     const int64_t tile_rows = (m + 255) / 256;
     const int nch = (int)(tile_rows < kPushChunks ? tile_rows : kPushChunks);
     cudaError_t e = cudaEventRecord(c->ev[kPushChunks], st);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(c->copy, c->ev[kPushChunks], 0);
+    for (int d = 1; d < g && e == cudaSuccess; ++d) e = cudaStreamWaitEvent(c->copy[d - 1], c->ev[kPushChunks], 0);
     uint16_t* own = static_cast<uint16_t*>(outs[r]);
     for (int j = 0; j < nch && e == cudaSuccess; ++j) {
       const int64_t r0 = tile_rows * j / nch * 256, r1 = tile_rows * (j + 1) / nch * 256;
@@ -335,16 +347,20 @@ h3q_status h3q_gemm_s8_nsplit(h3q_comm* c, int mode, const int8_t* a, const floa
       void* dst[1] = {own + r0 * n_total};
       e = h3q::launch_gemm_i8_allgather(a + r0 * k, w_local, ga, dst, 1, n_total, lo, st);
       if (e == cudaSuccess) e = cudaEventRecord(c->ev[j], st);
-      if (e == cudaSuccess) e = cudaStreamWaitEvent(c->copy, c->ev[j], 0);
       for (int d = 1; d < g && e == cudaSuccess; ++d) {
         const int p = (r + d) % g;  // peers in a rotating order, so no destination is everyone's first
+        cudaStream_t cs = c->copy[d - 1];
+        e = cudaStreamWaitEvent(cs, c->ev[j], 0);
         uint16_t* dstp = static_cast<uint16_t*>(outs[p]) + r0 * n_total + lo;
-        e = cudaMemcpy2DAsync(dstp, (size_t)n_total * 2, own + r0 * n_total + lo, (size_t)n_total * 2, (size_t)nl * 2,
-                              (size_t)rows, cudaMemcpyDeviceToDevice, c->copy);
+        if (e == cudaSuccess)
+          e = cudaMemcpy2DAsync(dstp, (size_t)n_total * 2, own + r0 * n_total + lo, (size_t)n_total * 2,
+                                (size_t)nl * 2, (size_t)rows, cudaMemcpyDeviceToDevice, cs);
       }
     }
-    if (e == cudaSuccess) e = cudaEventRecord(c->ev[kPushChunks + 1], c->copy);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(st, c->ev[kPushChunks + 1], 0);
+    for (int d = 1; d < g && e == cudaSuccess; ++d) {
+      e = cudaEventRecord(c->done[d - 1], c->copy[d - 1]);
+      if (e == cudaSuccess) e = cudaStreamWaitEvent(st, c->done[d - 1], 0);
+    }
     if (h3q_status s = cuda_status(e, what)) return s;
   }
   return h3q_comm_barrier(c, stream);
