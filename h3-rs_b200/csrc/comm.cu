@@ -120,22 +120,21 @@ int64_t widest_block(int64_t n, int g) {
 }
 
 // out[row, lo_r + c] = blocks[r][row][c] for c < width of rank r: the NCCL form's gathered [g][m][nmax] blocks into
-// the [m, n] output, 16 bytes per thread (every block offset and width is a multiple of 8 columns).
-__global__ void nsplit_relayout_kernel(const uint16_t* __restrict__ blocks, uint16_t* __restrict__ out, int64_t m,
-                                       int64_t n, int64_t nmax, int g) {
+// the [m, n] output.  One (rank, row) per block-iteration, 16 bytes per thread (every block offset and width is a
+// multiple of 8 columns); the rank's column range is worked out once per row, not per element.
+__global__ void __launch_bounds__(256) nsplit_relayout_kernel(const uint16_t* __restrict__ blocks,
+                                                              uint16_t* __restrict__ out, int64_t m, int64_t n,
+                                                              int64_t nmax, int g) {
   const int64_t tiles = (n + kNsplitAlign - 1) / kNsplitAlign;
-  const int64_t vec_per_row = nmax / 8;
-  const int64_t total = (int64_t)g * m * vec_per_row;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t v = i % vec_per_row;
-    const int64_t row = (i / vec_per_row) % m;
-    const int r = (int)(i / (vec_per_row * m));
+  for (int64_t rr = blockIdx.x; rr < (int64_t)g * m; rr += gridDim.x) {
+    const int r = (int)(rr / m);
+    const int64_t row = rr - (int64_t)r * m;
     const int64_t t0 = tiles * r / g, t1 = tiles * (r + 1) / g;
     const int64_t lo = t0 * kNsplitAlign < n ? t0 * kNsplitAlign : n;
     const int64_t hi = t1 * kNsplitAlign < n ? t1 * kNsplitAlign : n;
-    if (8 * v >= hi - lo) continue;
-    const uint4 d = *reinterpret_cast<const uint4*>(blocks + ((int64_t)r * m + row) * nmax + 8 * v);
-    *reinterpret_cast<uint4*>(out + row * n + lo + 8 * v) = d;
+    const uint4* src = reinterpret_cast<const uint4*>(blocks + rr * nmax);
+    uint4* dst = reinterpret_cast<uint4*>(out + row * n + lo);
+    for (int64_t v = threadIdx.x; v < (hi - lo) / 8; v += blockDim.x) dst[v] = __ldg(src + v);
   }
 }
 
@@ -306,9 +305,8 @@ h3q_status h3q_gemm_s8_nsplit(h3q_comm* c, int mode, const int8_t* a, const floa
     }
     if (h3q_status s = nccl_status(nccl().all_gather(send, recv, (size_t)m * nmax * 2, ncclUint8, c->nc, st), what))
       return s;
-    const int64_t total = (int64_t)g * m * (nmax / 8);
-    const int64_t blocks = (total + 255) / 256;
-    nsplit_relayout_kernel<<<(unsigned)(blocks < 8 * 148 ? blocks : 8 * 148), 256, 0, st>>>(
+    const int64_t rows = (int64_t)g * m;
+    nsplit_relayout_kernel<<<(unsigned)(rows < 16 * 148 ? rows : 16 * 148), 256, 0, st>>>(
         recv, static_cast<uint16_t*>(outs[r]), m, n_total, nmax, g);
     return cuda_status(cudaGetLastError(), what);
   }

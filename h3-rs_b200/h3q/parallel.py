@@ -184,12 +184,16 @@ class NSplitLinear:
                the peers' buffers while the next chunk computes;
       "nccl"   local GEMM, ncclAllGather of the column blocks, relayout kernel.
 
-    mode=None picks the form measured fastest on B200 for the four c1 linears (M = 32760, DEFAULT_MODE): "push"
-    (2 GPUs: 4.28 ms against 4.49 fused and 7.61 nccl).
+    mode=None picks the form measured fastest on B200 for the four c1 linears (M = 32760, default_mode): "push" up
+    to 2 ranks (2 GPUs: 4.28 ms against 4.49 fused and 7.61 nccl), "nccl" beyond (8 GPUs: 7.0 ms against 9.8 push
+    and 26.8 fused: with 8 ranks the copy engines forward only ~0.27 TB/s per GPU).
     shard_quant=True quantizes only this rank's row_range of x and all-gathers the int8 codes and row scales
-    (M K + 4 M bytes over NVLink) instead of every rank quantizing all rows (needs M % world == 0)."""
+    (M K + 4 M bytes over NVLink) instead of every rank quantizing all rows (needs M % world == 0).
+    """
 
-    DEFAULT_MODE = "push"
+    @staticmethod
+    def default_mode(world: int) -> str:
+        return "push" if world <= 2 else "nccl"
 
     def __init__(self, w, ws, bias, comm: Comm, mode: str | None = None, rotate: bool = True,
                  shard_quant: bool = False, group=None):
@@ -202,7 +206,7 @@ class NSplitLinear:
         ws = ws.to(torch.float32).reshape(-1)
         self.ws = (ws[self.n0:self.n1] if ws.numel() == self.n and self.n > 1 else ws[:1]).contiguous()
         self.bias = None if bias is None else bias.to(torch.float32)[self.n0:self.n1].contiguous()
-        mode = mode or self.DEFAULT_MODE
+        mode = mode or self.default_mode(self.world)
         if mode not in NSPLIT_MODES:
             raise ValueError(f"NSplitLinear: unknown mode {mode!r}")
         self.mode = mode
