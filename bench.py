@@ -686,6 +686,7 @@ def multi_gpu_extras(dist, dev, reps: int = 3) -> dict:
                  (M = 32760 in total, strong scaling), through h3q_gemm_s8_nsplit: "fused" is one GEMM per rank
                  storing its column block into every rank's output over NVLink, "push" the GEMM in row chunks with
                  the copy engines forwarding each finished chunk, "nccl" a local GEMM + ncclAllGather + relayout,
+                 "peer" the GEMM then a kernel on every SM storing the column block into the peers' outputs,
                  "push_shard_quant" push with each rank quantizing only its row block and all-gathering the codes;
                  exchange_ms = the form's time minus the local work alone (compute_only_ms); each output must
                  equal, bit for bit, the whole linear computed on one GPU (the weak run's output of the same
@@ -727,7 +728,7 @@ def multi_gpu_extras(dist, dev, reps: int = 3) -> dict:
     compute_ms = _max_over_ranks(time_steps(compute_only, reps, dev), dist, dev)
     del lins
     for name, mode, shard in (("fused", "fused", False), ("push", "push", False), ("nccl", "nccl", False),
-                              ("push_shard_quant", "push", True)):
+                              ("peer", "peer", False), ("push_shard_quant", "push", True)):
         lins = [P.NSplitLinear(ly["w"], ly["ws"], ly["b"], comm, mode=mode, shard_quant=shard) for ly in layers]
         outs = [None] * len(lins)
 

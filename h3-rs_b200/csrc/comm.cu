@@ -13,8 +13,10 @@
 //                     copy engines pushing each finished chunk into every peer's buffer (2-D copies over NVLink,
 //                     straight into the final column positions) while the next chunk computes;
 //   H3Q_NSPLIT_NCCL   a local GEMM into a packed block, ncclAllGather of the blocks, and a relayout kernel
-//                     (the library-collective baseline).
-// FUSED and PUSH write into peers' buffers, so a barrier first makes sure every rank has finished with the
+//                     (the library-collective baseline);
+//   H3Q_NSPLIT_PEER   the GEMM into this rank's own buffer, then a kernel on every SM storing the column block
+//                     into every peer's buffer, 16 bytes at a time, destinations rotating.
+// FUSED, PUSH and PEER write into peers' buffers, so a barrier first makes sure every rank has finished with the
 // previous contents of its output (stream-ordered), and a barrier last makes the complete output readable.
 #include <dlfcn.h>
 #include <nccl.h>
@@ -138,6 +140,33 @@ __global__ void __launch_bounds__(256) nsplit_relayout_kernel(const uint16_t* __
   }
 }
 
+// The PEER form's exchange: this rank's column block [lo, lo + width) of rows [0, m) of its own output, read once
+// 16 bytes at a time and stored to the same place in every peer's output (peer memory over NVLink), every SM
+// taking part.  Destinations rotate with the element index, so the seven stores of a thread go to seven different
+// GPUs and the links are loaded evenly.
+constexpr int kMaxPeerDst = 8;
+struct PeerDsts {
+  uint16_t* p[kMaxPeerDst];  // peers' outputs (this rank's own excluded)
+  int n;
+};
+
+__global__ void __launch_bounds__(512) nsplit_peer_store_kernel(const uint16_t* __restrict__ own, PeerDsts dsts,
+                                                                int64_t m, int64_t n, int64_t lo, int64_t width) {
+  const int64_t vpr = width / 8;  // 16-byte vectors per row
+  const int64_t total = m * vpr;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = i / vpr, v = i - row * vpr;
+    const int64_t off = row * n + lo + 8 * v;
+    const uint4 d = __ldg(reinterpret_cast<const uint4*>(own + off));
+    const int first = (int)(i % dsts.n);
+#pragma unroll 1
+    for (int j = 0; j < dsts.n; ++j) {
+      const int t = first + j < dsts.n ? first + j : first + j - dsts.n;
+      *reinterpret_cast<uint4*>(dsts.p[t] + off) = d;
+    }
+  }
+}
+
 size_t align256(size_t v) { return (v + 255) / 256 * 256; }
 
 }  // namespace
@@ -256,8 +285,10 @@ h3q_status h3q_gemm_s8_nsplit(h3q_comm* c, int mode, const int8_t* a, const floa
                               void* stream) {
   const char* what = "h3q_gemm_s8_nsplit";
   if (!c) return fail(H3Q_ERR_ARG, "%s: null communicator", what);
-  if (mode != H3Q_NSPLIT_FUSED && mode != H3Q_NSPLIT_PUSH && mode != H3Q_NSPLIT_NCCL)
+  if (mode != H3Q_NSPLIT_FUSED && mode != H3Q_NSPLIT_PUSH && mode != H3Q_NSPLIT_NCCL && mode != H3Q_NSPLIT_PEER)
     return fail(H3Q_ERR_ARG, "%s: unknown mode %d", what, mode);
+  if (mode == H3Q_NSPLIT_PEER && c->nranks > kMaxPeerDst + 1)
+    return fail(H3Q_ERR_UNSUPPORTED, "%s: the peer form stores to at most %d peers", what, kMaxPeerDst);
   if (m < 0 || n_total < 0 || k < 0) return fail(H3Q_ERR_ARG, "%s: negative shape", what);
   const int g = c->nranks, r = c->rank;
   if (mode == H3Q_NSPLIT_FUSED && g > h3q::kMaxGatherRanks)
@@ -313,6 +344,30 @@ h3q_status h3q_gemm_s8_nsplit(h3q_comm* c, int mode, const int8_t* a, const floa
 
   // FUSED and PUSH: every rank must be done with its output buffer's previous contents before peers write into it
   if (h3q_status s = h3q_comm_barrier(c, stream)) return s;
+  if (mode == H3Q_NSPLIT_PEER) {
+    // the GEMM writes this rank's columns into its own output, then every SM forwards them to the peers
+    if (nl > 0) {
+      ga.M = m;
+      ga.N = nl;
+      ga.xs = xs;
+      ga.out = outs[r];
+      void* dst[1] = {outs[r]};
+      if (h3q_status s = cuda_status(h3q::launch_gemm_i8_allgather(a, w_local, ga, dst, 1, n_total, lo, st), what))
+        return s;
+      PeerDsts pd{};
+      pd.n = 0;
+      for (int d = 1; d < g; ++d) pd.p[pd.n++] = static_cast<uint16_t*>(outs[(r + d) % g]);
+      if (pd.n > 0) {
+        int dev = 0, sms = 148;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        nsplit_peer_store_kernel<<<(unsigned)(4 * sms), 512, 0, st>>>(static_cast<const uint16_t*>(outs[r]), pd, m,
+                                                                      n_total, lo, nl);
+        if (h3q_status s = cuda_status(cudaGetLastError(), what)) return s;
+      }
+    }
+    return h3q_comm_barrier(c, stream);
+  }
   if (mode == H3Q_NSPLIT_FUSED) {
     if (nl > 0) {
       ga.M = m;

@@ -131,8 +131,8 @@ class PeerBuffers:
                 self._own = None
 
 
-NSPLIT_FUSED, NSPLIT_PUSH, NSPLIT_NCCL = 0, 1, 2
-NSPLIT_MODES = {"fused": NSPLIT_FUSED, "push": NSPLIT_PUSH, "nccl": NSPLIT_NCCL}
+NSPLIT_FUSED, NSPLIT_PUSH, NSPLIT_NCCL, NSPLIT_PEER = 0, 1, 2, 3
+NSPLIT_MODES = {"fused": NSPLIT_FUSED, "push": NSPLIT_PUSH, "nccl": NSPLIT_NCCL, "peer": NSPLIT_PEER}
 
 
 class Comm:
@@ -182,7 +182,9 @@ class NSplitLinear:
                NVLink), so the transfer runs inside the GEMM;
       "push"   the GEMM in row chunks into this rank's buffer, the copy engines pushing each finished chunk into
                the peers' buffers while the next chunk computes;
-      "nccl"   local GEMM, ncclAllGather of the column blocks, relayout kernel.
+      "nccl"   local GEMM, ncclAllGather of the column blocks, relayout kernel;
+      "peer"   the GEMM into this rank's buffer, then a kernel on every SM storing the column block into every
+               peer's buffer.
 
     mode=None picks the form measured fastest on B200 for the four c1 linears (M = 32760, default_mode): "push" up
     to 2 ranks (2 GPUs: 4.28 ms against 4.49 fused and 7.61 nccl), "nccl" beyond (8 GPUs: 7.0 ms against 9.8 push

@@ -509,7 +509,8 @@ h3q_status h3q_comm_barrier(h3q_comm* comm, void* stream);
 enum {
   H3Q_NSPLIT_FUSED = 0, /* the GEMM's epilogue stores every output box into every rank's buffer (peer memory) */
   H3Q_NSPLIT_PUSH = 1,  /* GEMM in row chunks into this rank's buffer; copy engines push finished chunks to peers */
-  H3Q_NSPLIT_NCCL = 2   /* local GEMM into a packed block, ncclAllGather, relayout kernel into the output */
+  H3Q_NSPLIT_NCCL = 2,  /* local GEMM into a packed block, ncclAllGather, relayout kernel into the output */
+  H3Q_NSPLIT_PEER = 3   /* GEMM into this rank's buffer, then every SM stores the column block into every peer's */
 };
 
 /* Output columns [lo, hi) of rank `rank` in the N split of n columns: whole 256-column GEMM tiles, spread as evenly
@@ -521,7 +522,7 @@ size_t h3q_gemm_s8_nsplit_workspace_size(int64_t m, int64_t n_total, int nranks,
  * activations a [m, k] with row scales xs [m] (the same on every rank), this rank's weight rows w_local
  * [n_local, k] for its columns h3q_nsplit_range(n_total, nranks, rank) (scales ws_local per row when
  * ws_numel == n_local > 1, bias_local [n_local] or NULL).  Every rank receives the whole output [m, n_total] in
- * outs[rank].  FUSED and PUSH write into peers' buffers: outs[d] is rank d's output mapped into this process
+ * outs[rank].  FUSED, PUSH and PEER write into peers' buffers: outs[d] is rank d's output mapped into this process
  * (h3q_peer_buffer_open); NCCL reads only outs[rank].  Barriers inside the call order the peers' writes after every
  * rank's earlier use of its output and make the output complete when the call's work on the stream is done.
  * Collective: every rank calls it with the same mode and shape.  n_total % 8 == 0, k % 16 == 0. */

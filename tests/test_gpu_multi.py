@@ -1,7 +1,7 @@
 """Multi-GPU parity of h3q.parallel (one NCCL rank per GPU in child processes, 2 to 8 GPUs; skipped with fewer than
-two): the N-split linear through the C ABI (h3q_gemm_s8_nsplit) in its three forms (fused: every rank's column
+two): the N-split linear through the C ABI (h3q_gemm_s8_nsplit) in its four forms (fused: every rank's column
 block stored into every rank's output by the GEMM; push: row chunks forwarded by the copy engines; nccl:
-ncclAllGather + relayout), with the activations quantized whole or per row block and all-gathered, the library's
+ncclAllGather + relayout; peer: a kernel on every SM storing the block into the peers), with the activations quantized whole or per row block and all-gathered, the library's
 byte all-gather, and query-sharded attention, each bit-identical to the single-GPU result."""
 import datetime
 import os
@@ -50,7 +50,7 @@ def _worker(rank: int, world: int, port: int, errors):
         for M in (1000, 1003):
             x = torch.randn((M, K), generator=g, device=dev).to(torch.bfloat16)
             want = h3q.gemm_s8(x, w, ws, b, swiglu=False, rotate=True)
-            for mode in ("fused", "push", "nccl"):
+            for mode in ("fused", "push", "nccl", "peer"):
                 for shard in (False, True):
                     lin = P.NSplitLinear(w, ws, b, comm, mode=mode, shard_quant=shard)
                     for _ in range(2):  # twice: the output buffers are reused
