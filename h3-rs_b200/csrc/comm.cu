@@ -1,5 +1,5 @@
 // comm.cu -- the multi-GPU data plane of the C ABI (one process per GPU): NCCL communicators, a byte all-gather, a
-// cross-rank barrier, and the N-split linear step with its all-gather of output columns in three forms.
+// cross-rank barrier, and the N-split linear step with its all-gather of output columns in four forms.
 //
 // NCCL is resolved at run time (dlopen of libnccl.so.2, preferring a copy the process has already loaded, such as
 // the one a framework brought in), so the library neither links nor pins an NCCL build; a process without NCCL
@@ -15,7 +15,7 @@
 //   H3Q_NSPLIT_NCCL   a local GEMM into a packed block, ncclAllGather of the blocks, and a relayout kernel
 //                     (the library-collective baseline);
 //   H3Q_NSPLIT_PEER   the GEMM into this rank's own buffer, then a kernel on every SM storing the column block
-//                     into every peer's buffer, 16 bytes at a time, destinations rotating.
+//                     into every peer's buffer, a warp per row, whole 512-byte stores to one peer at a time.
 // FUSED, PUSH and PEER write into peers' buffers, so a barrier first makes sure every rank has finished with the
 // previous contents of its output (stream-ordered), and a barrier last makes the complete output readable.
 #include <dlfcn.h>
@@ -142,8 +142,10 @@ __global__ void __launch_bounds__(256) nsplit_relayout_kernel(const uint16_t* __
 
 // The PEER form's exchange: this rank's column block [lo, lo + width) of rows [0, m) of its own output, read once
 // 16 bytes at a time and stored to the same place in every peer's output (peer memory over NVLink), every SM
-// taking part.  Destinations rotate with the element index, so the seven stores of a thread go to seven different
-// GPUs and the links are loaded evenly.
+// taking part.  One warp per row: each store instruction writes 512 contiguous bytes of the row to ONE peer, so
+// NVLink carries whole lines (a destination that changed from lane to lane split every warp store into 16-byte
+// pieces bound for seven GPUs and ran 2.6x slower at 8 ranks).  The order of the destinations rotates with the
+// row, so the warps in flight load the links evenly.
 constexpr int kMaxPeerDst = 8;
 struct PeerDsts {
   uint16_t* p[kMaxPeerDst];  // peers' outputs (this rank's own excluded)
@@ -152,17 +154,20 @@ struct PeerDsts {
 
 __global__ void __launch_bounds__(512) nsplit_peer_store_kernel(const uint16_t* __restrict__ own, PeerDsts dsts,
                                                                 int64_t m, int64_t n, int64_t lo, int64_t width) {
-  const int64_t vpr = width / 8;  // 16-byte vectors per row
-  const int64_t total = m * vpr;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t row = i / vpr, v = i - row * vpr;
-    const int64_t off = row * n + lo + 8 * v;
-    const uint4 d = __ldg(reinterpret_cast<const uint4*>(own + off));
-    const int first = (int)(i % dsts.n);
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int vpr = (int)(width / 8);  // 16-byte vectors per row
+  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < m; row += warps) {
+    const int64_t base = row * n + lo;
+    const uint4* src = reinterpret_cast<const uint4*>(own + base);
+    const int first = (int)(row % dsts.n);
+    for (int v = lane; v < vpr; v += 32) {
+      const uint4 d = __ldg(src + v);
 #pragma unroll 1
-    for (int j = 0; j < dsts.n; ++j) {
-      const int t = first + j < dsts.n ? first + j : first + j - dsts.n;
-      *reinterpret_cast<uint4*>(dsts.p[t] + off) = d;
+      for (int j = 0; j < dsts.n; ++j) {
+        const int t = first + j < dsts.n ? first + j : first + j - dsts.n;
+        reinterpret_cast<uint4*>(dsts.p[t] + base)[v] = d;
+      }
     }
   }
 }
