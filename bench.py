@@ -690,7 +690,8 @@ def multi_gpu_extras(dist, dev, reps: int = 3) -> dict:
                  "push_shard_quant" push with each rank quantizing only its row block and all-gathering the codes;
                  exchange_ms = the form's time minus the local work alone (compute_only_ms); each output must
                  equal, bit for bit, the whole linear computed on one GPU (the weak run's output of the same
-                 activations);
+                 activations); allgather_alone times the all-gather of the nccl form's column blocks by itself,
+                 the link's ceiling for the exchange;
       attention: query-sharded c4 attention (S = 32760, H = 40 in total): K/V rows all-gathered, each rank attends
                  its 32760 / N queries (h3q_attention_rows); its rows must equal those of the whole-sequence
                  attention computed on one GPU."""
@@ -751,6 +752,22 @@ def multi_gpu_extras(dist, dev, reps: int = 3) -> dict:
         dist.barrier()
     res["compute_only_ms"] = round(compute_ms, 3)
     res["output_bytes_received_per_rank"] = int(sum(M * ly["n"] * 2 for ly in layers) * (world - 1) / world)
+    # the exchange alone: the library's all-gather (NCCL) of each layer's [M, n_max] column blocks, the bytes the
+    # nccl form moves, with no GEMM and no relayout -- what the link delivers to the N split
+    widths = [max(hi - lo for lo, hi in (P.nsplit_range(ly["n"], world, r) for r in range(world))) for ly in layers]
+    send = torch.zeros(M * max(widths), dtype=torch.bfloat16, device=dev)
+    recv = torch.empty(world * M * max(widths), dtype=torch.bfloat16, device=dev)
+
+    def gather_only():
+        for wd in widths:
+            comm.allgather(send[:M * wd], recv[:world * M * wd])
+    gather_only()
+    dist.barrier()
+    ms = _max_over_ranks(time_steps(gather_only, reps, dev), dist, dev)
+    moved = sum((world - 1) * M * wd * 2 for wd in widths)
+    res["allgather_alone"] = {"ms": round(ms, 3), "bytes_received_per_rank": moved,
+                              "gbs_received_per_rank": round(moved / (ms * 1e-3) / 1e9, 1)}
+    del send, recv
     del layers
     S, H = 32760, 40
     lo, hi = P.row_range(S, world, rank)

@@ -15,7 +15,7 @@
 //   H3Q_NSPLIT_NCCL   a local GEMM into a packed block, ncclAllGather of the blocks, and a relayout kernel
 //                     (the library-collective baseline);
 //   H3Q_NSPLIT_PEER   the GEMM into this rank's own buffer, then a kernel on every SM storing the column block
-//                     into every peer's buffer, a warp per row, whole 512-byte stores to one peer at a time.
+//                     into every peer's buffer, a warp per row, whole 512-byte stores, one peer per phase.
 // FUSED, PUSH and PEER write into peers' buffers, so a barrier first makes sure every rank has finished with the
 // previous contents of its output (stream-ordered), and a barrier last makes the complete output readable.
 #include <dlfcn.h>
@@ -140,15 +140,16 @@ __global__ void __launch_bounds__(256) nsplit_relayout_kernel(const uint16_t* __
   }
 }
 
-// The PEER form's exchange: this rank's column block [lo, lo + width) of rows [0, m) of its own output, read once
-// 16 bytes at a time and stored to the same place in every peer's output (peer memory over NVLink), every SM
-// taking part.  One warp per row: each store instruction writes 512 contiguous bytes of the row to ONE peer, so
-// NVLink carries whole lines (a destination that changed from lane to lane split every warp store into 16-byte
-// pieces bound for seven GPUs and ran 2.6x slower at 8 ranks).  The order of the destinations rotates with the
-// row, so the warps in flight load the links evenly.
+// The PEER form's exchange: this rank's column block [lo, lo + width) of rows [0, m) of its own output, read 16
+// bytes at a time and stored to the same place in every peer's output (peer memory over NVLink), every SM taking
+// part.  One warp per row: each store instruction writes 512 contiguous bytes of the row to ONE peer, so NVLink
+// carries whole lines (a destination that changed from lane to lane split every warp store into 16-byte pieces
+// bound for seven GPUs and ran 2.6x slower at 8 ranks).  The peers are served in phases: in phase d every warp
+// stores to p[d] only, rank (r + 1 + d) mod g, so while the ranks run the same phase every GPU sends to one GPU
+// and receives from one.  The block is re-read once per phase, mostly from L2.
 constexpr int kMaxPeerDst = 8;
 struct PeerDsts {
-  uint16_t* p[kMaxPeerDst];  // peers' outputs (this rank's own excluded)
+  uint16_t* p[kMaxPeerDst];  // peers' outputs in phase order (this rank's own excluded)
   int n;
 };
 
@@ -156,18 +157,16 @@ __global__ void __launch_bounds__(512) nsplit_peer_store_kernel(const uint16_t* 
                                                                 int64_t m, int64_t n, int64_t lo, int64_t width) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  const int64_t w0 = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int vpr = (int)(width / 8);  // 16-byte vectors per row
-  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); row < m; row += warps) {
-    const int64_t base = row * n + lo;
-    const uint4* src = reinterpret_cast<const uint4*>(own + base);
-    const int first = (int)(row % dsts.n);
-    for (int v = lane; v < vpr; v += 32) {
-      const uint4 d = __ldg(src + v);
 #pragma unroll 1
-      for (int j = 0; j < dsts.n; ++j) {
-        const int t = first + j < dsts.n ? first + j : first + j - dsts.n;
-        reinterpret_cast<uint4*>(dsts.p[t] + base)[v] = d;
-      }
+  for (int d = 0; d < dsts.n; ++d) {  // phase d: every warp stores to peer p[d] only
+    uint16_t* out = dsts.p[d];
+    for (int64_t row = w0; row < m; row += warps) {
+      const int64_t base = row * n + lo;
+      const uint4* src = reinterpret_cast<const uint4*>(own + base);
+      uint4* dst = reinterpret_cast<uint4*>(out + base);
+      for (int v = lane; v < vpr; v += 32) dst[v] = __ldg(src + v);
     }
   }
 }
@@ -366,7 +365,7 @@ h3q_status h3q_gemm_s8_nsplit(h3q_comm* c, int mode, const int8_t* a, const floa
         int dev = 0, sms = 148;
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        nsplit_peer_store_kernel<<<(unsigned)(4 * sms), 512, 0, st>>>(static_cast<const uint16_t*>(outs[r]), pd, m,
+        nsplit_peer_store_kernel<<<(unsigned)(2 * sms), 512, 0, st>>>(static_cast<const uint16_t*>(outs[r]), pd, m,
                                                                       n_total, lo, nl);
         if (h3q_status s = cuda_status(cudaGetLastError(), what)) return s;
       }

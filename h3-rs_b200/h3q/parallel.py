@@ -187,15 +187,17 @@ class NSplitLinear:
                peer's buffer.
 
     mode=None picks the form measured fastest on B200 for the four c1 linears (M = 32760, default_mode): "push" up
-    to 2 ranks (2 GPUs: 4.28 ms against 4.49 fused and 7.61 nccl), "nccl" beyond (8 GPUs: 7.0 ms against 9.8 push
-    and 26.8 fused: with 8 ranks the copy engines forward only ~0.27 TB/s per GPU).
+    to 2 ranks (2 GPUs: 4.13 ms against 4.47 fused and 7.02 nccl), "peer" up to 4 (4 GPUs: 4.97 ms against 5.98
+    fused, 6.52 nccl and 6.62 push; the SM stores deliver ~0.7 TB/s per GPU there), "nccl" beyond (8 GPUs: 7.17 ms
+    against 7.53 peer and 9.82 push: with every GPU sending to seven, stores and copies deliver ~0.4 TB/s per GPU
+    and NCCL's all-gather ~0.6).
     shard_quant=True quantizes only this rank's row_range of x and all-gathers the int8 codes and row scales
     (M K + 4 M bytes over NVLink) instead of every rank quantizing all rows (needs M % world == 0).
     """
 
     @staticmethod
     def default_mode(world: int) -> str:
-        return "push" if world <= 2 else "nccl"
+        return "push" if world <= 2 else "peer" if world <= 4 else "nccl"
 
     def __init__(self, w, ws, bias, comm: Comm, mode: str | None = None, rotate: bool = True,
                  shard_quant: bool = False, group=None):
