@@ -100,3 +100,10 @@ def test_ranges_cover_and_align():
         ranges = [P.row_range(m, g, r) for r in range(g)]
         assert ranges[0][0] == 0 and ranges[-1][1] == m
         assert max(hi - lo for lo, hi in ranges) - min(hi - lo for lo, hi in ranges) <= 1
+
+
+def test_nsplit_default_form_by_world_size():
+    """NSplitLinear's default form is the one measured fastest on B200 for the four c1 linears: the copy-engine
+    push up to 2 ranks, the SM peer stores up to 4, NCCL's all-gather beyond; every default is a known form."""
+    assert [P.NSplitLinear.default_mode(g) for g in (2, 3, 4, 5, 8)] == ["push", "peer", "peer", "nccl", "nccl"]
+    assert all(P.NSplitLinear.default_mode(g) in P.NSPLIT_MODES for g in range(2, 17))
